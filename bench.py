@@ -1,0 +1,342 @@
+"""Benchmark of the B200 video self-attention block (LTX-2.3, as served by plugyawn/opengenie).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+
+One step = one forward of the video self-attention block (AdaZero -> FP8 QKV ->
+Q/K RMSNorm + RoPE -> attention -> FP8 out-projection + gated residual) over the
+configuration's synthetic inputs (seeded, random-init weights; see
+opengenie_b200/synthetic.py).  The metric is the block's attention throughput,
+TFLOP/s = 4*L^2*128*32 / t_block, as BASELINE.json defines it; µs per block is
+`ms_per_step`.  N > 1 runs one process per GPU (torchrun) with Ulysses head
+sharding; `value` is then the whole job's throughput on one block (strong scaling).
+
+Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "video self-attn block µs & TFLOP/s (% BF16 peak) at L=9216, 1/2/4/8 B200"
+UNIT = "TFLOP/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def attn_flops(L: int, heads: int = 32, d: int = 128) -> float:
+    return 4.0 * L * L * d * heads
+
+
+def measured_peaks() -> tuple[dict, str]:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.05):
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: report no clocks
+            self._nvml = None
+        self.period = period_s
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM))
+                mask = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for name, bit in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+def dist_setup(n_gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist.group.WORLD
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local, pg
+
+
+def barrier(pg):
+    if pg is not None:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, pg) -> float:
+    if pg is None:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- CPU reference arm
+def cpu_reference(cfg_name: str, steps: int, warmup: int, budget_s: float = 25.0) -> dict:
+    """The reference's algorithm for the block on the host cores (the oracle port), bounded sample."""
+    from oracle import ltx_block_oracle as O
+    from opengenie_b200 import synthetic
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    cfg = synthetic.CONFIGS[cfg_name]
+    inp = synthetic.make_inputs(cfg, seed=1)
+    w = synthetic.make_weights(seed=0)
+    ts_view = inp.timestep.reshape(1, cfg.tokens, 6, 4096)
+    # static input scales as the GPU arm calibrates them (amax / 448)
+    for lin in (w.to_q, w.to_k, w.to_v):
+        lin.input_scale = torch.tensor(0.02, dtype=torch.float32)
+    w.to_out.input_scale = torch.tensor(0.002, dtype=torch.float32)
+    times = []
+    t_start = time.perf_counter()
+    with torch.no_grad():
+        for i in range(max(1, steps)):
+            t0 = time.perf_counter()
+            O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s:
+                break
+    per_block = min(times)
+    return {
+        "value": attn_flops(cfg.tokens) / per_block / 1e12,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{len(times)} full {cfg_name} block(s) (L={cfg.tokens}) in torch fp32 on the host, best of "
+                  f"{len(times)}; {per_block * 1e3:.0f} ms/block",
+        "ms_per_block": per_block * 1e3,
+    }
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cb = cpu_reference(args.config, args.steps, args.warmup)
+    line = {
+        "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_block"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16/e4m3 (fp32 on CPU)", "data": "synthetic",
+        "config": config_dict(args.config, args.gpus),
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(name: str, n: int) -> dict:
+    from opengenie_b200 import synthetic
+
+    cfg = synthetic.CONFIGS[name]
+    return {
+        "workload": f"LTX-2.3 video self-attention block, {name}",
+        "tokens": cfg.tokens, "latent_grid": [cfg.frames, cfg.grid_h, cfg.grid_w], "hidden": 4096, "heads": 32,
+        "head_dim": 128, "batch": 1, "qkv_out_proj": "e4m3 per-tensor scales, fp32 accumulate",
+        "attention": "bf16, fp32 softmax/accumulate", "per_token_timestep": cfg.per_token_timestep,
+        "parallelism": "single GPU" if n == 1 else f"ulysses heads {32 // n}/GPU",
+        "l2": "inputs larger than L2 (x 75 MB + weights 67 MB + cos/sin 75 MB read per block)",
+    }
+
+
+# --------------------------------------------------------------------------- GPU arm
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c1_l9216")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    from opengenie_b200 import _lib, synthetic
+    from opengenie_b200.video_block import VideoSelfAttentionBlock
+
+    rank, world, local, pg = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    cfg = synthetic.CONFIGS[args.config]
+    L = cfg.tokens
+    inp_cpu = synthetic.make_inputs(cfg, seed=1)
+    w = synthetic.make_weights(seed=0)
+    inp = inp_cpu.to(dev)
+
+    if world == 1:
+        blk = VideoSelfAttentionBlock(w, dev)
+        blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
+        launches_per_step = 5
+
+        def step(x):
+            return blk(x, inp.timestep, (inp.cos, inp.sin))
+    else:
+        from opengenie_b200.ulysses import UlyssesVideoSelfAttention
+
+        blk = UlyssesVideoSelfAttention(w, dev, pg)
+        blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
+        launches_per_step = blk.kernel_launches_per_step
+
+        def step(x):
+            return blk(x, inp.timestep, (inp.cos, inp.sin))
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step(inp.x)
+    torch.cuda.synchronize(dev)
+    if _lib.device_status(clear=True):
+        raise SystemExit("device status reported a timed-out wait during warm-up")
+
+    # ---- device-timed region: K block forwards, inputs resident in HBM
+    barrier(pg)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step(inp.x)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(pg)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, pg)
+    value = attn_flops(L) / (ms * 1e-3) / 1e12
+
+    # ---- e2e: host x (pinned) -> device, block, device -> host output, every step
+    x_host = inp_cpu.x.pin_memory() if world == 1 else blk.local_slice(inp_cpu.x).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x_host, device=dev)
+    barrier(pg)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        y = step(x_dev) if world == 1 else blk.forward_local(x_dev, inp.timestep, (inp.cos, inp.sin))
+        out_host.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, pg)
+    h2d = x_host.numel() * x_host.element_size()
+    d2h = out_host.numel() * out_host.element_size()
+
+    # ---- dominant kernel (attention) timed alone on the launching stream
+    attn_ms = blk.time_attention(args.steps, args.warmup) if hasattr(blk, "time_attention") else None
+    attn_ms = max_over_ranks(attn_ms, pg) if attn_ms is not None else None
+    status = _lib.device_status(clear=True)
+
+    if rank == 0:
+        peaks, peak_kind = measured_peaks()
+        heads_local = 32 // world
+        attn_unit_flops = attn_flops(L, heads=heads_local)
+        achieved = attn_unit_flops / (attn_ms * 1e-3) / 1e12 if attn_ms else None
+        traffic = None
+        tpath = os.path.join(REPO, "profiles", "fmha_traffic.json")
+        if os.path.exists(tpath):
+            with open(tpath) as f:
+                t = json.load(f)
+            # bytes per (head, 256-query block) CTA scale with L: K/V re-reads per query block
+            traffic = t.get("bytes_per_launch", {}).get(f"{args.config}_h{heads_local}")
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "us_per_block": ms * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16 attention / e4m3 projections",
+            "data": "synthetic (seeded inputs, random-init weights)", "config": config_dict(args.config, world),
+            "roofline": {
+                "bound": "tensor", "kernel": "fmha_fwd_kernel (attention, dominant)",
+                "achieved": achieved, "peak": peaks.get("bf16_tflops"), "unit": "TFLOP/s",
+                "frac": (achieved / peaks["bf16_tflops"]) if achieved else None,
+                "peak_kind": f"{peak_kind} bf16 dense (burst)",
+                "algorithmic_flops_per_launch": attn_unit_flops, "kernel_ms": attn_ms, "traffic": traffic,
+                "block_frac_of_bf16_peak": value / peaks["bf16_tflops"],
+            },
+            "e2e": {"value": attn_flops(L) / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+            "device_status": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            cb = cpu_reference(args.config, 2, 0, budget_s=20.0)
+            line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,165 @@
+/*
+ * opengenie-b200 C ABI: the hot path of LTX-2.3's video self-attention block
+ * on NVIDIA B200 (sm_100a).
+ *
+ * Every entry point:
+ *   - takes device pointers the caller allocated (the library never allocates,
+ *     frees or keeps tensor memory), plain sizes and element strides, and a
+ *     cudaStream_t passed as `void*` (null = legacy default stream);
+ *   - is stream-ordered and asynchronous: it enqueues kernels and returns;
+ *   - returns OGX_OK (0) or a negative OGX_E* code; ogx_last_error() then
+ *     names the failed guard with the reference's reason string (e.g.
+ *     "qk_shape", "rope_shape") or the CUDA error.  There is no CPU fallback.
+ * Device-side waits are bounded; a wait that gives up sets a status bit that
+ * ogx_device_status() reads.
+ *
+ * Reference interfaces (plugyawn/opengenie) each entry point replaces are
+ * cited as file:line.
+ */
+#ifndef OGX_H_
+#define OGX_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OGX_OK 0
+#define OGX_EINVAL (-1)   /* a guard rejected the arguments */
+#define OGX_ECUDA (-2)    /* a CUDA runtime/driver call failed */
+
+/* dtype codes */
+#define OGX_DTYPE_BF16 0
+#define OGX_DTYPE_F32 1
+#define OGX_DTYPE_F16 2
+
+/* E4M3 quantiser semantics */
+#define OGX_QUANT_TORCH 0  /* ltx_serve/triton_ltx_ops.py:146-148 (bit-exact target) */
+#define OGX_QUANT_SINGLE 1 /* ltx_serve/triton_ltx_ops.py:3429-3444 (one rounding)  */
+
+int ogx_version(void);
+const char* ogx_last_error(void);
+
+/* Reads (and with clear != 0 resets) the device status word of the current
+ * device: bit 1 = a bounded device-side wait gave up.  Synchronous. */
+int ogx_device_status(unsigned int* status, int clear);
+
+/* AdaZero with Ada values read from scale_shift_table + timestep:
+ *   y = rmsnorm(x, eps) * (1 + scale) + shift, fp32 math, one bf16 rounding,
+ *   shift/scale = bf16?(bf16?(table[idx]) + ts[b, t, idx, :]).
+ * x: bf16 [batch, tokens, cols] contiguous, cols in {2048, 4096};
+ * table: [P, cols] (bf16/f32), row stride table_stride_row, unit column stride;
+ * timestep viewed [batch, tokens, P, cols] with strides (ts_stride_b,
+ * ts_stride_t, ts_stride_p, 1) elements (ts_stride_t may be 0).
+ * Replaces fused_adazero_from_ada, ltx_serve/triton_ltx_ops.py:40-91. */
+int ogx_adazero_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                         int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                         int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
+                         int scale_index, float eps, void* y, void* stream);
+
+/* Same, fused with the per-tensor E4M3 activation quantiser: q = quant(y)
+ * (y itself is written only when y != NULL).  The codes equal
+ * ogx_fp8_quantize_e4m3 applied to the bf16 y.
+ * Replaces fused_adazero_from_ada (:40-91) followed by
+ * fused_fp8_quantize_e4m3 (:144-161) inside FP8Linear.forward (:1676-1716). */
+int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                              int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                              int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
+                              int scale_index, float eps, const float* input_scale, int quant_mode, void* y,
+                              void* q, void* stream);
+
+/* Per-tensor E4M3 quantiser: q = e4m3(clamp(x * (1/s), -448, 448)).
+ * x: bf16 or f16, n elements contiguous; input_scale: device f32 scalar.
+ * Replaces fused_fp8_quantize_e4m3, ltx_serve/triton_ltx_ops.py:144-161. */
+int ogx_fp8_quantize_e4m3(const void* x, int x_dtype, int64_t n, const float* input_scale, int quant_mode, void* q,
+                          void* stream);
+
+/* out = bf16(x + bf16(bias)); x bf16 [rows, cols] contiguous, bias [cols].
+ * Replaces fused_bias_add_bf16, ltx_serve/triton_ltx_ops.py:185-201. */
+int ogx_bias_add_bf16(const void* x, int64_t rows, int64_t cols, const void* bias, int bias_dtype, void* out,
+                      void* stream);
+
+/* out = bf16(x + bf16(bf16(y + bf16(bias)) * gate)), gate from table/timestep
+ * slot gate_index (same conventions as ogx_adazero_from_ada).
+ * Replaces fused_residual_gate_bias_from_ada, ltx_serve/triton_ltx_ops.py:204-262. */
+int ogx_residual_gate_bias_from_ada(const void* x, const void* y, int64_t batch, int64_t tokens, int64_t cols,
+                                    const void* bias, int bias_dtype, const void* table, int table_dtype,
+                                    int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                                    int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int gate_index,
+                                    void* out, void* stream);
+
+/* Q/K RMSNorm over 4096 columns (with weight) + split RoPE per head (32 heads
+ * x 128), fp32 math, one bf16 rounding.  q/k: bf16 rows of 4096 with token
+ * stride in_stride_t; cos/sin: [32, tokens, 64] with strides (cs_stride_h,
+ * cs_stride_t, 1) (bf16 or f32); outputs bf16 with token stride out_stride_t
+ * (may alias the inputs).
+ * Replaces fused_video_qk_rmsnorm_rope, ltx_serve/triton_ltx_ops.py:320-378. */
+int ogx_video_qk_rmsnorm_rope(const void* q, const void* k, int64_t tokens, int64_t in_stride_t,
+                              const void* q_weight, const void* k_weight, int weight_dtype, float eps,
+                              const void* cos, const void* sin, int cs_dtype, int64_t cs_stride_h,
+                              int64_t cs_stride_t, void* q_out, void* k_out, int64_t out_stride_t, void* stream);
+
+/* The same normalisation + RoPE, writing Q/K and copying V into the
+ * head-grouped send layout of the sequence-to-head exchange: head h of token t
+ * goes to out + t*out_stride_t + (h / heads_per_group)*out_stride_g +
+ * (h % heads_per_group)*128.  No reference counterpart for the layout (the
+ * reference is single-GPU); the arithmetic is that of
+ * fused_video_qk_rmsnorm_rope (:320-378). */
+int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void* v, int64_t tokens,
+                                       int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                       int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
+                                       int64_t cs_stride_h, int64_t cs_stride_t, void* q_out, void* k_out,
+                                       void* v_out, int64_t out_stride_t, int64_t out_stride_g,
+                                       int heads_per_group, void* stream);
+
+/* FP8 scaled matmul with bias epilogue (tcgen05, e4m3 x e4m3 -> f32 -> bf16):
+ *   out[m, n] = bf16(bf16(acc * scale_a * scale_b[n / n_per_scale]) + bf16(bias[n]))
+ * a: e4m3 [M, K] (row stride lda), w: e4m3 [N, K] (row stride ldw), both
+ * K-major; scales are device f32 (scale_b has N / n_per_scale entries); bias
+ * may be NULL; out bf16 [M, N] with row stride ldo.  K % 16 == 0, N % 32 == 0.
+ * Replaces torch._scaled_mm(a, w.t(), scale_a, scale_b, out_dtype=bf16,
+ * use_fast_accum=True) + bias add in FP8Linear.forward,
+ * ltx_serve/triton_ltx_ops.py:1695-1707 and :742-759. */
+int ogx_fp8_scaled_mm(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                      const float* scale_a, const float* scale_b, int64_t n_per_scale, const void* bias,
+                      int bias_dtype, void* out, int64_t ldo, void* stream);
+
+/* FP8 scaled matmul fused with the block's output epilogue:
+ *   y = bf16(bf16(acc * scale_a * scale_b) + bf16(bias)),
+ *   out = bf16(x + bf16(y * gate)), gate from table/timestep slot gate_index
+ * (rows are tokens of batch 1).
+ * Replaces fp8_linear_without_bias (ltx_serve/triton_ltx_ops.py:762-781)
+ * followed by fused_residual_gate_bias_from_ada (:204-262). */
+int ogx_fp8_scaled_mm_residual_gate(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
+                                    int64_t ldw, const float* scale_a, const float* scale_b, int64_t n_per_scale,
+                                    const void* bias, int bias_dtype, const void* x, int64_t ldx,
+                                    const void* table, int table_dtype, int64_t table_stride_row,
+                                    const void* timestep, int timestep_dtype, int64_t ts_stride_t,
+                                    int64_t ts_stride_p, int gate_index, void* out, int64_t ldo, void* stream);
+
+/* Dense bidirectional attention (tcgen05 + TMEM, online softmax), head_dim 128:
+ *   out[b, t, h, :] = softmax(q[b,t,h,:] . k[b,:,h,:]^T * softmax_scale) v[b,:,h,:]
+ * q/k/v: bf16, element (b, t, h, d) at ptr + b*stride_b + t*stride_t + h*128 + d
+ * (all three share the strides; stride_t % 8 == 0); out bf16 with its own
+ * strides.  Replaces the attention backend call attn.attention_function(q, k,
+ * v, heads) (ltx_serve/triton_ltx_ops.py:2636; backend contract
+ * benchmarks/official_ltx23_benchmark.py:3289-3373). */
+int ogx_attention_fwd(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens, int64_t heads,
+                      int64_t head_dim, int64_t stride_b, int64_t stride_t, float softmax_scale, void* out,
+                      int64_t out_stride_b, int64_t out_stride_t, void* stream);
+
+/* Same attention, with the output quantised to e4m3 for the output projection
+ * (bf16 rounding of O first, then the torch-path quantiser with *out_scale),
+ * i.e. fused_fp8_quantize_e4m3(attention(q, k, v), to_out.input_scale) as in
+ * fp8_linear_without_bias (ltx_serve/triton_ltx_ops.py:770-771). */
+int ogx_attention_fwd_e4m3(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens,
+                           int64_t heads, int64_t head_dim, int64_t stride_b, int64_t stride_t, float softmax_scale,
+                           const float* out_scale, void* out_q, int64_t out_stride_b, int64_t out_stride_t,
+                           void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OGX_H_ */

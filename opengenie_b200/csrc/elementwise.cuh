@@ -1,0 +1,428 @@
+// HBM-bound stages of the video self-attention block: AdaZero-from-table
+// (optionally fused with the E4M3 activation quantiser), the standalone E4M3
+// quantiser, the bf16 bias add, the bias + Ada-gated residual, and the fused
+// Q/K RMSNorm + split RoPE (which also scatters Q/K/V into a head-grouped
+// layout for the sequence-to-head exchange).
+//
+// All of them move 16-byte vectors (8 x bf16) per lane so every warp access is
+// a fully used 512-byte span, keep fp32 arithmetic and round to bf16 exactly
+// where the reference rounds.
+#pragma once
+
+#include "ogx_sm100.cuh"
+
+namespace ogx {
+
+// ----------------------------------------------------------------- dtype helpers
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 p = __bfloat1622float2(h[i]);
+    f[2 * i] = p.x;
+    f[2 * i + 1] = p.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 v;
+  v.x = pack_bf16x2(f[0], f[1]);
+  v.y = pack_bf16x2(f[2], f[3]);
+  v.z = pack_bf16x2(f[4], f[5]);
+  v.w = pack_bf16x2(f[6], f[7]);
+  return v;
+}
+
+// Loads 8 consecutive values of type T (bf16 or fp32) as fp32.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&f)[8]);
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&f)[8]) {
+  unpack8(*reinterpret_cast<const uint4*>(p), f);
+}
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&f)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Ada value for one slot: table row (rounded to bf16 when the table's dtype
+// differs from the timestep's) plus the timestep slot, rounded to bf16 when
+// the timestep is bf16.  Mirrors `_torch_ada_values_from_table`
+// (ltx_serve/triton_ltx_ops.py:983-998): `table.to(ts.dtype)[idx] + ts[..., idx, :]`.
+template <typename TableT, typename TsT>
+__device__ __forceinline__ void ada_values8(const TableT* table_row, const TsT* ts_row, float (&out)[8]) {
+  constexpr bool round_table = !std::is_same<TableT, TsT>::value;
+  constexpr bool round_ada = std::is_same<TsT, __nv_bfloat16>::value;
+  float t[8], s[8];
+  load8<TableT>(table_row, t);
+  load8<TsT>(ts_row, s);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float a = round_table ? bf16_round(t[i]) : t[i];
+    float v = a + s[i];
+    out[i] = round_ada ? bf16_round(v) : v;
+  }
+}
+
+// ----------------------------------------------------------------- E4M3
+// Round-to-nearest-even fp32 -> e4m3fn with saturation to +-448; NaN -> 0x7F
+// (the code torch produces for any NaN input).
+__device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
+  if (v != v) return 0x7F;
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+// Quantiser semantics.
+//  kQuantTorch : the reference's torch path, triton_ltx_ops.py:146-148:
+//                t = round_to_input_dtype(float(x) * (1/s)); clamp(t, +-448); e4m3 RNE.
+//                (x * s.reciprocal() on a bf16/fp16 tensor and an fp32 0-dim
+//                tensor keeps the fp32 reciprocal and rounds the product once
+//                to the input dtype; clamp is exact; the cast is RNE.)
+//  kQuantSingle: the reference's Triton kernel, triton_ltx_ops.py:3429-3444:
+//                e4m3(clamp(float(x) / s, +-448)), one rounding.
+enum QuantMode : int { kQuantTorch = 0, kQuantSingle = 1 };
+
+template <typename InT>
+__device__ __forceinline__ float round_to(float v);
+template <>
+__device__ __forceinline__ float round_to<__nv_bfloat16>(float v) {
+  return bf16_round(v);
+}
+template <>
+__device__ __forceinline__ float round_to<__half>(float v) {
+  return __half2float(__float2half_rn(v));
+}
+
+template <typename InT, int MODE>
+__device__ __forceinline__ uint8_t quant_one(float x, float s, float r) {
+  float t;
+  if (MODE == kQuantTorch) {
+    t = round_to<InT>(__fmul_rn(x, r));
+  } else {
+    t = __fdiv_rn(x, s);
+  }
+  // clamp with NaN passing through (torch.clamp propagates NaN)
+  t = (t < -448.0f) ? -448.0f : ((t > 448.0f) ? 448.0f : t);
+  return f32_to_e4m3(t);
+}
+
+template <typename InT, int MODE>
+__device__ __forceinline__ uint2 quant8(const float (&f)[8], float s, float r) {
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) lo |= static_cast<uint32_t>(quant_one<InT, MODE>(f[i], s, r)) << (8 * i);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hi |= static_cast<uint32_t>(quant_one<InT, MODE>(f[4 + i], s, r)) << (8 * i);
+  return make_uint2(lo, hi);
+}
+
+// ----------------------------------------------------------------- AdaZero
+// y = rmsnorm(x) * (1 + scale) + shift in fp32 with one bf16 rounding
+// (the reference's GPU kernel, triton_ltx_ops.py:3359-3427), with
+// shift/scale read from scale_shift_table + timestep.  One 128-thread CTA per
+// row (COLS / 1024 16-byte vectors per thread, the row stays in registers
+// between the reduction and the normalisation).  With QUANT the bf16 result
+// is also (or only) quantised to e4m3, so the codes are bit-equal to
+// quantising the bf16 output separately.
+struct AdaArgs {
+  const __nv_bfloat16* x;
+  const void* table;
+  const void* ts;
+  int64_t ts_stride_b, ts_stride_t, ts_stride_p;  // elements; innermost stride is 1
+  int64_t table_stride_row;                       // elements; innermost stride is 1
+  int64_t rows, tokens;
+  int shift_index, scale_index;
+  float eps;
+  const float* input_scale;  // device scalar (QUANT only)
+  __nv_bfloat16* y;          // may be null when only q is wanted
+  uint8_t* q;                // e4m3 output (QUANT only)
+};
+
+constexpr int kRowThreads = 128;
+
+// Sum over the 128 threads of a row CTA.
+__device__ __forceinline__ float row_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  return red[0] + red[1] + red[2] + red[3];
+}
+
+template <int COLS, typename TableT, typename TsT, bool QUANT, int QMODE>
+__global__ void __launch_bounds__(kRowThreads) adazero_from_ada_kernel(AdaArgs a) {
+  constexpr int VPT = COLS / 8 / kRowThreads;  // 16-byte vectors per thread
+  __shared__ float red[4];
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int64_t b = row / a.tokens;
+  const int64_t t = row - b * a.tokens;
+
+  const uint4* xr = reinterpret_cast<const uint4*>(a.x + row * COLS);
+  uint4 xv[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    xv[j] = __ldg(xr + j * kRowThreads + tid);
+    float f[8];
+    unpack8(xv[j], f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+  }
+  ss = row_sum(ss, red);
+  const float inv_rms = rsqrtf(ss / static_cast<float>(COLS) + a.eps);
+
+  const TableT* table = static_cast<const TableT*>(a.table);
+  const TsT* ts = static_cast<const TsT*>(a.ts) + b * a.ts_stride_b + t * a.ts_stride_t;
+  const TableT* tshift = table + a.shift_index * a.table_stride_row;
+  const TableT* tscale = table + a.scale_index * a.table_stride_row;
+  const TsT* sshift = ts + a.shift_index * a.ts_stride_p;
+  const TsT* sscale = ts + a.scale_index * a.ts_stride_p;
+
+  float s = 0.f, r = 0.f;
+  if (QUANT) {
+    s = __ldg(a.input_scale);
+    r = __frcp_rn(s);
+  }
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int vec = j * kRowThreads + tid;
+    const int col = vec * 8;
+    float f[8], shift[8], scale[8], y[8];
+    unpack8(xv[j], f);
+    ada_values8<TableT, TsT>(tshift + col, sshift + col, shift);
+    ada_values8<TableT, TsT>(tscale + col, sscale + col, scale);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = fmaf(f[i] * inv_rms, 1.0f + scale[i], shift[i]);
+    const uint4 yv = pack8(y);
+    if (a.y != nullptr) reinterpret_cast<uint4*>(a.y + row * COLS)[vec] = yv;
+    if (QUANT) {
+      float yb[8];
+      unpack8(yv, yb);
+      reinterpret_cast<uint2*>(a.q + row * COLS)[vec] = quant8<__nv_bfloat16, QMODE>(yb, s, r);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- quantiser
+template <typename InT, int MODE>
+__global__ void __launch_bounds__(256) fp8_quantize_kernel(const InT* __restrict__ x, int64_t n,
+                                                           const float* __restrict__ input_scale,
+                                                           uint8_t* __restrict__ q) {
+  const float s = __ldg(input_scale);
+  const float r = __frcp_rn(s);
+  const int64_t nvec = n >> 3;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x) + v);
+    float f[8];
+    if (std::is_same<InT, __nv_bfloat16>::value) {
+      unpack8(raw, f);
+    } else {
+      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 p = __half22float2(h[i]);
+        f[2 * i] = p.x;
+        f[2 * i + 1] = p.y;
+      }
+    }
+    reinterpret_cast<uint2*>(q)[v] = quant8<InT, MODE>(f, s, r);
+  }
+  // ragged tail (n % 8), handled by the first threads of block 0
+  if (blockIdx.x == 0) {
+    const int64_t tail0 = nvec << 3;
+    for (int64_t i = tail0 + threadIdx.x; i < n; i += blockDim.x) {
+      float f;
+      if (std::is_same<InT, __nv_bfloat16>::value)
+        f = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
+      else
+        f = __half2float(reinterpret_cast<const __half*>(x)[i]);
+      q[i] = quant_one<InT, MODE>(f, s, r);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- bias add
+// out = bf16(x + bf16(bias)) (triton_ltx_ops.py:3446-3464; the bias is rounded
+// to bf16 first when it is fp32, like `bias.to(x.dtype)`).
+template <typename BiasT>
+__global__ void __launch_bounds__(256) bias_add_kernel(const __nv_bfloat16* __restrict__ x,
+                                                       const BiasT* __restrict__ bias, int64_t rows, int64_t cols,
+                                                       __nv_bfloat16* __restrict__ out) {
+  const int64_t cvec = cols >> 3;
+  const int64_t nvec = rows * cvec;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    const int64_t c = (v % cvec) << 3;
+    float f[8], bb[8], o[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(x) + v), f);
+    load8<BiasT>(bias + c, bb);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = f[i] + bf16_round(bb[i]);
+    reinterpret_cast<uint4*>(out)[v] = pack8(o);
+  }
+}
+
+// ----------------------------------------------------------------- bias + gate + residual
+// out = bf16(x + bf16(bf16(y + bf16(bias)) * gate)), gate from the table and
+// timestep slot `gate_index` (triton_ltx_ops.py:3663-3721).
+struct ResidualArgs {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* y;
+  const void* bias;
+  const void* table;
+  const void* ts;
+  int64_t ts_stride_b, ts_stride_t, ts_stride_p;
+  int64_t table_stride_row;
+  int64_t rows, tokens, cols;
+  int gate_index;
+  __nv_bfloat16* out;
+};
+
+template <typename BiasT, typename TableT, typename TsT>
+__global__ void __launch_bounds__(256) residual_gate_bias_kernel(ResidualArgs a) {
+  const int64_t cvec = a.cols >> 3;
+  const int64_t nvec = a.rows * cvec;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const BiasT* bias = static_cast<const BiasT*>(a.bias);
+  const TableT* tgate = static_cast<const TableT*>(a.table) + a.gate_index * a.table_stride_row;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    const int64_t row = v / cvec;
+    const int64_t c = (v - row * cvec) << 3;
+    const int64_t b = row / a.tokens;
+    const int64_t t = row - b * a.tokens;
+    const TsT* sgate = static_cast<const TsT*>(a.ts) + b * a.ts_stride_b + t * a.ts_stride_t +
+                       a.gate_index * a.ts_stride_p;
+    float xf[8], yf[8], bf[8], g[8], o[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(a.x) + v), xf);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(a.y) + v), yf);
+    load8<BiasT>(bias + c, bf);
+    ada_values8<TableT, TsT>(tgate + c, sgate + c, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float yb = bf16_round(yf[i] + bf16_round(bf[i]));
+      const float prod = bf16_round(yb * g[i]);
+      o[i] = xf[i] + prod;
+    }
+    reinterpret_cast<uint4*>(a.out)[v] = pack8(o);
+  }
+}
+
+// ----------------------------------------------------------------- Q/K RMSNorm + split RoPE
+// Per token: q_hat = q * rsqrt(mean(q^2) + eps) * w_q over all 4096 columns,
+// then per head h and half index j < 64:
+//   o[j]    = q_hat[j] * cos[h,t,j] - q_hat[j+64] * sin[h,t,j]
+//   o[j+64] = q_hat[j+64] * cos[h,t,j] + q_hat[j] * sin[h,t,j]
+// in fp32 with one bf16 rounding (triton_ltx_ops.py:3901-3978).  Same for k.
+// One warp per token.  Lane l holds vectors v = 32*j + l (8 columns each); the
+// partner half of the same head sits in lane l ^ 8, reached with a shuffle.
+//
+// Outputs are addressed per (token, head): out + t*out_stride_t +
+// (h / heads_per_group)*out_stride_g + (h % heads_per_group)*128 + d, which
+// is the plain [L, 4096] layout for heads_per_group = 32 and the per-rank
+// send layout of the sequence-to-head exchange otherwise.  V (optional) is
+// copied through the same addressing.
+struct RopeArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;  // optional
+  int64_t in_stride_t;      // elements between tokens of q/k/v
+  const void* q_weight;
+  const void* k_weight;
+  const void* cos;
+  const void* sin;
+  int64_t cs_stride_h, cs_stride_t;  // elements; innermost stride 1
+  int64_t tokens;
+  float eps;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_out;
+  __nv_bfloat16* v_out;  // optional
+  int64_t out_stride_t, out_stride_g;
+  int heads_per_group;
+};
+
+template <typename WT, typename CsT>
+__device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* in, const WT* w, const CsT* cosb,
+                                                 const CsT* sinb, const RopeArgs& a, int64_t t, float* red,
+                                                 __nv_bfloat16* outb) {
+  constexpr int VPT = 4096 / 8 / kRowThreads;  // 4
+  const int tid = threadIdx.x;
+  uint4 xv[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    xv[j] = __ldg(reinterpret_cast<const uint4*>(in) + j * kRowThreads + tid);
+    float f[8];
+    unpack8(xv[j], f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+  }
+  ss = row_sum(ss, red);
+  const float inv_rms = rsqrtf(ss / 4096.f + a.eps);
+  // vector v holds columns [8v, 8v+8): head v/16, its partner half is v ^ 8,
+  // which lives in lane (tid ^ 8) of the same warp.
+  const bool second = (tid & 8) != 0;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int vec = j * kRowThreads + tid;
+    const int col = vec * 8;
+    const int head = col >> 7;
+    const int half_off = col & 63;  // index into the 64 cos/sin values
+    float f[8], wv[8], n[8], other[8], c[8], s[8], o[8];
+    unpack8(xv[j], f);
+    load8<WT>(w + col, wv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[i] = f[i] * inv_rms * wv[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) other[i] = __shfl_xor_sync(0xffffffffu, n[i], 8);
+    load8<CsT>(cosb + head * a.cs_stride_h + t * a.cs_stride_t + half_off, c);
+    load8<CsT>(sinb + head * a.cs_stride_h + t * a.cs_stride_t + half_off, s);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      o[i] = second ? fmaf(n[i], c[i], other[i] * s[i]) : fmaf(n[i], c[i], -(other[i] * s[i]));
+    const int g = head / a.heads_per_group;
+    const int hl = head - g * a.heads_per_group;
+    __nv_bfloat16* dst = outb + t * a.out_stride_t + g * a.out_stride_g + hl * 128 + (col & 127);
+    *reinterpret_cast<uint4*>(dst) = pack8(o);
+  }
+}
+
+// One 128-thread CTA per token.
+template <typename WT, typename CsT>
+__global__ void __launch_bounds__(kRowThreads) qk_rmsnorm_rope_kernel(RopeArgs a) {
+  __shared__ float red[2][4];
+  const int64_t t = blockIdx.x;
+  const CsT* cosb = static_cast<const CsT*>(a.cos);
+  const CsT* sinb = static_cast<const CsT*>(a.sin);
+  rmsnorm_rope_row<WT, CsT>(a.q + t * a.in_stride_t, static_cast<const WT*>(a.q_weight), cosb, sinb, a, t, red[0],
+                            a.q_out);
+  rmsnorm_rope_row<WT, CsT>(a.k + t * a.in_stride_t, static_cast<const WT*>(a.k_weight), cosb, sinb, a, t, red[1],
+                            a.k_out);
+  if (a.v != nullptr && a.v_out != nullptr) {
+    const __nv_bfloat16* vin = a.v + t * a.in_stride_t;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int vec = j * kRowThreads + threadIdx.x;
+      const int col = vec * 8;
+      const int head = col >> 7;
+      const int g = head / a.heads_per_group;
+      const int hl = head - g * a.heads_per_group;
+      const uint4 val = __ldg(reinterpret_cast<const uint4*>(vin) + vec);
+      *reinterpret_cast<uint4*>(a.v_out + t * a.out_stride_t + g * a.out_stride_g + hl * 128 + (col & 127)) = val;
+    }
+  }
+}
+
+}  // namespace ogx

@@ -1,0 +1,277 @@
+// FP8 (e4m3 x e4m3 -> fp32) GEMM on the 5th-generation tensor cores:
+//   out[m, n] = epilogue( scale_a * scale_b[n / n_per_scale] * sum_k A[m, k] * W[n, k] )
+// A is the quantised activation [M, K] and W the quantised weight [N, K]
+// (nn.Linear layout), both K-major, which is exactly torch._scaled_mm(A, W.t()).
+//
+// Persistent kernel, one CTA per SM, 128x256 output tiles:
+//   warp 0      TMA producer: A/W tiles (128-byte swizzle) into a 4-stage ring
+//   warp 1      MMA issuer:   tcgen05.mma kind::f8f6f4, M=128 N=256 K=32,
+//                             fp32 accumulators in TMEM (2 x 256 columns, so
+//                             the epilogue of one tile overlaps the next tile)
+//   warps 2..5  epilogue:     tcgen05.ld -> scale -> bf16 -> bias (-> gate +
+//                             residual) -> global
+// Epilogues reproduce the reference's rounding sequence:
+//   EPI_BIAS:     bf16(bf16(acc*s) + bf16(bias))            (scaled_mm, then
+//                 fused_bias_add_bf16, triton_ltx_ops.py:1695-1707)
+//   EPI_RESIDUAL: bf16(x + bf16(bf16(bf16(acc*s) + bf16(bias)) * gate))
+//                 (fp8_linear_without_bias :762-781 then
+//                 fused_residual_gate_bias_from_ada :204-262)
+#pragma once
+
+#include "ogx_sm100.cuh"
+#include "elementwise.cuh"
+
+namespace ogx {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // fp8 elements = bytes per row of a stage
+constexpr int STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK;
+constexpr int B_STAGE_BYTES = BN * BK;
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = 512;
+constexpr int kThreads = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+
+enum Epilogue : int { EPI_BIAS = 0, EPI_RESIDUAL = 1 };
+
+struct Params {
+  int M, N, K;
+  const float* scale_a;  // device scalar
+  const float* scale_b;  // device array, one entry per n_per_scale columns
+  int n_per_scale;
+  const void* bias;  // [N] or null
+  int bias_fp32;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  // EPI_RESIDUAL only
+  const __nv_bfloat16* resid_x;
+  int64_t ldx;
+  const void* table;
+  int table_fp32;
+  int64_t table_stride_row;
+  const void* ts;
+  int ts_fp32;
+  int64_t ts_stride_t, ts_stride_p;
+  int gate_index;
+};
+
+struct SharedState {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[NUM_ACC];
+  uint64_t tmem_empty[NUM_ACC];
+  uint64_t drained;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ float load_scalar(const void* p, int is_fp32, int64_t i) {
+  return is_fp32 ? __ldg(static_cast<const float*>(p) + i)
+                 : __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ SharedState st;
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* smem_aligned = smem_raw + (smem_base - smem_u32(smem_raw));
+
+  const uint32_t warp = warp_idx();
+  const uint32_t lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&st.full[s], 1);
+      mbar_init(&st.empty[s], 1);
+    }
+    for (int a = 0; a < NUM_ACC; ++a) {
+      mbar_init(&st.tmem_full[a], 1);
+      mbar_init(&st.tmem_empty[a], 128);
+    }
+    mbar_init(&st.drained, 1);
+    st.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&st.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = st.tmem_base;
+  volatile int* abort = &st.abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % num_m) * BM;
+        const int n0 = (tile / num_m) * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&st.empty[stage], phase ^ 1u, abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem_aligned + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_STAGE_BYTES;
+          mbar_arrive_expect_tx(&st.full[stage], STAGE_BYTES);
+          tma_load_2d(sa, &tmap_a, &st.full[stage], kb * BK, m0);
+          tma_load_2d(sb, &tmap_b, &st.full[stage], kb * BK, n0);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already in flight land before the CTA exits.
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          int s = stage - 1 - i;
+          uint32_t ph = phase;
+          if (s < 0) {
+            s += STAGES;
+            ph ^= 1u;
+          }
+          mbar_wait(&st.full[s], ph, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&st.tmem_empty[acc], acc_phase ^ 1u, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&st.full[stage], phase, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * STAGE_BYTES;
+          const uint32_t sb = sa + A_STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint64_t adesc = make_sdesc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bdesc = make_sdesc_sw128(sb + kk * 32, 16, 1024);
+            mma_f8_ss(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&st.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(&st.tmem_full[acc]);
+      }
+      // every MMA issued above has completed once `drained` fires
+      mma_commit(&st.drained);
+      mbar_wait(&st.drained, 0, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const uint32_t quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    const float sa = __ldg(p.scale_a);
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&st.tmem_full[acc], acc_phase, abort)) break;
+      tc_fence_after();
+      const int m0 = (tile % num_m) * BM;
+      const int n0 = (tile / num_m) * BN;
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+      const uint32_t taddr_row = tmem_base + ((quarter * 32u) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr_row + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        const float scale = sa * __ldg(p.scale_b + col0 / p.n_per_scale);
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = bf16_round(__uint_as_float(r[i]) * scale);
+          if (p.bias != nullptr) v = bf16_round(v + bf16_round(load_scalar(p.bias, p.bias_fp32, col0 + i)));
+          o[i] = v;
+        }
+        if (EPI == EPI_RESIDUAL) {
+          const __nv_bfloat16* xr = p.resid_x + static_cast<int64_t>(row) * p.ldx + col0;
+          const int64_t tso = static_cast<int64_t>(row) * p.ts_stride_t + p.gate_index * p.ts_stride_p + col0;
+          const int64_t tbo = p.gate_index * p.table_stride_row + col0;
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            float xf[8];
+            unpack8(__ldg(reinterpret_cast<const uint4*>(xr) + v8), xf);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int cc = v8 * 8 + i;
+              float tg = load_scalar(p.table, p.table_fp32, tbo + cc);
+              const float sg = load_scalar(p.ts, p.ts_fp32, tso + cc);
+              if (p.table_fp32 != p.ts_fp32) tg = bf16_round(tg);
+              float g = tg + sg;
+              if (!p.ts_fp32) g = bf16_round(g);
+              o[cc] = xf[i] + bf16_round(o[cc] * g);
+            }
+          }
+        }
+        uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(row) * p.ldo + col0);
+#pragma unroll
+        for (int v8 = 0; v8 < 4; ++v8) {
+          float f[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = o[v8 * 8 + i];
+          dst[v8] = pack8(f);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&st.tmem_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm
+}  // namespace ogx

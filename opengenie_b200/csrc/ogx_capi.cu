@@ -1,0 +1,556 @@
+// C ABI of the B200 video self-attention block (declarations and reference
+// citations in include/ogx.h).  Host-side guards mirror the reference's
+// `_can_use_*` / `*_guard_reason` checks; a failed guard is an error (no
+// fallback).  Tensor maps for TMA are built per call on the host with the
+// driver's cuTensorMapEncodeTiled, fetched through the runtime so the library
+// does not link libcuda directly.
+
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/ogx.h"
+#include "elementwise.cuh"
+#include "fmha.cuh"
+#include "fp8_gemm.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(OGX_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return OGX_OK;
+}
+
+int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// ------------------------------------------------------------- tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int make_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+             const uint64_t* strides_bytes, const uint32_t* box) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(OGX_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  uint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, dt, rank, const_cast<void*>(base), dims, strides_bytes, box, elem_strides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(OGX_EINVAL, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return OGX_OK;
+}
+
+// Raise the dynamic shared-memory limit of a kernel once per device.
+template <typename K>
+int ensure_smem(K kernel, int bytes) {
+  static std::mutex mu;
+  static uint64_t done_mask = 0;  // one bit per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(OGX_ECUDA, "cudaGetDevice failed");
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && (done_mask >> dev) & 1u) return OGX_OK;
+  int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                      "cudaFuncSetAttribute");
+  if (rc == OGX_OK && dev < 64) done_mask |= (uint64_t{1} << dev);
+  return rc;
+}
+
+bool dtype_ok(int dt) { return dt == OGX_DTYPE_BF16 || dt == OGX_DTYPE_F32; }
+
+// ------------------------------------------------------------- AdaZero
+template <int COLS, typename TableT, typename TsT>
+void launch_ada_cols(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(a.rows));
+  const int threads = ogx::kRowThreads;
+  if (!quant)
+    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, false, 0><<<grid, threads, 0, s>>>(a);
+  else if (qmode == OGX_QUANT_TORCH)
+    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantTorch><<<grid, threads, 0, s>>>(a);
+  else
+    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantSingle><<<grid, threads, 0, s>>>(a);
+}
+
+template <typename TableT, typename TsT>
+void launch_ada_t(const ogx::AdaArgs& a, int64_t cols, bool quant, int qmode, cudaStream_t s) {
+  if (cols == 4096)
+    launch_ada_cols<4096, TableT, TsT>(a, quant, qmode, s);
+  else
+    launch_ada_cols<2048, TableT, TsT>(a, quant, qmode, s);
+}
+
+int ada_guard(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table, int table_dtype,
+              const void* ts, int ts_dtype, int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p,
+              int idx0, int idx1) {
+  if (x == nullptr || table == nullptr || ts == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (batch < 1 || tokens < 0) return fail(OGX_EINVAL, "x_shape");
+  if (cols != 2048 && cols != 4096) return fail(OGX_EINVAL, "cols");
+  if (!dtype_ok(table_dtype)) return fail(OGX_EINVAL, "table_dtype");
+  if (!dtype_ok(ts_dtype)) return fail(OGX_EINVAL, "timestep_dtype");
+  if (idx0 < 0 || idx1 < 0) return fail(OGX_EINVAL, "ada_index");
+  const int esz = ts_dtype == OGX_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(x) || !aligned16(table) || !aligned16(ts)) return fail(OGX_EINVAL, "alignment");
+  if ((ts_stride_b * esz) % 16 || (ts_stride_t * esz) % 16 || (ts_stride_p * esz) % 16)
+    return fail(OGX_EINVAL, "timestep_stride");
+  return OGX_OK;
+}
+
+int ada_dispatch(const ogx::AdaArgs& a, int64_t cols, int table_dtype, int ts_dtype, bool quant, int qmode,
+                 cudaStream_t s) {
+  if (a.rows == 0) return OGX_OK;
+  if (table_dtype == OGX_DTYPE_F32 && ts_dtype == OGX_DTYPE_BF16)
+    launch_ada_t<float, __nv_bfloat16>(a, cols, quant, qmode, s);
+  else if (table_dtype == OGX_DTYPE_BF16 && ts_dtype == OGX_DTYPE_BF16)
+    launch_ada_t<__nv_bfloat16, __nv_bfloat16>(a, cols, quant, qmode, s);
+  else if (table_dtype == OGX_DTYPE_F32 && ts_dtype == OGX_DTYPE_F32)
+    launch_ada_t<float, float>(a, cols, quant, qmode, s);
+  else
+    launch_ada_t<__nv_bfloat16, float>(a, cols, quant, qmode, s);
+  return check_launch("adazero_from_ada_kernel");
+}
+
+int grid_for(int64_t nvec) {
+  const int64_t want = (nvec + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+}  // namespace
+
+extern "C" {
+
+int ogx_version(void) { return 1; }
+
+const char* ogx_last_error(void) { return g_last_error.c_str(); }
+
+int ogx_device_status(unsigned int* status, int clear) {
+  unsigned int v = 0;
+  int rc = check_cuda(cudaMemcpyFromSymbol(&v, g_ogx_status, sizeof(v)), "read status");
+  if (rc != OGX_OK) return rc;
+  if (status) *status = v;
+  if (clear) {
+    const unsigned int z = 0;
+    rc = check_cuda(cudaMemcpyToSymbol(g_ogx_status, &z, sizeof(z)), "clear status");
+  }
+  return rc;
+}
+
+int ogx_adazero_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                         int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                         int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
+                         int scale_index, float eps, void* y, void* stream) {
+  int rc = ada_guard(x, batch, tokens, cols, table, table_dtype, timestep, timestep_dtype, ts_stride_b, ts_stride_t,
+                     ts_stride_p, shift_index, scale_index);
+  if (rc) return rc;
+  if (y == nullptr || !aligned16(y)) return fail(OGX_EINVAL, "output");
+  ogx::AdaArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.table = table;
+  a.ts = timestep;
+  a.ts_stride_b = ts_stride_b;
+  a.ts_stride_t = ts_stride_t;
+  a.ts_stride_p = ts_stride_p;
+  a.table_stride_row = table_stride_row;
+  a.rows = batch * tokens;
+  a.tokens = tokens > 0 ? tokens : 1;
+  a.shift_index = shift_index;
+  a.scale_index = scale_index;
+  a.eps = eps;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  return ada_dispatch(a, cols, table_dtype, timestep_dtype, false, 0, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                              int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                              int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
+                              int scale_index, float eps, const float* input_scale, int quant_mode, void* y,
+                              void* q, void* stream) {
+  int rc = ada_guard(x, batch, tokens, cols, table, table_dtype, timestep, timestep_dtype, ts_stride_b, ts_stride_t,
+                     ts_stride_p, shift_index, scale_index);
+  if (rc) return rc;
+  if (q == nullptr || (y != nullptr && !aligned16(y)) || (reinterpret_cast<uintptr_t>(q) & 7u))
+    return fail(OGX_EINVAL, "output");
+  if (input_scale == nullptr) return fail(OGX_EINVAL, "input_scale");
+  if (quant_mode != OGX_QUANT_TORCH && quant_mode != OGX_QUANT_SINGLE) return fail(OGX_EINVAL, "quant_mode");
+  ogx::AdaArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.table = table;
+  a.ts = timestep;
+  a.ts_stride_b = ts_stride_b;
+  a.ts_stride_t = ts_stride_t;
+  a.ts_stride_p = ts_stride_p;
+  a.table_stride_row = table_stride_row;
+  a.rows = batch * tokens;
+  a.tokens = tokens > 0 ? tokens : 1;
+  a.shift_index = shift_index;
+  a.scale_index = scale_index;
+  a.eps = eps;
+  a.input_scale = input_scale;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.q = static_cast<uint8_t*>(q);
+  return ada_dispatch(a, cols, table_dtype, timestep_dtype, true, quant_mode, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_fp8_quantize_e4m3(const void* x, int x_dtype, int64_t n, const float* input_scale, int quant_mode, void* q,
+                          void* stream) {
+  if (x == nullptr || q == nullptr || input_scale == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (x_dtype != OGX_DTYPE_BF16 && x_dtype != OGX_DTYPE_F16) return fail(OGX_EINVAL, "x_dtype");
+  if (quant_mode != OGX_QUANT_TORCH && quant_mode != OGX_QUANT_SINGLE) return fail(OGX_EINVAL, "quant_mode");
+  if (n < 0) return fail(OGX_EINVAL, "numel");
+  if (n == 0) return OGX_OK;
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail(OGX_EINVAL, "alignment");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for((n >> 3) > 0 ? (n >> 3) : 1);
+  if (x_dtype == OGX_DTYPE_BF16) {
+    if (quant_mode == OGX_QUANT_TORCH)
+      ogx::fp8_quantize_kernel<__nv_bfloat16, ogx::kQuantTorch><<<grid, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), n, input_scale, static_cast<uint8_t*>(q));
+    else
+      ogx::fp8_quantize_kernel<__nv_bfloat16, ogx::kQuantSingle><<<grid, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), n, input_scale, static_cast<uint8_t*>(q));
+  } else {
+    if (quant_mode == OGX_QUANT_TORCH)
+      ogx::fp8_quantize_kernel<__half, ogx::kQuantTorch><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), n,
+                                                                              input_scale, static_cast<uint8_t*>(q));
+    else
+      ogx::fp8_quantize_kernel<__half, ogx::kQuantSingle><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), n,
+                                                                               input_scale, static_cast<uint8_t*>(q));
+  }
+  return check_launch("fp8_quantize_kernel");
+}
+
+int ogx_bias_add_bf16(const void* x, int64_t rows, int64_t cols, const void* bias, int bias_dtype, void* out,
+                      void* stream) {
+  if (x == nullptr || bias == nullptr || out == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (!dtype_ok(bias_dtype)) return fail(OGX_EINVAL, "bias_dtype");
+  if (rows < 0 || cols <= 0 || cols % 8) return fail(OGX_EINVAL, "shape");
+  if (!aligned16(x) || !aligned16(out) || !aligned16(bias)) return fail(OGX_EINVAL, "alignment");
+  if (rows == 0) return OGX_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(rows * cols / 8);
+  if (bias_dtype == OGX_DTYPE_F32)
+    ogx::bias_add_kernel<float><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                     static_cast<const float*>(bias), rows, cols,
+                                                     static_cast<__nv_bfloat16*>(out));
+  else
+    ogx::bias_add_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                             static_cast<const __nv_bfloat16*>(bias), rows, cols,
+                                                             static_cast<__nv_bfloat16*>(out));
+  return check_launch("bias_add_kernel");
+}
+
+int ogx_residual_gate_bias_from_ada(const void* x, const void* y, int64_t batch, int64_t tokens, int64_t cols,
+                                    const void* bias, int bias_dtype, const void* table, int table_dtype,
+                                    int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                                    int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int gate_index,
+                                    void* out, void* stream) {
+  int rc = ada_guard(x, batch, tokens, cols, table, table_dtype, timestep, timestep_dtype, ts_stride_b, ts_stride_t,
+                     ts_stride_p, gate_index, gate_index);
+  if (rc) return rc;
+  if (y == nullptr || bias == nullptr || out == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (!dtype_ok(bias_dtype)) return fail(OGX_EINVAL, "bias_dtype");
+  if (!aligned16(y) || !aligned16(out) || !aligned16(bias)) return fail(OGX_EINVAL, "alignment");
+  const int64_t rows = batch * tokens;
+  if (rows == 0) return OGX_OK;
+  ogx::ResidualArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.y = static_cast<const __nv_bfloat16*>(y);
+  a.bias = bias;
+  a.table = table;
+  a.ts = timestep;
+  a.ts_stride_b = ts_stride_b;
+  a.ts_stride_t = ts_stride_t;
+  a.ts_stride_p = ts_stride_p;
+  a.table_stride_row = table_stride_row;
+  a.rows = rows;
+  a.tokens = tokens;
+  a.cols = cols;
+  a.gate_index = gate_index;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(rows * cols / 8);
+  const bool bf = bias_dtype == OGX_DTYPE_F32;
+  const bool tf = table_dtype == OGX_DTYPE_F32;
+  const bool sf = timestep_dtype == OGX_DTYPE_F32;
+#define OGX_RES(B, T, S) ogx::residual_gate_bias_kernel<B, T, S><<<grid, 256, 0, s>>>(a)
+  if (bf) {
+    if (tf) { if (sf) OGX_RES(float, float, float); else OGX_RES(float, float, __nv_bfloat16); }
+    else { if (sf) OGX_RES(float, __nv_bfloat16, float); else OGX_RES(float, __nv_bfloat16, __nv_bfloat16); }
+  } else {
+    if (tf) { if (sf) OGX_RES(__nv_bfloat16, float, float); else OGX_RES(__nv_bfloat16, float, __nv_bfloat16); }
+    else {
+      if (sf) OGX_RES(__nv_bfloat16, __nv_bfloat16, float);
+      else OGX_RES(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
+    }
+  }
+#undef OGX_RES
+  return check_launch("residual_gate_bias_kernel");
+}
+
+int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void* v, int64_t tokens,
+                                       int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                       int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
+                                       int64_t cs_stride_h, int64_t cs_stride_t, void* q_out, void* k_out,
+                                       void* v_out, int64_t out_stride_t, int64_t out_stride_g,
+                                       int heads_per_group, void* stream) {
+  if (q == nullptr || k == nullptr || q_out == nullptr || k_out == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (q_weight == nullptr || k_weight == nullptr) return fail(OGX_EINVAL, "qk_weight_shape");
+  if (cos == nullptr || sin == nullptr) return fail(OGX_EINVAL, "rope_shape");
+  if (tokens < 1) return fail(OGX_EINVAL, "empty_tokens");
+  if (!dtype_ok(weight_dtype) || !dtype_ok(cs_dtype)) return fail(OGX_EINVAL, "qk_device_or_dtype");
+  if (heads_per_group < 1 || 32 % heads_per_group) return fail(OGX_EINVAL, "heads_per_group");
+  if (in_stride_t % 8 || out_stride_t % 8 || out_stride_g % 8) return fail(OGX_EINVAL, "qk_noncontiguous");
+  const int cesz = cs_dtype == OGX_DTYPE_F32 ? 4 : 2;
+  if ((cs_stride_h * cesz) % 16 || (cs_stride_t * cesz) % 16) return fail(OGX_EINVAL, "rope_shape");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(cos) ||
+      !aligned16(sin) || !aligned16(q_weight) || !aligned16(k_weight) || (v && !aligned16(v)) ||
+      (v_out && !aligned16(v_out)))
+    return fail(OGX_EINVAL, "alignment");
+  ogx::RopeArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.in_stride_t = in_stride_t;
+  a.q_weight = q_weight;
+  a.k_weight = k_weight;
+  a.cos = cos;
+  a.sin = sin;
+  a.cs_stride_h = cs_stride_h;
+  a.cs_stride_t = cs_stride_t;
+  a.tokens = tokens;
+  a.eps = eps;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_out = static_cast<__nv_bfloat16*>(k_out);
+  a.v_out = static_cast<__nv_bfloat16*>(v_out);
+  a.out_stride_t = out_stride_t;
+  a.out_stride_g = out_stride_g;
+  a.heads_per_group = heads_per_group;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(tokens));
+  const int threads = ogx::kRowThreads;
+  const bool wf = weight_dtype == OGX_DTYPE_F32;
+  const bool cf = cs_dtype == OGX_DTYPE_F32;
+  if (wf) {
+    if (cf) ogx::qk_rmsnorm_rope_kernel<float, float><<<grid, threads, 0, s>>>(a);
+    else ogx::qk_rmsnorm_rope_kernel<float, __nv_bfloat16><<<grid, threads, 0, s>>>(a);
+  } else {
+    if (cf) ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, float><<<grid, threads, 0, s>>>(a);
+    else ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, s>>>(a);
+  }
+  return check_launch("qk_rmsnorm_rope_kernel");
+}
+
+int ogx_video_qk_rmsnorm_rope(const void* q, const void* k, int64_t tokens, int64_t in_stride_t,
+                              const void* q_weight, const void* k_weight, int weight_dtype, float eps,
+                              const void* cos, const void* sin, int cs_dtype, int64_t cs_stride_h,
+                              int64_t cs_stride_t, void* q_out, void* k_out, int64_t out_stride_t, void* stream) {
+  return ogx_video_qkv_rmsnorm_rope_scatter(q, k, nullptr, tokens, in_stride_t, q_weight, k_weight, weight_dtype, eps,
+                                            cos, sin, cs_dtype, cs_stride_h, cs_stride_t, q_out, k_out, nullptr,
+                                            out_stride_t, 0, 32, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int gemm_common(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                const float* scale_a, const float* scale_b, int64_t n_per_scale, CUtensorMap* ma, CUtensorMap* mb) {
+  if (a == nullptr || w == nullptr || scale_a == nullptr || scale_b == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (M < 0 || N <= 0 || K <= 0) return fail(OGX_EINVAL, "shape");
+  if (K % 16 || N % 32) return fail(OGX_EINVAL, "shape: K % 16 and N % 32 must be 0");
+  if (lda < K || ldw < K || lda % 16 || ldw % 16) return fail(OGX_EINVAL, "leading_dimension");
+  if (n_per_scale <= 0 || n_per_scale % 32) return fail(OGX_EINVAL, "n_per_scale");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(OGX_EINVAL, "shape");
+  if (!aligned16(a) || !aligned16(w)) return fail(OGX_EINVAL, "alignment");
+  if (M == 0) return OGX_OK;
+  const uint64_t da[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+  const uint64_t sa[1] = {static_cast<uint64_t>(lda)};
+  const uint32_t ba[2] = {static_cast<uint32_t>(ogx::gemm::BK), static_cast<uint32_t>(ogx::gemm::BM)};
+  int rc = make_map(ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa, ba);
+  if (rc) return rc;
+  const uint64_t db[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+  const uint64_t sb[1] = {static_cast<uint64_t>(ldw)};
+  const uint32_t bb[2] = {static_cast<uint32_t>(ogx::gemm::BK), static_cast<uint32_t>(ogx::gemm::BN)};
+  return make_map(mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, db, sb, bb);
+}
+
+template <int EPI>
+int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::Params& p, cudaStream_t s) {
+  auto kern = ogx::gemm::fp8_gemm_kernel<EPI>;
+  int rc = ensure_smem(kern, ogx::gemm::SMEM_BYTES);
+  if (rc) return rc;
+  const int tiles = ((p.M + ogx::gemm::BM - 1) / ogx::gemm::BM) * ((p.N + ogx::gemm::BN - 1) / ogx::gemm::BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, ogx::gemm::kThreads, ogx::gemm::SMEM_BYTES, s>>>(ma, mb, p);
+  return check_launch("fp8_gemm_kernel");
+}
+
+int attention_common(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens, int64_t heads,
+                     int64_t head_dim, int64_t stride_b, int64_t stride_t, CUtensorMap* mq, CUtensorMap* mk,
+                     CUtensorMap* mv) {
+  if (q == nullptr || k == nullptr || v == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (head_dim != 128) return fail(OGX_EINVAL, "head_dim: only 128 is supported");
+  if (batch < 1 || tokens < 1 || heads < 1) return fail(OGX_EINVAL, "shape");
+  if (tokens > INT32_MAX || heads > 65535 || batch > 65535) return fail(OGX_EINVAL, "shape");
+  if (stride_t % 8 || stride_b % 8 || stride_t < heads * 128) return fail(OGX_EINVAL, "stride");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(OGX_EINVAL, "alignment");
+  const uint64_t dims[4] = {128, static_cast<uint64_t>(heads), static_cast<uint64_t>(tokens),
+                            static_cast<uint64_t>(batch)};
+  const uint64_t strides[3] = {256, static_cast<uint64_t>(stride_t) * 2, static_cast<uint64_t>(stride_b) * 2};
+  const uint32_t box[4] = {64, 1, 128, 1};
+  int rc = make_map(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, q, dims, strides, box);
+  if (rc) return rc;
+  rc = make_map(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k, dims, strides, box);
+  if (rc) return rc;
+  return make_map(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v, dims, strides, box);
+}
+
+template <bool E4M3>
+int attention_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int64_t batch,
+                     int64_t tokens, int64_t heads, const ogx::fmha::Params& p, cudaStream_t s) {
+  auto kern = ogx::fmha::fmha_fwd_kernel<E4M3>;
+  int rc = ensure_smem(kern, ogx::fmha::SMEM_BYTES);
+  if (rc) return rc;
+  const dim3 grid(static_cast<unsigned>((tokens + 255) / 256), static_cast<unsigned>(heads),
+                  static_cast<unsigned>(batch));
+  kern<<<grid, ogx::fmha::kThreads, ogx::fmha::SMEM_BYTES, s>>>(mq, mk, mv, p);
+  return check_launch("fmha_fwd_kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int ogx_fp8_scaled_mm(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                      const float* scale_a, const float* scale_b, int64_t n_per_scale, const void* bias,
+                      int bias_dtype, void* out, int64_t ldo, void* stream) {
+  CUtensorMap ma, mb;
+  int rc = gemm_common(a, M, K, lda, w, N, ldw, scale_a, scale_b, n_per_scale, &ma, &mb);
+  if (rc || M == 0) return rc;
+  if (out == nullptr || !aligned16(out) || ldo % 8 || ldo < N) return fail(OGX_EINVAL, "output");
+  if (bias != nullptr && (!dtype_ok(bias_dtype) || !aligned16(bias))) return fail(OGX_EINVAL, "bias");
+  ogx::gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.scale_a = scale_a;
+  p.scale_b = scale_b;
+  p.n_per_scale = static_cast<int>(n_per_scale);
+  p.bias = bias;
+  p.bias_fp32 = bias_dtype == OGX_DTYPE_F32;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  return gemm_launch<ogx::gemm::EPI_BIAS>(ma, mb, p, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_fp8_scaled_mm_residual_gate(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
+                                    int64_t ldw, const float* scale_a, const float* scale_b, int64_t n_per_scale,
+                                    const void* bias, int bias_dtype, const void* x, int64_t ldx,
+                                    const void* table, int table_dtype, int64_t table_stride_row,
+                                    const void* timestep, int timestep_dtype, int64_t ts_stride_t,
+                                    int64_t ts_stride_p, int gate_index, void* out, int64_t ldo, void* stream) {
+  CUtensorMap ma, mb;
+  int rc = gemm_common(a, M, K, lda, w, N, ldw, scale_a, scale_b, n_per_scale, &ma, &mb);
+  if (rc || M == 0) return rc;
+  if (out == nullptr || !aligned16(out) || ldo % 8 || ldo < N) return fail(OGX_EINVAL, "output");
+  if (bias != nullptr && (!dtype_ok(bias_dtype) || !aligned16(bias))) return fail(OGX_EINVAL, "bias");
+  if (x == nullptr || !aligned16(x) || ldx % 8 || ldx < N) return fail(OGX_EINVAL, "residual");
+  if (table == nullptr || timestep == nullptr || !dtype_ok(table_dtype) || !dtype_ok(timestep_dtype) ||
+      gate_index < 0)
+    return fail(OGX_EINVAL, "ada");
+  const int tesz = timestep_dtype == OGX_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(table) || !aligned16(timestep) || (ts_stride_t * tesz) % 16 || (ts_stride_p * tesz) % 16)
+    return fail(OGX_EINVAL, "timestep_stride");
+  ogx::gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.scale_a = scale_a;
+  p.scale_b = scale_b;
+  p.n_per_scale = static_cast<int>(n_per_scale);
+  p.bias = bias;
+  p.bias_fp32 = bias_dtype == OGX_DTYPE_F32;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.resid_x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.table = table;
+  p.table_fp32 = table_dtype == OGX_DTYPE_F32;
+  p.table_stride_row = table_stride_row;
+  p.ts = timestep;
+  p.ts_fp32 = timestep_dtype == OGX_DTYPE_F32;
+  p.ts_stride_t = ts_stride_t;
+  p.ts_stride_p = ts_stride_p;
+  p.gate_index = gate_index;
+  return gemm_launch<ogx::gemm::EPI_RESIDUAL>(ma, mb, p, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_attention_fwd(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens, int64_t heads,
+                      int64_t head_dim, int64_t stride_b, int64_t stride_t, float softmax_scale, void* out,
+                      int64_t out_stride_b, int64_t out_stride_t, void* stream) {
+  CUtensorMap mq, mk, mv;
+  int rc = attention_common(q, k, v, batch, tokens, heads, head_dim, stride_b, stride_t, &mq, &mk, &mv);
+  if (rc) return rc;
+  if (out == nullptr || !aligned16(out) || out_stride_t % 8 || out_stride_b % 8) return fail(OGX_EINVAL, "output");
+  ogx::fmha::Params p{};
+  p.L = static_cast<int>(tokens);
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_b = out_stride_b;
+  p.out_stride_t = out_stride_t;
+  return attention_launch<false>(mq, mk, mv, batch, tokens, heads, p, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_attention_fwd_e4m3(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens,
+                           int64_t heads, int64_t head_dim, int64_t stride_b, int64_t stride_t, float softmax_scale,
+                           const float* out_scale, void* out_q, int64_t out_stride_b, int64_t out_stride_t,
+                           void* stream) {
+  CUtensorMap mq, mk, mv;
+  int rc = attention_common(q, k, v, batch, tokens, heads, head_dim, stride_b, stride_t, &mq, &mk, &mv);
+  if (rc) return rc;
+  if (out_q == nullptr || out_scale == nullptr || (reinterpret_cast<uintptr_t>(out_q) & 7u) || out_stride_t % 8 ||
+      out_stride_b % 8)
+    return fail(OGX_EINVAL, "output");
+  ogx::fmha::Params p{};
+  p.L = static_cast<int>(tokens);
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.out_q = static_cast<uint8_t*>(out_q);
+  p.out_scale = out_scale;
+  p.out_stride_b = out_stride_b;
+  p.out_stride_t = out_stride_t;
+  return attention_launch<true>(mq, mk, mv, batch, tokens, heads, p, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,505 @@
+"""B200-native operator surface of the LTX-2.3 video self-attention block.
+
+Drop-in counterparts of the hot-path functions of ``ltx_serve/triton_ltx_ops.py``
+(same names, argument meaning and reason strings).  Every op runs a hand-written
+sm_100a kernel through the C ABI in ``libogx.so``.  Where the reference's guard
+would fall back to eager torch, these ops raise ``ValueError(reason)``: there is
+no CPU or torch fallback.
+
+Ownership follows the reference wrappers: outputs are allocated here with
+``torch.empty_like`` / ``torch.empty`` on the input's device and the kernels
+only read inputs and write outputs, on the current CUDA stream.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import DTYPE_BF16, DTYPE_F16, DTYPE_F32, QUANT_SINGLE, QUANT_TORCH
+
+# Call counters, as the reference keeps them (triton_ltx_ops.py:1902-1946).
+_VIDEO_ADA_VALUES_CALLS = 0
+_VIDEO_TEXT_ADALN_CALLS = 0
+
+_DTYPE_CODES = {torch.bfloat16: DTYPE_BF16, torch.float32: DTYPE_F32, torch.float16: DTYPE_F16}
+
+
+def _code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODES[t.dtype]
+    except KeyError as exc:
+        raise ValueError(f"unsupported dtype {t.dtype}") from exc
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("device: the B200 ops need CUDA tensors (there is no CPU path)")
+
+
+# ---------------------------------------------------------------- guards (reference reason strings)
+def ada_from_table_guard_reason(x: torch.Tensor, scale_shift_table: torch.Tensor, timestep: torch.Tensor) -> str | None:
+    """Mirrors `_can_use_ada_from_table` (ltx_serve/triton_ltx_ops.py:1001-1018) as a reason string."""
+    if not x.is_cuda or not x.is_contiguous() or x.dtype != torch.bfloat16:
+        return "x_device_or_dtype"
+    if x.ndim != 3 or x.shape[-1] not in (2048, 4096):
+        return "x_shape"
+    if not scale_shift_table.is_cuda or scale_shift_table.dtype not in (torch.bfloat16, torch.float32):
+        return "table_device_or_dtype"
+    if scale_shift_table.ndim != 2 or scale_shift_table.shape[-1] != x.shape[-1]:
+        return "table_shape"
+    if scale_shift_table.stride(-1) != 1:
+        return "table_stride"
+    if not timestep.is_cuda or timestep.dtype not in (torch.bfloat16, torch.float32) or timestep.ndim < 2:
+        return "timestep_device_or_dtype"
+    if timestep.shape[0] != x.shape[0] or timestep.shape[1] != x.shape[1]:
+        return "timestep_shape"
+    if timestep.numel() != x.shape[0] * x.shape[1] * scale_shift_table.shape[0] * x.shape[-1]:
+        return "timestep_numel"
+    return None
+
+
+def _ts_view(x: torch.Tensor, table: torch.Tensor, timestep: torch.Tensor) -> torch.Tensor:
+    ts_view = timestep.reshape(x.shape[0], timestep.shape[1], table.shape[0], x.shape[-1])
+    if ts_view.stride(-1) != 1:
+        ts_view = ts_view.contiguous()
+    return ts_view
+
+
+def _check_index(table: torch.Tensor, *indices: int) -> None:
+    for idx in indices:
+        if not 0 <= idx < table.shape[0]:
+            raise ValueError("ada_index")
+
+
+# ---------------------------------------------------------------- AdaZero
+def fused_adazero_from_ada(
+    x: torch.Tensor,
+    eps: float,
+    scale_shift_table: torch.Tensor,
+    timestep: torch.Tensor,
+    *,
+    shift_index: int,
+    scale_index: int,
+    counter: str = "video",
+) -> torch.Tensor:
+    """`rmsnorm(x)*(1+scale)+shift` with shift/scale from the table + timestep.
+
+    Reference: fused_adazero_from_ada, ltx_serve/triton_ltx_ops.py:40-91 (GPU kernel
+    :3359-3427: fp32 math, one bf16 rounding).
+    """
+    global _VIDEO_ADA_VALUES_CALLS
+    reason = ada_from_table_guard_reason(x, scale_shift_table, timestep)
+    if reason is not None:
+        raise ValueError(reason)
+    _check_index(scale_shift_table, shift_index, scale_index)
+    if counter == "video":
+        _VIDEO_ADA_VALUES_CALLS += 1
+    ts_view = _ts_view(x, scale_shift_table, timestep)
+    y = torch.empty_like(x)
+    _lib.call(
+        "ogx_adazero_from_ada",
+        x.data_ptr(), x.shape[0], x.shape[1], x.shape[2],
+        scale_shift_table.data_ptr(), _code(scale_shift_table), scale_shift_table.stride(0),
+        ts_view.data_ptr(), _code(ts_view), ts_view.stride(0), ts_view.stride(1), ts_view.stride(2),
+        shift_index, scale_index, float(eps), y.data_ptr(), _stream(x),
+    )
+    return y
+
+
+def fused_adazero_from_ada_fp8(
+    x: torch.Tensor,
+    eps: float,
+    scale_shift_table: torch.Tensor,
+    timestep: torch.Tensor,
+    input_scale: torch.Tensor,
+    *,
+    shift_index: int,
+    scale_index: int,
+    return_bf16: bool = False,
+    quant_mode: int = QUANT_TORCH,
+) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
+    """AdaZero fused with the E4M3 quantiser of the following FP8 linear.
+
+    Equals ``fused_fp8_quantize_e4m3(fused_adazero_from_ada(...), input_scale)``
+    bit for bit (reference :40-91 then :144-161), without writing the bf16
+    activation unless ``return_bf16``.
+    """
+    global _VIDEO_ADA_VALUES_CALLS
+    reason = ada_from_table_guard_reason(x, scale_shift_table, timestep)
+    if reason is not None:
+        raise ValueError(reason)
+    _check_index(scale_shift_table, shift_index, scale_index)
+    if input_scale.numel() != 1 or not input_scale.is_cuda or input_scale.dtype != torch.float32:
+        raise ValueError("input_scale")
+    _VIDEO_ADA_VALUES_CALLS += 1
+    ts_view = _ts_view(x, scale_shift_table, timestep)
+    q = torch.empty(x.shape, device=x.device, dtype=torch.float8_e4m3fn)
+    y = torch.empty_like(x) if return_bf16 else None
+    _lib.call(
+        "ogx_adazero_from_ada_e4m3",
+        x.data_ptr(), x.shape[0], x.shape[1], x.shape[2],
+        scale_shift_table.data_ptr(), _code(scale_shift_table), scale_shift_table.stride(0),
+        ts_view.data_ptr(), _code(ts_view), ts_view.stride(0), ts_view.stride(1), ts_view.stride(2),
+        shift_index, scale_index, float(eps), input_scale.data_ptr(), int(quant_mode), _ptr(y), q.data_ptr(),
+        _stream(x),
+    )
+    return (q, y) if return_bf16 else q
+
+
+# ---------------------------------------------------------------- quantiser
+def fused_fp8_quantize_e4m3(x: torch.Tensor, input_scale: torch.Tensor, *, quant_mode: int = QUANT_TORCH) -> torch.Tensor:
+    """Per-tensor E4M3 quantisation, bit-exact to the reference's torch path.
+
+    Reference: fused_fp8_quantize_e4m3, ltx_serve/triton_ltx_ops.py:144-161; the
+    torch path :146-148 is ``clamp(x * input_scale.reciprocal(), -448, 448).to(e4m3)``.
+    ``quant_mode=QUANT_SINGLE`` gives the single-rounding semantics of the
+    reference's Triton kernel (:3429-3444) instead.
+    """
+    _require_cuda(x, input_scale)
+    if not x.is_contiguous() or input_scale.numel() != 1 or x.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("fp8_quantize_input")
+    if input_scale.dtype != torch.float32:
+        raise ValueError("input_scale")
+    q = torch.empty_strided(x.shape, x.stride(), device=x.device, dtype=torch.float8_e4m3fn)
+    _lib.call(
+        "ogx_fp8_quantize_e4m3",
+        x.data_ptr(), _code(x), x.numel(), input_scale.data_ptr(), int(quant_mode), q.data_ptr(), _stream(x),
+    )
+    return q
+
+
+# ---------------------------------------------------------------- bias add / residual
+def fused_bias_add_bf16(x: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """``x + bias.to(bf16)``; reference ltx_serve/triton_ltx_ops.py:185-201."""
+    _require_cuda(x, bias)
+    if not x.is_contiguous() or x.dtype != torch.bfloat16 or x.ndim < 2:
+        raise ValueError("bias_add_input")
+    if bias.ndim != 1 or bias.shape[0] != x.shape[-1] or bias.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("bias_shape")
+    out = torch.empty_like(x)
+    cols = x.shape[-1]
+    _lib.call(
+        "ogx_bias_add_bf16", x.data_ptr(), x.numel() // cols, cols, bias.contiguous().data_ptr(), _code(bias),
+        out.data_ptr(), _stream(x),
+    )
+    return out
+
+
+def fused_residual_gate_bias_from_ada(
+    x: torch.Tensor,
+    y_no_bias: torch.Tensor,
+    bias: torch.Tensor,
+    scale_shift_table: torch.Tensor,
+    timestep: torch.Tensor,
+    *,
+    gate_index: int,
+    count_video_ada: bool = True,
+) -> torch.Tensor:
+    """``x + (y + bias.to(bf16)) * gate`` with bf16 rounding after each op.
+
+    Reference: fused_residual_gate_bias_from_ada, ltx_serve/triton_ltx_ops.py:204-262
+    (kernel :3663-3721), pinned bitwise by tests/test_triton_ltx_ops.py:182-204.
+    """
+    global _VIDEO_ADA_VALUES_CALLS, _VIDEO_TEXT_ADALN_CALLS
+    reason = ada_from_table_guard_reason(x, scale_shift_table, timestep)
+    if reason is not None:
+        raise ValueError(reason)
+    if not y_no_bias.is_contiguous() or y_no_bias.shape != x.shape or y_no_bias.dtype != torch.bfloat16:
+        raise ValueError("y_shape")
+    if bias.ndim != 1 or bias.shape[0] != x.shape[-1] or bias.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("bias_shape")
+    _check_index(scale_shift_table, gate_index)
+    if count_video_ada:
+        _VIDEO_ADA_VALUES_CALLS += 1
+    else:
+        _VIDEO_TEXT_ADALN_CALLS += 1
+    ts_view = _ts_view(x, scale_shift_table, timestep)
+    out = torch.empty_like(x)
+    _lib.call(
+        "ogx_residual_gate_bias_from_ada",
+        x.data_ptr(), y_no_bias.data_ptr(), x.shape[0], x.shape[1], x.shape[2],
+        bias.contiguous().data_ptr(), _code(bias),
+        scale_shift_table.data_ptr(), _code(scale_shift_table), scale_shift_table.stride(0),
+        ts_view.data_ptr(), _code(ts_view), ts_view.stride(0), ts_view.stride(1), ts_view.stride(2),
+        gate_index, out.data_ptr(), _stream(x),
+    )
+    return out
+
+
+# ---------------------------------------------------------------- Q/K RMSNorm + split RoPE
+def fused_video_qk_rmsnorm_rope_guard_reason(
+    q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor
+) -> str | None:
+    """Mirrors `_fused_video_qk_rmsnorm_rope_guard_reason` (ltx_serve/triton_ltx_ops.py:1513-1537)."""
+    if not q.is_cuda or not k.is_cuda or q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        return "qk_device_or_dtype"
+    if q.shape != k.shape or q.ndim != 3 or q.shape[0] != 1 or q.shape[-1] != 4096:
+        return "qk_shape"
+    if q.shape[1] < 1:
+        return "empty_tokens"
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or q.stride(1) != k.stride(1) or q.stride(1) % 8:
+        return "qk_noncontiguous"
+    if q_weight.shape != (4096,) or k_weight.shape != (4096,) or q_weight.dtype != k_weight.dtype:
+        return "qk_weight_shape"
+    if cos.ndim != 4 or sin.ndim != 4 or cos.shape != sin.shape or cos.stride() != sin.stride() or cos.dtype != sin.dtype:
+        return "rope_shape"
+    if cos.shape[0] not in (1, q.shape[0]) or cos.shape[1] != 32 or cos.shape[2] != q.shape[1] or cos.shape[3] != 64:
+        return "rope_shape"
+    if cos.stride(-1) != 1:
+        return "rope_shape"
+    return None
+
+
+def fused_video_qk_rmsnorm_rope(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    q_weight: torch.Tensor,
+    k_weight: torch.Tensor,
+    eps: float,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    *,
+    out: tuple[torch.Tensor, torch.Tensor] | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Q/K RMSNorm over 4096 columns + split RoPE per head; q/k [1, L, 4096] bf16, cos/sin [1|B, 32, L, 64].
+
+    Reference: fused_video_qk_rmsnorm_rope, ltx_serve/triton_ltx_ops.py:320-378
+    (kernel :3901-3978).  ``out`` may alias (q, k) for an in-place update.
+    """
+    reason = fused_video_qk_rmsnorm_rope_guard_reason(q, k, q_weight, k_weight, cos, sin)
+    if reason is not None:
+        raise ValueError(reason)
+    if out is None:
+        q_out, k_out = torch.empty_like(q), torch.empty_like(k)
+    else:
+        q_out, k_out = out
+        if q_out.stride(1) != k_out.stride(1) or q_out.shape != q.shape or k_out.shape != k.shape:
+            raise ValueError("qk_out_shape")
+    _lib.call(
+        "ogx_video_qk_rmsnorm_rope",
+        q.data_ptr(), k.data_ptr(), q.shape[1], q.stride(1),
+        q_weight.contiguous().data_ptr(), k_weight.contiguous().data_ptr(), _code(q_weight), float(eps),
+        cos.data_ptr(), sin.data_ptr(), _code(cos), cos.stride(1), cos.stride(2),
+        q_out.data_ptr(), k_out.data_ptr(), q_out.stride(1), _stream(q),
+    )
+    return q_out, k_out
+
+
+# ---------------------------------------------------------------- FP8 linears
+def _scale_ptr(t: torch.Tensor) -> int:
+    if t.numel() != 1 or t.dtype != torch.float32 or not t.is_cuda:
+        raise ValueError("scale")
+    return t.data_ptr()
+
+
+def fp8_scaled_mm(
+    qinput: torch.Tensor,
+    weight: torch.Tensor,
+    scale_a: torch.Tensor,
+    scale_b: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    n_per_scale: int | None = None,
+) -> torch.Tensor:
+    """``bf16(qinput @ weight.t() * scale_a * scale_b) (+ bf16(bias))`` on tcgen05.
+
+    Counterpart of ``torch._scaled_mm(qinput, weight.t(), scale_a, scale_b,
+    out_dtype=bf16, use_fast_accum=True)`` followed by the bias add of
+    FP8Linear.forward (ltx_serve/triton_ltx_ops.py:1695-1707).  ``scale_b`` may
+    hold one scale per ``n_per_scale`` output columns (packed Q/K/V weights).
+    """
+    _require_cuda(qinput, weight, scale_a, scale_b)
+    if qinput.dtype != torch.float8_e4m3fn or weight.dtype != torch.float8_e4m3fn:
+        raise ValueError("fp8_dtype")
+    a2 = qinput.reshape(-1, qinput.shape[-1])
+    if a2.stride(-1) != 1 or weight.stride(-1) != 1 or weight.ndim != 2 or weight.shape[1] != a2.shape[1]:
+        raise ValueError("fp8_shape")
+    M, K = a2.shape
+    N = weight.shape[0]
+    if scale_a.numel() != 1 or scale_a.dtype != torch.float32 or scale_b.dtype != torch.float32:
+        raise ValueError("scale")
+    nps = n_per_scale if n_per_scale is not None else N // scale_b.numel()
+    if nps * scale_b.numel() != N:
+        raise ValueError("scale")
+    if out is None:
+        out = torch.empty((M, N), device=qinput.device, dtype=torch.bfloat16)
+    if bias is not None and (bias.ndim != 1 or bias.shape[0] != N):
+        raise ValueError("bias_shape")
+    _lib.call(
+        "ogx_fp8_scaled_mm",
+        a2.data_ptr(), M, K, a2.stride(0), weight.data_ptr(), N, weight.stride(0),
+        scale_a.data_ptr(), scale_b.contiguous().data_ptr(), nps,
+        _ptr(bias.contiguous()) if bias is not None else None, _code(bias) if bias is not None else DTYPE_BF16,
+        out.data_ptr(), out.stride(0), _stream(qinput),
+    )
+    return out.reshape(*qinput.shape[:-1], N)
+
+
+def fp8_linear_from_quantized_e4m3(linear, qinput: torch.Tensor, *, out_dtype: torch.dtype) -> torch.Tensor:
+    """Reference: fp8_linear_from_quantized_e4m3, ltx_serve/triton_ltx_ops.py:742-759."""
+    if out_dtype != torch.bfloat16:
+        raise ValueError("out_dtype")
+    return fp8_scaled_mm(qinput, linear.weight, linear.input_scale, linear.weight_scale, bias=linear.bias)
+
+
+def fp8_linear_without_bias(linear, x: torch.Tensor, *, out_dtype: torch.dtype) -> torch.Tensor:
+    """Quantise x with the linear's input scale and run the FP8 matmul without bias.
+
+    Reference: fp8_linear_without_bias, ltx_serve/triton_ltx_ops.py:762-781.
+    """
+    if out_dtype != torch.bfloat16:
+        raise ValueError("out_dtype")
+    if x.shape[-1] != linear.in_features:
+        raise ValueError("in_features")
+    qinput = fused_fp8_quantize_e4m3(x.contiguous(), linear.input_scale)
+    return fp8_scaled_mm(qinput, linear.weight, linear.input_scale, linear.weight_scale)
+
+
+def fp8_linear_forward(linear, x: torch.Tensor) -> torch.Tensor:
+    """The patched FP8Linear.forward (ltx_serve/triton_ltx_ops.py:1676-1716): quant -> scaled-mm -> bias."""
+    qinput = fused_fp8_quantize_e4m3(x.contiguous(), linear.input_scale)
+    return fp8_scaled_mm(qinput, linear.weight, linear.input_scale, linear.weight_scale, bias=linear.bias)
+
+
+def fp8_qkv_from_shared_quantized_input(attn, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None:
+    """Q/K/V from one quantised input; reference ltx_serve/triton_ltx_ops.py:805-819.
+
+    Returns None when the three input scales differ (as the reference's guard does).
+    """
+    scales = [attn.to_q.input_scale, attn.to_k.input_scale, attn.to_v.input_scale]
+    if not all(torch.equal(scales[0], s) for s in scales[1:]):
+        return None
+    qinput = fused_fp8_quantize_e4m3(x.contiguous(), attn.to_q.input_scale)
+    return (
+        fp8_linear_from_quantized_e4m3(attn.to_q, qinput, out_dtype=x.dtype),
+        fp8_linear_from_quantized_e4m3(attn.to_k, qinput, out_dtype=x.dtype),
+        fp8_linear_from_quantized_e4m3(attn.to_v, qinput, out_dtype=x.dtype),
+    )
+
+
+def fp8_scaled_mm_residual_gate(
+    qinput: torch.Tensor,
+    weight: torch.Tensor,
+    scale_a: torch.Tensor,
+    scale_b: torch.Tensor,
+    bias: torch.Tensor,
+    x: torch.Tensor,
+    scale_shift_table: torch.Tensor,
+    timestep: torch.Tensor,
+    *,
+    gate_index: int,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Out-projection fused with bias + Ada-gated residual (batch 1).
+
+    Equals ``fused_residual_gate_bias_from_ada(x, fp8_linear_without_bias(...), bias,
+    table, timestep, gate_index=...)`` (reference :762-781 then :204-262) given the
+    same fp32 accumulation.
+    """
+    global _VIDEO_ADA_VALUES_CALLS
+    reason = ada_from_table_guard_reason(x, scale_shift_table, timestep)
+    if reason is not None:
+        raise ValueError(reason)
+    if x.shape[0] != 1:
+        raise ValueError("x_shape")
+    _check_index(scale_shift_table, gate_index)
+    a2 = qinput.reshape(-1, qinput.shape[-1])
+    M, K = a2.shape
+    N = weight.shape[0]
+    if x.shape[1] != M or x.shape[2] != N:
+        raise ValueError("x_shape")
+    _VIDEO_ADA_VALUES_CALLS += 1
+    ts_view = _ts_view(x, scale_shift_table, timestep)
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call(
+        "ogx_fp8_scaled_mm_residual_gate",
+        a2.data_ptr(), M, K, a2.stride(0), weight.data_ptr(), N, weight.stride(0),
+        _scale_ptr(scale_a), _scale_ptr(scale_b), N,
+        bias.contiguous().data_ptr(), _code(bias), x.data_ptr(), x.stride(1),
+        scale_shift_table.data_ptr(), _code(scale_shift_table), scale_shift_table.stride(0),
+        ts_view.data_ptr(), _code(ts_view), ts_view.stride(1), ts_view.stride(2), gate_index,
+        out.data_ptr(), out.stride(1), _stream(x),
+    )
+    return out
+
+
+# ---------------------------------------------------------------- attention
+def attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    heads: int,
+    *,
+    softmax_scale: float | None = None,
+    out: torch.Tensor | None = None,
+    out_e4m3_scale: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Dense bidirectional attention, q/k/v [B, L, H*128] bf16 (token rows may be strided).
+
+    The attention-backend contract of the reference (benchmarks/official_ltx23_benchmark.py:3289-3373;
+    call site ltx_serve/triton_ltx_ops.py:2636).  With ``out_e4m3_scale`` the bf16
+    result is quantised to e4m3 in the epilogue (torch-path semantics).
+    """
+    _require_cuda(q, k, v)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise ValueError("qkv_dtype")
+    if q.ndim != 3 or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("qkv_shape")
+    B, L, HD = q.shape
+    if HD % heads or HD // heads != 128:
+        raise ValueError("head_dim")
+    if q.stride() != k.stride() or q.stride() != v.stride() or q.stride(-1) != 1:
+        raise ValueError("qkv_stride")
+    scale = float(softmax_scale) if softmax_scale is not None else 128 ** -0.5
+    if out_e4m3_scale is None:
+        if out is None:
+            out = torch.empty((B, L, HD), device=q.device, dtype=torch.bfloat16)
+        _lib.call(
+            "ogx_attention_fwd",
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, heads, 128, q.stride(0), q.stride(1), scale,
+            out.data_ptr(), out.stride(0), out.stride(1), _stream(q),
+        )
+    else:
+        if out is None:
+            out = torch.empty((B, L, HD), device=q.device, dtype=torch.float8_e4m3fn)
+        _lib.call(
+            "ogx_attention_fwd_e4m3",
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, heads, 128, q.stride(0), q.stride(1), scale,
+            _scale_ptr(out_e4m3_scale), out.data_ptr(), out.stride(0), out.stride(1), _stream(q),
+        )
+    return out
+
+
+def collect_video_ada_values_calls() -> int:
+    return _VIDEO_ADA_VALUES_CALLS
+
+
+__all__ = [
+    "QUANT_SINGLE",
+    "QUANT_TORCH",
+    "attention",
+    "fp8_linear_forward",
+    "fp8_linear_from_quantized_e4m3",
+    "fp8_linear_without_bias",
+    "fp8_qkv_from_shared_quantized_input",
+    "fp8_scaled_mm",
+    "fp8_scaled_mm_residual_gate",
+    "fused_adazero_from_ada",
+    "fused_adazero_from_ada_fp8",
+    "fused_bias_add_bf16",
+    "fused_fp8_quantize_e4m3",
+    "fused_residual_gate_bias_from_ada",
+    "fused_video_qk_rmsnorm_rope",
+]

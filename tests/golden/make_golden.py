@@ -1,0 +1,167 @@
+"""Generates the golden fixtures in this directory from the reference itself.
+
+Run in a container where the reference (plugyawn/opengenie) is importable:
+
+    python tests/golden/make_golden.py --reference /path/to/opengenie
+
+It imports ``ltx_serve.triton_ltx_ops`` on the CPU, where every CUDA/Triton guard
+fails and the reference's own torch paths run, and records their outputs on
+seeded inputs:
+
+- quant_bf16.npz / quant_f16.npz: ``fused_fp8_quantize_e4m3`` (torch path,
+  triton_ltx_ops.py:146-148) on every bf16 / fp16 bit pattern for several scales;
+- ops.npz: ``fused_adazero_from_ada`` (:40-91), ``fused_bias_add_bf16`` (:185-201),
+  ``fused_residual_gate_bias_from_ada`` (:204-262, residual mode
+  "triton_simple_bf16_round" as production sets it) and the reference test's
+  split-RoPE restatement (tests/test_triton_ltx_ops.py:232-249);
+- block.npz: the video self-attention block composed from those functions with
+  CPU ``torch._scaled_mm`` (the FP8 linears) and fp32 SDPA, for a 16-token input
+  with the synthetic weights of ``opengenie_b200.synthetic.make_weights(seed=7)``.
+
+Inputs that are cheap to regenerate (seeded ``torch.Generator``) are stored too so
+the tests do not depend on regeneration.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+QUANT_SCALES_BF16 = [1.0, 0.0371, 0.00123, 3.7, 0.0107421875, 1.0 / 448.0]
+QUANT_SCALES_F16 = [1.0, 0.0371, 0.5]
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def load_reference(root: str):
+    sys.path.insert(0, root)
+    import ltx_serve.triton_ltx_ops as ops  # noqa: E402
+
+    ops._BLOCK_RESIDUAL_MODE = "triton_simple_bf16_round"
+    spec = importlib.util.spec_from_file_location("ref_kernel_tests", os.path.join(root, "tests", "test_triton_ltx_ops.py"))
+    tests = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(tests)
+    return ops, tests._torch_video_rmsnorm_split_rope
+
+
+def make_quant(ops) -> None:
+    allbits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    xb = torch.from_numpy(allbits.view(np.int16)).view(torch.bfloat16)
+    codes = []
+    for s in QUANT_SCALES_BF16:
+        q = ops.fused_fp8_quantize_e4m3(xb.reshape(256, 256), torch.tensor(s, dtype=torch.float32))
+        codes.append(q.view(torch.uint8).reshape(-1).numpy().copy())
+    np.savez_compressed(os.path.join(HERE, "quant_bf16.npz"), scales=np.array(QUANT_SCALES_BF16, np.float32),
+                        codes=np.stack(codes))
+    xh = torch.from_numpy(allbits.view(np.int16)).view(torch.float16)
+    codes = []
+    for s in QUANT_SCALES_F16:
+        q = ops.fused_fp8_quantize_e4m3(xh.reshape(256, 256), torch.tensor(s, dtype=torch.float32))
+        codes.append(q.view(torch.uint8).reshape(-1).numpy().copy())
+    np.savez_compressed(os.path.join(HERE, "quant_f16.npz"), scales=np.array(QUANT_SCALES_F16, np.float32),
+                        codes=np.stack(codes))
+
+
+def make_ops(ops, rope_ref) -> None:
+    out = {}
+    g = torch.Generator().manual_seed(2024)
+    # AdaZero from table: [1, 5, 4096] with uniform (stride-0) timestep, idx 0/1, fp32 table
+    for tag, cols, rows, tdt, sh, sc in (("a", 4096, 5, torch.float32, 0, 1), ("b", 2048, 7, torch.bfloat16, 3, 4)):
+        x = torch.randn((1, rows, cols), generator=g).to(torch.bfloat16)
+        table = (torch.randn((6, cols), generator=g) * 0.5).to(tdt)
+        ts = torch.randn((1, rows, 6 * cols), generator=g).to(torch.bfloat16)
+        y = ops.fused_adazero_from_ada(x, 1e-6, table, ts, shift_index=sh, scale_index=sc)
+        out[f"ada_{tag}_x"] = bits(x)
+        out[f"ada_{tag}_table"] = table.float().numpy()
+        out[f"ada_{tag}_table_bf16"] = np.array(tdt == torch.bfloat16)
+        out[f"ada_{tag}_ts"] = bits(ts)
+        out[f"ada_{tag}_idx"] = np.array([sh, sc])
+        out[f"ada_{tag}_y"] = bits(y)
+    # bias add [11, 2048] with fp32 bias
+    x = torch.randn((11, 2048), generator=g).to(torch.bfloat16)
+    bias = torch.randn((2048,), generator=g)
+    out["bias_x"], out["bias_b"] = bits(x), bias.numpy()
+    out["bias_y"] = bits(ops.fused_bias_add_bf16(x, bias))
+    # bias + gate + residual [1, 9, 2048], fp32 table with 9 slots, gate idx 8 (the reference test's shape)
+    x = torch.randn((1, 9, 2048), generator=g).to(torch.bfloat16)
+    y = torch.randn((1, 9, 2048), generator=g).to(torch.bfloat16)
+    bias = torch.randn((2048,), generator=g)
+    table = torch.randn((9, 2048), generator=g)
+    ts = torch.randn((1, 9, 9 * 2048), generator=g).to(torch.bfloat16)
+    r = ops.fused_residual_gate_bias_from_ada(x, y, bias, table, ts, gate_index=8)
+    out.update(res_x=bits(x), res_y=bits(y), res_bias=bias.numpy(), res_table=table.numpy(), res_ts=bits(ts),
+               res_out=bits(r))
+    # Q/K RMSNorm + split RoPE restatement (tests/test_triton_ltx_ops.py:232-249), 17 tokens
+    q = torch.randn((1, 17, 4096), generator=g).to(torch.bfloat16)
+    w = (1.0 + 0.1 * torch.randn((4096,), generator=g)).to(torch.bfloat16)
+    freqs = torch.randn((1, 32, 17, 64), generator=g)
+    cos, sin = freqs.cos().to(torch.bfloat16), freqs.sin().to(torch.bfloat16)
+    o = rope_ref(q, w, 1e-6, cos, sin)
+    out.update(rope_x=bits(q), rope_w=bits(w), rope_cos=bits(cos), rope_sin=bits(sin), rope_out=bits(o))
+    np.savez_compressed(os.path.join(HERE, "ops.npz"), **out)
+
+
+def make_block(ops, rope_ref) -> None:
+    from opengenie_b200 import synthetic
+
+    cfg = synthetic.small_config(1, 2, 8)  # 16 tokens
+    inp = synthetic.make_inputs(cfg, seed=11)
+    w = synthetic.make_weights(seed=7)
+    x, ts, cos, sin = inp.x, inp.timestep, inp.cos, inp.sin
+    table = w.scale_shift_table
+    # static input scales (amax/448 of each FP8 linear's input), fixed here and stored
+    norm = ops.fused_adazero_from_ada(x, 1e-6, table, ts, shift_index=0, scale_index=1)
+    s_in = (norm.float().abs().amax() / 448.0).to(torch.float32)
+
+    def linear(inp_q, s_a, lin, bias=True):
+        o = torch._scaled_mm(inp_q.reshape(-1, inp_q.shape[-1]), lin.weight.t(), scale_a=s_a, scale_b=lin.weight_scale,
+                             out_dtype=torch.bfloat16, use_fast_accum=True)
+        if bias:
+            o = ops.fused_bias_add_bf16(o, lin.bias)
+        return o.reshape(1, -1, o.shape[-1])
+
+    xq = ops.fused_fp8_quantize_e4m3(norm, s_in)
+    q, k, v = (linear(xq, s_in, lin) for lin in (w.to_q, w.to_k, w.to_v))
+    qr = rope_ref(q, w.q_norm_weight, 1e-6, cos, sin)
+    kr = rope_ref(k, w.k_norm_weight, 1e-6, cos, sin)
+    qh, kh, vh = (t.float().view(1, -1, 32, 128).transpose(1, 2) for t in (qr, kr, v))
+    attn = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh).transpose(1, 2).reshape(1, -1, 4096)
+    attn = attn.to(torch.bfloat16)
+    s_out = (attn.float().abs().amax() / 448.0).to(torch.float32)
+    oq = ops.fused_fp8_quantize_e4m3(attn, s_out)
+    y = linear(oq, s_out, w.to_out, bias=False)
+    out = ops.fused_residual_gate_bias_from_ada(x, y, w.to_out.bias, table, ts, gate_index=2)
+    np.savez_compressed(
+        os.path.join(HERE, "block.npz"),
+        s_in=s_in.numpy(), s_out=s_out.numpy(), x=bits(x), out=bits(out), attn=bits(attn), q=bits(qr), k=bits(kr),
+        v=bits(v), xq=xq.view(torch.uint8).numpy(), seed_inputs=np.array(11), seed_weights=np.array(7),
+    )
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="root of the plugyawn/opengenie checkout")
+    args = ap.parse_args()
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    ops, rope_ref = load_reference(args.reference)
+    make_quant(ops)
+    make_ops(ops, rope_ref)
+    make_block(ops, rope_ref)
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            print(f, os.path.getsize(os.path.join(HERE, f)))
+
+
+if __name__ == "__main__":
+    main()

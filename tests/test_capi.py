@@ -1,0 +1,71 @@
+"""The C-ABI library loads and exports what include/ogx.h declares; host-side guards (no GPU needed)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from opengenie_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "ogx.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ogx_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == sorted(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol(ogx_lib):
+    for name in declared_functions():
+        assert hasattr(ogx_lib, name), name
+
+
+def test_version(ogx_lib):
+    assert ogx_lib.ogx_version() == 1
+
+
+def _err(ogx_lib):
+    return ogx_lib.ogx_last_error().decode()
+
+
+def test_guards_reject_before_touching_the_device(ogx_lib):
+    # tokens < 1 -> the reference's "empty_tokens" reason (triton_ltx_ops.py:1527-1528)
+    rc = ogx_lib.ogx_video_qk_rmsnorm_rope(1 << 20, 1 << 20, 0, 4096, 1 << 20, 1 << 20, 0, 1e-6, 1 << 20, 1 << 20, 0,
+                                          17 * 64, 64, 1 << 20, 1 << 20, 4096, None)
+    assert rc == -1 and _err(ogx_lib) == "empty_tokens"
+    # head_dim other than 128
+    rc = ogx_lib.ogx_attention_fwd(16, 16, 16, 1, 128, 32, 64, 0, 4096, 0.1, 16, 0, 4096, None)
+    assert rc == -1 and "head_dim" in _err(ogx_lib)
+    # GEMM K must be a multiple of 16 (TMA row pitch)
+    rc = ogx_lib.ogx_fp8_scaled_mm(16, 128, 100, 112, 16, 256, 112, 16, 16, 256, None, 0, 16, 256, None)
+    assert rc == -1 and "shape" in _err(ogx_lib)
+    # AdaZero column count outside {2048, 4096} (triton_ltx_ops.py:1005)
+    rc = ogx_lib.ogx_adazero_from_ada(16, 1, 4, 1024, 16, 1, 1024, 16, 0, 0, 0, 1024, 0, 1, 1e-6, 16, None)
+    assert rc == -1 and _err(ogx_lib) == "cols"
+    # quantiser dtype must be bf16 or f16 (triton_ltx_ops.py:1021-1022)
+    rc = ogx_lib.ogx_fp8_quantize_e4m3(16, 1, 64, 16, 0, 16, None)
+    assert rc == -1 and _err(ogx_lib) == "x_dtype"
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+
+    from opengenie_b200 import ltx_ops
+
+    x = torch.zeros((1, 4, 4096), dtype=torch.bfloat16)
+    s = torch.tensor(1.0)
+    with pytest.raises(ValueError):
+        ltx_ops.fused_fp8_quantize_e4m3(x, s)
+    table = torch.zeros((6, 4096))
+    ts = torch.zeros((1, 4, 6 * 4096), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="x_device_or_dtype"):
+        ltx_ops.fused_adazero_from_ada(x, 1e-6, table, ts, shift_index=0, scale_index=1)
+    cos = torch.zeros((1, 32, 4, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="qk_device_or_dtype"):
+        ltx_ops.fused_video_qk_rmsnorm_rope(x, x, x[0, 0], x[0, 0], 1e-6, cos, cos)

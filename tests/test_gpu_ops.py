@@ -1,0 +1,222 @@
+"""GPU parity of the HBM-bound stages (C ABI through opengenie_b200.ltx_ops) against the oracle and the
+reference's golden outputs.  Bit-exact where the reference is bitwise; <= 1 bf16 ulp where the kernel and
+the oracle share single-rounding semantics; the reference's own tolerances against its torch fallbacks."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import O, bf16_bits, codes, from_bits, status_clean, to_np, within_ulps
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def ops(ogx_lib):
+    from opengenie_b200 import ltx_ops
+
+    return ltx_ops
+
+
+def test_quantiser_bf16_all_bit_patterns_bit_exact(ops):
+    d = np.load(os.path.join(GOLD, "quant_bf16.npz"))
+    x = from_bits(np.arange(65536, dtype=np.uint32).astype(np.uint16)).reshape(256, 256)
+    for s, ref in zip(d["scales"], d["codes"]):
+        q = ops.fused_fp8_quantize_e4m3(x, torch.tensor(float(s), device="cuda"))
+        got = codes(q).reshape(-1)
+        assert np.array_equal(got, ref), f"scale {s}: {(got != ref).sum()} codes differ"
+    assert status_clean()
+
+
+def test_quantiser_f16_all_bit_patterns_bit_exact(ops):
+    d = np.load(os.path.join(GOLD, "quant_f16.npz"))
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    x = torch.from_numpy(bits.view(np.int16)).view(torch.float16).cuda().reshape(256, 256)
+    for s, ref in zip(d["scales"], d["codes"]):
+        got = codes(ops.fused_fp8_quantize_e4m3(x, torch.tensor(float(s), device="cuda"))).reshape(-1)
+        assert np.array_equal(got, ref), f"scale {s}: {(got != ref).sum()} codes differ"
+
+
+def test_quantiser_single_rounding_mode_matches_oracle(ops):
+    x = from_bits(np.arange(65536, dtype=np.uint32).astype(np.uint16)).reshape(256, 256)
+    xf = O.bf16_from_bits(np.arange(65536, dtype=np.uint32).astype(np.uint16))
+    for s in (1.0, 0.0371, 0.00123):
+        got = codes(ops.fused_fp8_quantize_e4m3(x, torch.tensor(s, device="cuda"), quant_mode=ops.QUANT_SINGLE)).reshape(-1)
+        ref = O.quantize_e4m3(xf, s, mode="single")
+        finite = ~np.isnan(xf)
+        assert np.array_equal(got[finite], ref[finite])
+
+
+@pytest.mark.parametrize("n", [0, 1, 7, 4096 * 3 + 5, 9216 * 4096])
+def test_quantiser_sizes_with_outliers_bit_exact(ops, n):
+    """C3's activation distribution: N(0,1) with 0.1% outliers x50, s = amax/448; ragged tails."""
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(n, generator=g)
+    if n:
+        idx = torch.randperm(n, generator=g)[: max(1, n // 1000)]
+        x[idx] *= 50
+    xb = x.to(torch.bfloat16)
+    s = float(xb.float().abs().amax() / 448.0) if n else 1.0
+    got = codes(ops.fused_fp8_quantize_e4m3(xb.cuda(), torch.tensor(s, device="cuda")))
+    ref = O.quantize_e4m3(xb.float().numpy(), s)
+    assert np.array_equal(got, ref)
+
+
+def test_quantiser_vs_torch_cuda_path_is_reported(ops, capsys):
+    """Informational: the reference's torch expression evaluated by torch on the GPU (where the 0-dim
+    fp32 reciprocal meets the bf16 tensor through torch's CUDA type promotion)."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(9216 * 512, generator=g).to(torch.bfloat16).cuda()
+    s = torch.tensor(0.0371, device="cuda")
+    torch_cuda = torch.clamp(x * s.reciprocal(), -448.0, 448.0).to(torch.float8_e4m3fn)
+    ours = ops.fused_fp8_quantize_e4m3(x, s)
+    differ = int((codes(torch_cuda) != codes(ours)).sum())
+    print(f"torch-on-CUDA path vs kernel (CPU torch-path semantics): {differ} of {x.numel()} codes differ")
+
+
+def _ada_case(rows, cols, table_dtype, ts_dtype, uniform, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((1, rows, cols), generator=g).to(torch.bfloat16)
+    table = (torch.randn((6, cols), generator=g) * 0.5).to(table_dtype)
+    if uniform:
+        ts = torch.randn((6 * cols,), generator=g).to(ts_dtype).view(1, 1, -1).expand(1, rows, 6 * cols)
+    else:
+        ts = torch.randn((1, rows, 6 * cols), generator=g).to(ts_dtype)
+    return x, table, ts
+
+
+@pytest.mark.parametrize("cols", [2048, 4096])
+@pytest.mark.parametrize("table_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("ts_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("uniform", [True, False])
+def test_adazero_from_ada_vs_oracle(ops, cols, table_dtype, ts_dtype, uniform):
+    x, table, ts = _ada_case(13, cols, table_dtype, ts_dtype, uniform, seed=cols)
+    ts_d = ts[:, :1].cuda().expand(ts.shape) if uniform else ts.cuda()
+    y = ops.fused_adazero_from_ada(x.cuda(), 1e-6, table.cuda(), ts_d, shift_index=0, scale_index=1)
+    ref = O.adazero_from_ada(x, 1e-6, table, ts.reshape(1, 13, 6, cols), shift_index=0, scale_index=1,
+                             table_is_bf16=table_dtype == torch.bfloat16, ts_is_bf16=ts_dtype == torch.bfloat16)
+    ok, worst = within_ulps(to_np(y), ref, ulps=1.0)
+    assert ok, worst
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_adazero_vs_reference_golden(ops, tag):
+    d = np.load(os.path.join(GOLD, "ops.npz"))
+    x = from_bits(d[f"ada_{tag}_x"])
+    tdt = torch.bfloat16 if bool(d[f"ada_{tag}_table_bf16"]) else torch.float32
+    table = torch.from_numpy(d[f"ada_{tag}_table"]).to(tdt).cuda()
+    ts = from_bits(d[f"ada_{tag}_ts"])
+    sh, sc = (int(v) for v in d[f"ada_{tag}_idx"])
+    y = ops.fused_adazero_from_ada(x, 1e-6, table, ts, shift_index=sh, scale_index=sc)
+    ref = O.bf16_from_bits(d[f"ada_{tag}_y"])
+    assert np.abs(to_np(y) - ref).max() <= 0.0625  # tests/test_triton_ltx_ops.py:92
+
+
+def test_adazero_fused_quant_equals_separate_quant(ops):
+    x, table, ts = _ada_case(37, 4096, torch.float32, torch.bfloat16, True, seed=5)
+    x, table = x.cuda(), table.cuda()
+    ts = ts[:, :1].cuda().expand(ts.shape)
+    s = torch.tensor(0.0123, device="cuda")
+    q, y = ops.fused_adazero_from_ada_fp8(x, 1e-6, table, ts, s, shift_index=0, scale_index=1, return_bf16=True)
+    y2 = ops.fused_adazero_from_ada(x, 1e-6, table, ts, shift_index=0, scale_index=1)
+    assert torch.equal(y, y2)
+    assert np.array_equal(codes(q), codes(ops.fused_fp8_quantize_e4m3(y, s)))
+    assert np.array_equal(codes(q), O.quantize_e4m3(to_np(y), 0.0123))
+    q_only = ops.fused_adazero_from_ada_fp8(x, 1e-6, table, ts, s, shift_index=0, scale_index=1)
+    assert np.array_equal(codes(q_only), codes(q))
+
+
+def test_bias_add_bitwise(ops):
+    d = np.load(os.path.join(GOLD, "ops.npz"))
+    out = ops.fused_bias_add_bf16(from_bits(d["bias_x"]), torch.from_numpy(d["bias_b"]).cuda())
+    assert np.array_equal(bf16_bits(out), d["bias_y"])
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn((33, 4096), generator=g).to(torch.bfloat16)
+    b = torch.randn((4096,), generator=g).to(torch.bfloat16)
+    out = ops.fused_bias_add_bf16(x.cuda(), b.cuda())
+    assert np.array_equal(to_np(out), O.bias_add_bf16(x, b))
+
+
+def test_residual_gate_bias_bitwise_vs_golden(ops):
+    d = np.load(os.path.join(GOLD, "ops.npz"))
+    out = ops.fused_residual_gate_bias_from_ada(
+        from_bits(d["res_x"]), from_bits(d["res_y"]), torch.from_numpy(d["res_bias"]).cuda(),
+        torch.from_numpy(d["res_table"]).cuda(), from_bits(d["res_ts"]), gate_index=8)
+    assert np.array_equal(bf16_bits(out), d["res_out"])
+
+
+@pytest.mark.parametrize("table_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("ts_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("bias_dtype", [torch.float32, torch.bfloat16])
+def test_residual_gate_bias_bitwise_vs_oracle(ops, table_dtype, ts_dtype, bias_dtype):
+    x, table, ts = _ada_case(11, 4096, table_dtype, ts_dtype, False, seed=9)
+    g = torch.Generator().manual_seed(10)
+    y = torch.randn((1, 11, 4096), generator=g).to(torch.bfloat16)
+    bias = torch.randn((4096,), generator=g).to(bias_dtype)
+    out = ops.fused_residual_gate_bias_from_ada(x.cuda(), y.cuda(), bias.cuda(), table.cuda(), ts.cuda(), gate_index=2)
+    ref = O.residual_gate_bias_from_ada(x, y, bias, table, ts.reshape(1, 11, 6, 4096), gate_index=2,
+                                        table_is_bf16=table_dtype == torch.bfloat16, ts_is_bf16=ts_dtype == torch.bfloat16)
+    assert np.array_equal(to_np(out), ref)
+
+
+def _rope_case(tokens, seed, cs_dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn((1, tokens, 4096), generator=g).to(torch.bfloat16)
+    k = torch.randn((1, tokens, 4096), generator=g).to(torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn((4096,), generator=g)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn((4096,), generator=g)).to(torch.bfloat16)
+    f = torch.randn((1, 32, tokens, 64), generator=g)
+    return q, k, qw, kw, f.cos().to(cs_dtype), f.sin().to(cs_dtype)
+
+
+@pytest.mark.parametrize("tokens", [1, 17, 300])
+@pytest.mark.parametrize("cs_dtype", [torch.bfloat16, torch.float32])
+def test_qk_rmsnorm_rope_vs_oracle(ops, tokens, cs_dtype):
+    q, k, qw, kw, cos, sin = _rope_case(tokens, tokens, cs_dtype)
+    oq, ok_ = ops.fused_video_qk_rmsnorm_rope(q.cuda(), k.cuda(), qw.cuda(), kw.cuda(), 1e-6, cos.cuda(), sin.cuda())
+    for got, x, w in ((oq, q, qw), (ok_, k, kw)):
+        ref = O.qk_rmsnorm_rope(x, w, 1e-6, cos, sin)
+        ok, worst = within_ulps(to_np(got), ref, ulps=1.0, atol=1e-6)
+        assert ok, worst
+
+
+def test_qk_rmsnorm_rope_vs_reference_golden(ops):
+    d = np.load(os.path.join(GOLD, "ops.npz"))
+    x = from_bits(d["rope_x"])
+    w = from_bits(d["rope_w"])
+    out, _ = ops.fused_video_qk_rmsnorm_rope(x, x, w, w, 1e-6, from_bits(d["rope_cos"]), from_bits(d["rope_sin"]))
+    assert np.abs(to_np(out) - O.bf16_from_bits(d["rope_out"])).max() <= 0.125  # tests/test_triton_ltx_ops.py:228
+
+
+def test_qk_rmsnorm_rope_in_place_on_packed_rows(ops):
+    q, k, qw, kw, cos, sin = _rope_case(40, 4)
+    packed = torch.cat([q, k, torch.zeros_like(q)], dim=-1).cuda()  # [1, L, 3*4096]
+    pq, pk = packed[..., :4096], packed[..., 4096:8192]
+    ops.fused_video_qk_rmsnorm_rope(pq, pk, qw.cuda(), kw.cuda(), 1e-6, cos.cuda(), sin.cuda(), out=(pq, pk))
+    assert np.array_equal(to_np(pq), to_np(ops.fused_video_qk_rmsnorm_rope(q.cuda(), k.cuda(), qw.cuda(), kw.cuda(),
+                                                                          1e-6, cos.cuda(), sin.cuda())[0]))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_qkv_rope_scatter_layout(ops, world):
+    """Sequence-to-head send layout [dst][L][3][H/P][128] written directly by the RoPE kernel."""
+    from opengenie_b200 import _lib
+    from opengenie_b200.ltx_ops import _stream
+
+    q, k, qw, kw, cos, sin = _rope_case(24, 7)
+    v = torch.randn((1, 24, 4096), generator=torch.Generator().manual_seed(8)).to(torch.bfloat16)
+    q, k, v, qw, kw, cos, sin = (t.cuda() for t in (q, k, v, qw, kw, cos, sin))
+    hpg = 32 // world
+    send = torch.empty((world, 24, 3, hpg, 128), device="cuda", dtype=torch.bfloat16)
+    _lib.call("ogx_video_qkv_rmsnorm_rope_scatter", q.data_ptr(), k.data_ptr(), v.data_ptr(), 24, 4096,
+              qw.data_ptr(), kw.data_ptr(), 0, 1e-6, cos.data_ptr(), sin.data_ptr(), 0, cos.stride(1), cos.stride(2),
+              send[:, :, 0].data_ptr(), send[:, :, 1].data_ptr(), send[:, :, 2].data_ptr(),
+              send.stride(1), send.stride(0), hpg, _stream(q))
+    rq, rk = ops.fused_video_qk_rmsnorm_rope(q, k, qw, kw, 1e-6, cos, sin)
+    for j, ref in enumerate((rq, rk, v)):
+        got = send[:, :, j].permute(1, 0, 2, 3).reshape(1, 24, 4096)
+        assert torch.equal(got, ref)
+    assert status_clean()
