@@ -76,10 +76,9 @@ __device__ __forceinline__ void ada_values8(const TableT* table_row, const TsT* 
 }
 
 // ----------------------------------------------------------------- E4M3
-// Round-to-nearest-even fp32 -> e4m3fn with saturation to +-448; NaN -> 0x7F
-// (the code torch produces for any NaN input).
+// Round-to-nearest-even fp32 -> e4m3fn with saturation to +-448 (finite
+// inputs; NaN is handled by the caller).
 __device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
-  if (v != v) return 0x7F;
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
 }
 
@@ -104,15 +103,22 @@ __device__ __forceinline__ float round_to<__half>(float v) {
   return __half2float(__float2half_rn(v));
 }
 
+// NaN inputs: torch's vectorised fp32->bf16 cast returns 0xFFFF for every
+// NaN, so the bf16 torch path quantises any NaN to 0xFF; fp16 (and the
+// single-rounding path) keep the NaN's sign: 0x7F | sign.
 template <typename InT, int MODE>
 __device__ __forceinline__ uint8_t quant_one(float x, float s, float r) {
+  if (x != x) {
+    if (MODE == kQuantTorch && std::is_same<InT, __nv_bfloat16>::value) return 0xFF;
+    return static_cast<uint8_t>(0x7F | ((__float_as_uint(x) >> 24) & 0x80));
+  }
   float t;
   if (MODE == kQuantTorch) {
     t = round_to<InT>(__fmul_rn(x, r));
   } else {
     t = __fdiv_rn(x, s);
   }
-  // clamp with NaN passing through (torch.clamp propagates NaN)
+  // t is not NaN here (NaN inputs returned above); inf saturates like torch.clamp
   t = (t < -448.0f) ? -448.0f : ((t > 448.0f) ? 448.0f : t);
   return f32_to_e4m3(t);
 }
@@ -229,6 +235,7 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(const InT* __restrict
     float f[8];
     if (std::is_same<InT, __nv_bfloat16>::value) {
       unpack8(raw, f);
+      reinterpret_cast<uint2*>(q)[v] = quant8<InT, MODE>(f, s, r);
     } else {
       const __half2* h = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
@@ -237,19 +244,36 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(const InT* __restrict
         f[2 * i] = p.x;
         f[2 * i + 1] = p.y;
       }
+      uint2 codes = quant8<InT, MODE>(f, s, r);
+      // half -> float conversion canonicalises NaN; restore each NaN's sign from the raw bits
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      uint32_t* c = reinterpret_cast<uint32_t*>(&codes);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t hb = (w[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+        if ((hb & 0x7C00u) == 0x7C00u && (hb & 0x03FFu) != 0u) {
+          const uint32_t code = 0x7Fu | ((hb >> 8) & 0x80u);
+          const int word = i >> 2, sh = 8 * (i & 3);
+          c[word] = (c[word] & ~(0xFFu << sh)) | (code << sh);
+        }
+      }
+      reinterpret_cast<uint2*>(q)[v] = codes;
     }
-    reinterpret_cast<uint2*>(q)[v] = quant8<InT, MODE>(f, s, r);
   }
   // ragged tail (n % 8), handled by the first threads of block 0
   if (blockIdx.x == 0) {
     const int64_t tail0 = nvec << 3;
     for (int64_t i = tail0 + threadIdx.x; i < n; i += blockDim.x) {
       float f;
-      if (std::is_same<InT, __nv_bfloat16>::value)
+      if (std::is_same<InT, __nv_bfloat16>::value) {
         f = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
-      else
+        q[i] = quant_one<InT, MODE>(f, s, r);
+      } else {
+        const uint32_t hb = reinterpret_cast<const uint16_t*>(x)[i];
         f = __half2float(reinterpret_cast<const __half*>(x)[i]);
-      q[i] = quant_one<InT, MODE>(f, s, r);
+        q[i] = ((hb & 0x7C00u) == 0x7C00u && (hb & 0x03FFu) != 0u) ? static_cast<uint8_t>(0x7Fu | ((hb >> 8) & 0x80u))
+                                                                  : quant_one<InT, MODE>(f, s, r);
+      }
     }
   }
 }

@@ -12,6 +12,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "../../include/ogx.h"
 #include "elementwise.cuh"
@@ -73,18 +74,20 @@ int make_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* bas
   return OGX_OK;
 }
 
-// Raise the dynamic shared-memory limit of a kernel once per device.
+// Raise the dynamic shared-memory limit of a kernel once per (kernel, device).
 template <typename K>
 int ensure_smem(K kernel, int bytes) {
   static std::mutex mu;
-  static uint64_t done_mask = 0;  // one bit per device
+  static std::unordered_map<const void*, uint64_t> done;  // kernel -> one bit per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(OGX_ECUDA, "cudaGetDevice failed");
+  const void* key = reinterpret_cast<const void*>(kernel);
   std::lock_guard<std::mutex> lock(mu);
-  if (dev < 64 && (done_mask >> dev) & 1u) return OGX_OK;
+  uint64_t& mask = done[key];
+  if (dev < 64 && (mask >> dev) & 1u) return OGX_OK;
   int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                       "cudaFuncSetAttribute");
-  if (rc == OGX_OK && dev < 64) done_mask |= (uint64_t{1} << dev);
+  if (rc == OGX_OK && dev < 64) mask |= (uint64_t{1} << dev);
   return rc;
 }
 
@@ -225,11 +228,11 @@ int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int6
 
 int ogx_fp8_quantize_e4m3(const void* x, int x_dtype, int64_t n, const float* input_scale, int quant_mode, void* q,
                           void* stream) {
-  if (x == nullptr || q == nullptr || input_scale == nullptr) return fail(OGX_EINVAL, "null_pointer");
   if (x_dtype != OGX_DTYPE_BF16 && x_dtype != OGX_DTYPE_F16) return fail(OGX_EINVAL, "x_dtype");
   if (quant_mode != OGX_QUANT_TORCH && quant_mode != OGX_QUANT_SINGLE) return fail(OGX_EINVAL, "quant_mode");
   if (n < 0) return fail(OGX_EINVAL, "numel");
   if (n == 0) return OGX_OK;
+  if (x == nullptr || q == nullptr || input_scale == nullptr) return fail(OGX_EINVAL, "null_pointer");
   if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail(OGX_EINVAL, "alignment");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = grid_for((n >> 3) > 0 ? (n >> 3) : 1);

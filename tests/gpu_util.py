@@ -32,11 +32,13 @@ def within_ulps(got: np.ndarray, ref: np.ndarray, ulps: float = 1.0, atol: float
     return bool((d <= bound).all()), float((d / bound).max())
 
 
-def block_tolerance(got: np.ndarray, ref: np.ndarray, *, atol: float = 2e-2, mean_rel: float = 1e-2) -> dict:
-    """The north-star tolerance: max-abs <= 2e-2 (plus one bf16 ulp of |ref|, the rounding of a
-    bf16 output alone) and sum|d| / sum|ref| <= 1e-2.  Returns the measured figures."""
+def block_tolerance(got: np.ndarray, ref: np.ndarray, *, atol: float = 2e-2, mean_rel: float = 1e-2,
+                    ulps: float = 1.0) -> dict:
+    """The north-star tolerance: max-abs <= 2e-2 plus ``ulps`` bf16 ulps of |ref| (a bf16 output's own
+    rounding is half an ulp, which exceeds 2e-2 once |out| >= 8) and sum|d| / sum|ref| <= 1e-2.
+    Returns the measured figures."""
     d = np.abs(np.asarray(got, np.float64) - np.asarray(ref, np.float64))
-    excess = d - (atol + np.abs(ref) * 2.0 ** -7)
+    excess = d - (atol + ulps * np.abs(ref) * 2.0 ** -7)
     ref_formula = float((d / np.maximum(np.abs(ref), 1e-6)).mean())  # the reference's own mean_rel
     return {
         "max_abs": float(d.max()),
@@ -45,6 +47,70 @@ def block_tolerance(got: np.ndarray, ref: np.ndarray, *, atol: float = 2e-2, mea
         "ref_mean_rel": ref_formula,
         "ok": bool(excess.max() <= 0 and d.sum() / max(np.abs(ref).sum(), 1e-30) <= mean_rel),
     }
+
+
+def reference_gpu_path_block(x, ts_view, cos, sin, w, *, eps=1e-6, heads=32):
+    """The reference's production GPU path for the block, rebuilt from torch's own GPU kernels:
+    single-rounding AdaZero / quantiser / RoPE (its Triton kernels, ltx_serve/triton_ltx_ops.py:3359-3444,
+    :3901-3978), torch._scaled_mm with use_fast_accum (:1695-1703) + bias add, SDPA on bf16 with the
+    cuDNN backend ('sdpa-cudnn', modal_apps/ltx23_live_h100_worker.py:49), the residual rounding of :3663-3721.
+    Used to put the fused block's deviation from the fp32 reference next to the reference's own."""
+    import torch.nn.functional as F
+
+    def r16(t):
+        return t.to(torch.bfloat16)
+
+    table = w.scale_shift_table.float()
+    if (w.scale_shift_table.dtype == torch.bfloat16) != (ts_view.dtype == torch.bfloat16):
+        table = r16(table).float()
+    ts = ts_view.float()
+
+    def ada(i):
+        v = table[i].view(1, 1, -1) + ts[:, :, i, :]
+        return r16(v).float() if ts_view.dtype == torch.bfloat16 else v
+
+    def quant(t, s):
+        return torch.clamp(t.float() / s.float(), -448.0, 448.0).to(torch.float8_e4m3fn)
+
+    xf = x.float()
+    norm = r16(xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1 + ada(1)) + ada(0))
+
+    def lin(q2, s_in, l, bias=True):
+        y = torch._scaled_mm(q2.reshape(-1, q2.shape[-1]), l.weight.t(), scale_a=s_in, scale_b=l.weight_scale,
+                             out_dtype=torch.bfloat16, use_fast_accum=True)
+        if bias:
+            y = r16(y.float() + r16(l.bias).float())
+        return y.view(1, -1, y.shape[-1])
+
+    q = lin(quant(norm, w.to_q.input_scale), w.to_q.input_scale, w.to_q)
+    k = lin(quant(norm, w.to_k.input_scale), w.to_k.input_scale, w.to_k)
+    v = lin(quant(norm, w.to_v.input_scale), w.to_v.input_scale, w.to_v)
+
+    def rope(t, weight):
+        tf = t.float()
+        n = tf * torch.rsqrt(tf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()
+        B, L, D = n.shape
+        nh = n.view(B, L, heads, D // heads).transpose(1, 2)
+        half = D // heads // 2
+        c, s_ = cos.float(), sin.float()
+        f, sd = nh[..., :half], nh[..., half:]
+        return r16(torch.cat([f * c - sd * s_, sd * c + f * s_], dim=-1).transpose(1, 2).reshape(B, L, D))
+
+    qr, kr = rope(q, w.q_norm_weight), rope(k, w.k_norm_weight)
+    B, L, D = qr.shape
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    qh, kh, vh = (t.view(B, L, heads, D // heads).transpose(1, 2) for t in (qr, kr, v))
+    try:
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            o = F.scaled_dot_product_attention(qh, kh, vh)
+    except RuntimeError:
+        o = F.scaled_dot_product_attention(qh, kh, vh)
+    attn = o.transpose(1, 2).reshape(B, L, D)
+    y = lin(quant(attn, w.to_out.input_scale), w.to_out.input_scale, w.to_out, bias=False)
+    yb = r16(y.float() + r16(w.to_out.bias).float())
+    gate = ada(2)
+    return r16(xf + r16(yb.float() * gate).float())
 
 
 def status_clean():

@@ -98,7 +98,9 @@ def test_adazero_from_ada_vs_oracle(ops, cols, table_dtype, ts_dtype, uniform):
     y = ops.fused_adazero_from_ada(x.cuda(), 1e-6, table.cuda(), ts_d, shift_index=0, scale_index=1)
     ref = O.adazero_from_ada(x, 1e-6, table, ts.reshape(1, 13, 6, cols), shift_index=0, scale_index=1,
                              table_is_bf16=table_dtype == torch.bfloat16, ts_is_bf16=ts_dtype == torch.bfloat16)
-    ok, worst = within_ulps(to_np(y), ref, ulps=1.0)
+    # fp32 arithmetic (as the reference's kernel) vs exact: 1 ulp, plus 1e-5 absolute where
+    # shift nearly cancels x*inv_rms*(1+scale)
+    ok, worst = within_ulps(to_np(y), ref, ulps=1.0, atol=1e-5)
     assert ok, worst
 
 
