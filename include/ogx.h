@@ -138,6 +138,20 @@ int ogx_fp8_scaled_mm_residual_gate(const void* a, int64_t M, int64_t K, int64_t
                                     const void* timestep, int timestep_dtype, int64_t ts_stride_t,
                                     int64_t ts_stride_p, int gate_index, void* out, int64_t ldo, void* stream);
 
+/* The same fused out-projection with A read from the receive buffer of the
+ * head-to-sequence exchange: A is K / k_block blocks of [M, k_block] e4m3
+ * (block s = the columns [s*k_block, (s+1)*k_block) sent by rank s), so no
+ * permute runs between the exchange and the GEMM.  k_block % 128 == 0.
+ * No reference counterpart for the layout (the reference is single-GPU); the
+ * arithmetic is that of ogx_fp8_scaled_mm_residual_gate. */
+int ogx_fp8_scaled_mm_residual_gate_kblocked(const void* a, int64_t M, int64_t K, int64_t k_block, const void* w,
+                                             int64_t N, int64_t ldw, const float* scale_a, const float* scale_b,
+                                             int64_t n_per_scale, const void* bias, int bias_dtype, const void* x,
+                                             int64_t ldx, const void* table, int table_dtype,
+                                             int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                                             int64_t ts_stride_t, int64_t ts_stride_p, int gate_index, void* out,
+                                             int64_t ldo, void* stream);
+
 /* Dense bidirectional attention (tcgen05 + TMEM, online softmax), head_dim 128:
  *   out[b, t, h, :] = softmax(q[b,t,h,:] . k[b,:,h,:]^T * softmax_scale) v[b,:,h,:]
  * q/k/v: bf16, element (b, t, h, d) at ptr + b*stride_b + t*stride_t + h*128 + d

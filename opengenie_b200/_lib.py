@@ -55,6 +55,11 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p, c_int, c_int64, c_int64,
         c_int, c_void_p, c_int64, c_void_p,
     ],
+    "ogx_fp8_scaled_mm_residual_gate_kblocked": [
+        c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
+        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p, c_int, c_int64, c_int64,
+        c_int, c_void_p, c_int64, c_void_p,
+    ],
     "ogx_attention_fwd": [
         c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_float,
         c_void_p, c_int64, c_int64, c_void_p,

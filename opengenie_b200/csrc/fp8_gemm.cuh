@@ -40,6 +40,11 @@ enum Epilogue : int { EPI_BIAS = 0, EPI_RESIDUAL = 1 };
 
 struct Params {
   int M, N, K;
+  // 0: A is a plain [M, K] map.  > 0: A is stored as K / a_k_block blocks of
+  // [M, a_k_block] (the receive buffer of the head-to-sequence exchange:
+  // block s holds the columns of source rank s), read through a 3-D map
+  // {a_k_block, M, K / a_k_block}; a_k_block is a multiple of BK.
+  int a_k_block;
   const float* scale_a;  // device scalar
   const float* scale_b;  // device array, one entry per n_per_scale columns
   int n_per_scale;
@@ -135,7 +140,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem_aligned + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_STAGE_BYTES;
           mbar_arrive_expect_tx(&st.full[stage], STAGE_BYTES);
-          tma_load_2d(sa, &tmap_a, &st.full[stage], kb * BK, m0);
+          if (p.a_k_block > 0)
+            tma_load_3d(sa, &tmap_a, &st.full[stage], (kb * BK) % p.a_k_block, m0, (kb * BK) / p.a_k_block);
+          else
+            tma_load_2d(sa, &tmap_a, &st.full[stage], kb * BK, m0);
           tma_load_2d(sb, &tmap_b, &st.full[stage], kb * BK, n0);
           ++issued;
           if (++stage == STAGES) {

@@ -389,19 +389,30 @@ int ogx_video_qk_rmsnorm_rope(const void* q, const void* k, int64_t tokens, int6
 namespace {
 
 int gemm_common(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
-                const float* scale_a, const float* scale_b, int64_t n_per_scale, CUtensorMap* ma, CUtensorMap* mb) {
+                const float* scale_a, const float* scale_b, int64_t n_per_scale, CUtensorMap* ma, CUtensorMap* mb,
+                int64_t a_k_block = 0) {
   if (a == nullptr || w == nullptr || scale_a == nullptr || scale_b == nullptr) return fail(OGX_EINVAL, "null_pointer");
   if (M < 0 || N <= 0 || K <= 0) return fail(OGX_EINVAL, "shape");
   if (K % 16 || N % 32) return fail(OGX_EINVAL, "shape: K % 16 and N % 32 must be 0");
-  if (lda < K || ldw < K || lda % 16 || ldw % 16) return fail(OGX_EINVAL, "leading_dimension");
+  if ((a_k_block == 0 && lda < K) || ldw < K || lda % 16 || ldw % 16) return fail(OGX_EINVAL, "leading_dimension");
   if (n_per_scale <= 0 || n_per_scale % 32) return fail(OGX_EINVAL, "n_per_scale");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(OGX_EINVAL, "shape");
   if (!aligned16(a) || !aligned16(w)) return fail(OGX_EINVAL, "alignment");
   if (M == 0) return OGX_OK;
-  const uint64_t da[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
-  const uint64_t sa[1] = {static_cast<uint64_t>(lda)};
-  const uint32_t ba[2] = {static_cast<uint32_t>(ogx::gemm::BK), static_cast<uint32_t>(ogx::gemm::BM)};
-  int rc = make_map(ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa, ba);
+  int rc;
+  if (a_k_block > 0) {
+    if (a_k_block % ogx::gemm::BK || K % a_k_block) return fail(OGX_EINVAL, "a_k_block");
+    const uint64_t da[3] = {static_cast<uint64_t>(a_k_block), static_cast<uint64_t>(M),
+                            static_cast<uint64_t>(K / a_k_block)};
+    const uint64_t sa[2] = {static_cast<uint64_t>(a_k_block), static_cast<uint64_t>(a_k_block * M)};
+    const uint32_t ba[3] = {static_cast<uint32_t>(ogx::gemm::BK), static_cast<uint32_t>(ogx::gemm::BM), 1};
+    rc = make_map(ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a, da, sa, ba);
+  } else {
+    const uint64_t da[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t sa[1] = {static_cast<uint64_t>(lda)};
+    const uint32_t ba[2] = {static_cast<uint32_t>(ogx::gemm::BK), static_cast<uint32_t>(ogx::gemm::BM)};
+    rc = make_map(ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa, ba);
+  }
   if (rc) return rc;
   const uint64_t db[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
   const uint64_t sb[1] = {static_cast<uint64_t>(ldw)};
@@ -478,14 +489,14 @@ int ogx_fp8_scaled_mm(const void* a, int64_t M, int64_t K, int64_t lda, const vo
   return gemm_launch<ogx::gemm::EPI_BIAS>(ma, mb, p, static_cast<cudaStream_t>(stream));
 }
 
-int ogx_fp8_scaled_mm_residual_gate(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
+static int residual_gate_impl(int64_t a_k_block, const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
                                     int64_t ldw, const float* scale_a, const float* scale_b, int64_t n_per_scale,
                                     const void* bias, int bias_dtype, const void* x, int64_t ldx,
                                     const void* table, int table_dtype, int64_t table_stride_row,
                                     const void* timestep, int timestep_dtype, int64_t ts_stride_t,
                                     int64_t ts_stride_p, int gate_index, void* out, int64_t ldo, void* stream) {
   CUtensorMap ma, mb;
-  int rc = gemm_common(a, M, K, lda, w, N, ldw, scale_a, scale_b, n_per_scale, &ma, &mb);
+  int rc = gemm_common(a, M, K, lda, w, N, ldw, scale_a, scale_b, n_per_scale, &ma, &mb, a_k_block);
   if (rc || M == 0) return rc;
   if (out == nullptr || !aligned16(out) || ldo % 8 || ldo < N) return fail(OGX_EINVAL, "output");
   if (bias != nullptr && (!dtype_ok(bias_dtype) || !aligned16(bias))) return fail(OGX_EINVAL, "bias");
@@ -517,7 +528,32 @@ int ogx_fp8_scaled_mm_residual_gate(const void* a, int64_t M, int64_t K, int64_t
   p.ts_stride_t = ts_stride_t;
   p.ts_stride_p = ts_stride_p;
   p.gate_index = gate_index;
+  p.a_k_block = static_cast<int>(a_k_block);
   return gemm_launch<ogx::gemm::EPI_RESIDUAL>(ma, mb, p, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_fp8_scaled_mm_residual_gate(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
+                                    int64_t ldw, const float* scale_a, const float* scale_b, int64_t n_per_scale,
+                                    const void* bias, int bias_dtype, const void* x, int64_t ldx,
+                                    const void* table, int table_dtype, int64_t table_stride_row,
+                                    const void* timestep, int timestep_dtype, int64_t ts_stride_t,
+                                    int64_t ts_stride_p, int gate_index, void* out, int64_t ldo, void* stream) {
+  return residual_gate_impl(0, a, M, K, lda, w, N, ldw, scale_a, scale_b, n_per_scale, bias, bias_dtype, x, ldx, table,
+                            table_dtype, table_stride_row, timestep, timestep_dtype, ts_stride_t, ts_stride_p,
+                            gate_index, out, ldo, stream);
+}
+
+int ogx_fp8_scaled_mm_residual_gate_kblocked(const void* a, int64_t M, int64_t K, int64_t k_block, const void* w,
+                                             int64_t N, int64_t ldw, const float* scale_a, const float* scale_b,
+                                             int64_t n_per_scale, const void* bias, int bias_dtype, const void* x,
+                                             int64_t ldx, const void* table, int table_dtype,
+                                             int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                                             int64_t ts_stride_t, int64_t ts_stride_p, int gate_index, void* out,
+                                             int64_t ldo, void* stream) {
+  if (k_block <= 0) return fail(OGX_EINVAL, "a_k_block");
+  return residual_gate_impl(k_block, a, M, K, k_block, w, N, ldw, scale_a, scale_b, n_per_scale, bias, bias_dtype, x,
+                            ldx, table, table_dtype, table_stride_row, timestep, timestep_dtype, ts_stride_t,
+                            ts_stride_p, gate_index, out, ldo, stream);
 }
 
 int ogx_attention_fwd(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens, int64_t heads,

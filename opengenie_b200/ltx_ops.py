@@ -318,6 +318,8 @@ def fp8_scaled_mm(
     out_dtype=bf16, use_fast_accum=True)`` followed by the bias add of
     FP8Linear.forward (ltx_serve/triton_ltx_ops.py:1695-1707).  ``scale_b`` may
     hold one scale per ``n_per_scale`` output columns (packed Q/K/V weights).
+    A caller-provided ``out`` ([M, N], any row stride) is returned as given; otherwise the
+    result has qinput's leading shape.
     """
     _require_cuda(qinput, weight, scale_a, scale_b)
     if qinput.dtype != torch.float8_e4m3fn or weight.dtype != torch.float8_e4m3fn:
@@ -332,8 +334,11 @@ def fp8_scaled_mm(
     nps = n_per_scale if n_per_scale is not None else N // scale_b.numel()
     if nps * scale_b.numel() != N:
         raise ValueError("scale")
+    given = out is not None
     if out is None:
         out = torch.empty((M, N), device=qinput.device, dtype=torch.bfloat16)
+    if out.dtype != torch.bfloat16 or out.ndim != 2 or out.shape != (M, N) or out.stride(1) != 1:
+        raise ValueError("out_shape: out must be a [M, N] bf16 matrix with unit column stride")
     if bias is not None and (bias.ndim != 1 or bias.shape[0] != N):
         raise ValueError("bias_shape")
     _lib.call(
@@ -343,7 +348,7 @@ def fp8_scaled_mm(
         _ptr(bias.contiguous()) if bias is not None else None, _code(bias) if bias is not None else DTYPE_BF16,
         out.data_ptr(), out.stride(0), _stream(qinput),
     )
-    return out.reshape(*qinput.shape[:-1], N)
+    return out if given else out.reshape(*qinput.shape[:-1], N)
 
 
 def fp8_linear_from_quantized_e4m3(linear, qinput: torch.Tensor, *, out_dtype: torch.dtype) -> torch.Tensor:

@@ -1,0 +1,220 @@
+"""Ulysses sequence parallelism for the video self-attention block on one 8xB200 box.
+
+One process per GPU.  Rank r owns tokens [r*L/P, (r+1)*L/P) for every
+sequence-local stage (AdaZero + quantiser, Q/K/V GEMM, Q/K RMSNorm + RoPE,
+out-projection + gated residual: RMSNorm spans all 32 heads, so it must run
+before the exchange).  Around attention two all-to-alls over NVLink (NCCL) swap
+the sharding:
+
+  exchange 1 (sequence -> heads): the RoPE kernel writes Q/K/V straight into the
+      send buffer [P dst][L/P][3][H/P][128]; the receive buffer
+      [P src][L/P][3][H/P][128] is [L][3][H/P][128] in token order and feeds the
+      attention kernel as strided q/k/v rows.
+  exchange 2 (heads -> sequence): attention writes its e4m3-quantised output
+      [L][H/P*128] (= [P dst][L/P][H/P*128]); the receive buffer
+      [P src][L/P][H/P*128] is read by the out-projection GEMM through a 3-D
+      tensor map (k-blocked A operand), so no permute runs.
+
+The per-tensor activation scales are static, so quantising before exchange 2 is
+exact and halves its bytes.  The reference is single-GPU (no collective anywhere);
+this module is the multi-GPU extension the block needs at 2/4/8 GPUs.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib, ltx_ops
+from ._lib import DTYPE_BF16
+from .synthetic import FP8_MAX, BlockWeights
+from .video_block import VideoSelfAttentionBlock
+
+
+class UlyssesPlan:
+    """Token partition, buffer shapes and the two exchanges (host logic; no kernels)."""
+
+    def __init__(self, world: int, rank: int, *, heads: int = 32, head_dim: int = 128, group=None):
+        if heads % world:
+            raise ValueError(f"{heads} heads do not split over {world} ranks")
+        self.world, self.rank, self.heads, self.head_dim, self.group = world, rank, heads, head_dim, group
+        self.heads_local = heads // world
+
+    def tokens_local(self, tokens: int) -> int:
+        if tokens % self.world:
+            raise ValueError(f"{tokens} tokens do not split over {self.world} ranks")
+        return tokens // self.world
+
+    def token_range(self, tokens: int) -> tuple[int, int]:
+        n = self.tokens_local(tokens)
+        return self.rank * n, (self.rank + 1) * n
+
+    def qkv_send_shape(self, tokens_local: int) -> tuple[int, ...]:
+        return (self.world, tokens_local, 3, self.heads_local, self.head_dim)
+
+    def out_send_shape(self, tokens_local: int) -> tuple[int, ...]:
+        return (self.world, tokens_local, self.heads_local * self.head_dim)
+
+    def _all_to_all(self, recv: torch.Tensor, send: torch.Tensor) -> None:
+        dist.all_to_all_single(recv.view(torch.uint8), send.view(torch.uint8), group=self.group)
+
+    def exchange_qkv(self, send: torch.Tensor, recv: torch.Tensor) -> None:
+        """Sequence -> heads: send [P dst][L/P][3][H/P][d] -> recv [P src][L/P][3][H/P][d]."""
+        self._all_to_all(recv, send)
+
+    def exchange_out(self, send: torch.Tensor, recv: torch.Tensor) -> None:
+        """Heads -> sequence: send [P dst][L/P][H/P*d] -> recv [P src][L/P][H/P*d]."""
+        self._all_to_all(recv, send)
+
+    def attention_views(self, recv: torch.Tensor, tokens: int):
+        """q/k/v [1, L, H/P*d] views of the receive buffer (token rows strided by 3*H/P*d)."""
+        flat = recv.reshape(1, tokens, 3 * self.heads_local * self.head_dim)
+        w = self.heads_local * self.head_dim
+        return flat[..., :w], flat[..., w:2 * w], flat[..., 2 * w:]
+
+
+class UlyssesVideoSelfAttention:
+    """The video self-attention block sharded over the ranks of ``group`` (one GPU each)."""
+
+    kernel_launches_per_step = 5  # adazero+quant, QKV GEMM, RoPE scatter, attention, out-proj GEMM
+
+    def __init__(self, weights: BlockWeights, device, group=None):
+        self.group = group
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        self.plan = UlyssesPlan(world, rank, group=group)
+        self.blk = VideoSelfAttentionBlock(weights, device)
+        self.w = self.blk.w
+        self.device = self.blk.device
+        self._ws: dict[int, dict[str, torch.Tensor]] = {}
+
+    # ------------------------------------------------------------------ buffers
+    def workspace(self, tokens_local: int) -> dict[str, torch.Tensor]:
+        ws = self._ws.get(tokens_local)
+        if ws is None:
+            p = self.plan
+            L = tokens_local * p.world
+            ws = {
+                "qkv": torch.empty((tokens_local, 3 * 4096), device=self.device, dtype=torch.bfloat16),
+                "send1": torch.empty(p.qkv_send_shape(tokens_local), device=self.device, dtype=torch.bfloat16),
+                "recv1": torch.empty(p.qkv_send_shape(tokens_local), device=self.device, dtype=torch.bfloat16),
+                "send2": torch.empty((L, p.heads_local * p.head_dim), device=self.device, dtype=torch.float8_e4m3fn),
+                "recv2": torch.empty(p.out_send_shape(tokens_local), device=self.device, dtype=torch.float8_e4m3fn),
+            }
+            self._ws[tokens_local] = ws
+        return ws
+
+    def local_slice(self, t: torch.Tensor) -> torch.Tensor:
+        t0, t1 = self.plan.token_range(t.shape[1])
+        return t[:, t0:t1]
+
+    # ------------------------------------------------------------------ stages
+    def _qkv_and_exchange(self, x_loc, ts_loc, cos_loc, sin_loc, ws):
+        w = self.w
+        p = self.plan
+        Ll = x_loc.shape[1]
+        xq = ltx_ops.fused_adazero_from_ada_fp8(x_loc, w.norm_eps, w.scale_shift_table, ts_loc, w.to_q.input_scale,
+                                                shift_index=0, scale_index=1)
+        qkv = ws["qkv"]
+        if qkv.shape != (Ll, 3 * 4096) or not qkv.is_contiguous():
+            raise ValueError("qkv workspace shape")
+        ltx_ops.fp8_scaled_mm(xq, self.blk.w_qkv, w.to_q.input_scale, self.blk.s_qkv, bias=self.blk.b_qkv, out=qkv,
+                              n_per_scale=4096)
+        send = ws["send1"]
+        D = 4096
+        if cos_loc.shape[2] != Ll or sin_loc.shape != cos_loc.shape or send.shape != p.qkv_send_shape(Ll):
+            raise ValueError("rope_shape")
+        _lib.call(
+            "ogx_video_qkv_rmsnorm_rope_scatter",
+            qkv.data_ptr(), qkv[:, D:].data_ptr(), qkv[:, 2 * D:].data_ptr(), Ll, qkv.stride(0),
+            w.q_norm_weight.data_ptr(), w.k_norm_weight.data_ptr(), ltx_ops._code(w.q_norm_weight), float(w.qk_eps),
+            cos_loc.data_ptr(), sin_loc.data_ptr(), ltx_ops._code(cos_loc), cos_loc.stride(1), cos_loc.stride(2),
+            send[:, :, 0].data_ptr(), send[:, :, 1].data_ptr(), send[:, :, 2].data_ptr(), send.stride(1),
+            send.stride(0), p.heads_local, ltx_ops._stream(qkv),
+        )
+        p.exchange_qkv(send, ws["recv1"])
+        return p.attention_views(ws["recv1"], Ll * p.world)
+
+    def forward_local(self, x_loc: torch.Tensor, timestep: torch.Tensor, pe: tuple[torch.Tensor, torch.Tensor]):
+        """x_loc: this rank's tokens [1, L/P, 4096]; timestep and pe span all L tokens."""
+        p = self.plan
+        w = self.w
+        Ll = x_loc.shape[1]
+        L = Ll * p.world
+        t0 = p.rank * Ll
+        ts_loc = timestep[:, t0:t0 + Ll]
+        cos_loc = pe[0][:, :, t0:t0 + Ll]
+        sin_loc = pe[1][:, :, t0:t0 + Ll]
+        ws = self.workspace(Ll)
+        q, k, v = self._qkv_and_exchange(x_loc, ts_loc, cos_loc, sin_loc, ws)
+        send2 = ws["send2"]
+        ltx_ops.attention(q, k, v, p.heads_local, out=send2.view(1, L, -1), out_e4m3_scale=w.to_out.input_scale)
+        p.exchange_out(send2, ws["recv2"])
+        out = torch.empty_like(x_loc)
+        ts_view = ltx_ops._ts_view(x_loc, w.scale_shift_table, ts_loc)
+        recv2 = ws["recv2"]
+        if recv2.shape != p.out_send_shape(Ll) or ts_view.shape[1] != Ll or x_loc.shape != out.shape:
+            raise ValueError("out_projection_shape")
+        _lib.call(
+            "ogx_fp8_scaled_mm_residual_gate_kblocked",
+            recv2.data_ptr(), Ll, 4096, p.heads_local * p.head_dim, w.to_out.weight.data_ptr(), 4096,
+            w.to_out.weight.stride(0), w.to_out.input_scale.data_ptr(), w.to_out.weight_scale.data_ptr(), 4096,
+            w.to_out.bias.data_ptr(), ltx_ops._code(w.to_out.bias), x_loc.data_ptr(), x_loc.stride(1),
+            w.scale_shift_table.data_ptr(), ltx_ops._code(w.scale_shift_table), w.scale_shift_table.stride(0),
+            ts_view.data_ptr(), ltx_ops._code(ts_view), ts_view.stride(1), ts_view.stride(2), 2,
+            out.data_ptr(), out.stride(1), ltx_ops._stream(x_loc),
+        )
+        return out
+
+    def forward(self, x: torch.Tensor, timestep: torch.Tensor, pe: tuple[torch.Tensor, torch.Tensor]):
+        """x: all tokens [1, L, 4096] (each rank reads its own slice); returns this rank's output slice."""
+        return self.forward_local(self.local_slice(x), timestep, pe)
+
+    __call__ = forward
+
+    # ------------------------------------------------------------------ calibration / timing
+    @torch.no_grad()
+    def calibrate_input_scales(self, x: torch.Tensor, timestep: torch.Tensor, pe) -> None:
+        """Static input scales = global amax / 448 (max over ranks) of each FP8 linear's input."""
+        p = self.plan
+        w = self.w
+        x_loc = self.local_slice(x)
+        Ll = x_loc.shape[1]
+        t0 = p.rank * Ll
+        ts_loc = timestep[:, t0:t0 + Ll]
+        norm = ltx_ops.fused_adazero_from_ada(x_loc, w.norm_eps, w.scale_shift_table, ts_loc, shift_index=0,
+                                              scale_index=1)
+        amax = norm.float().abs().amax().reshape(1)
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        s_in = (amax.clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
+        for lin in (w.to_q, w.to_k, w.to_v):
+            lin.input_scale = s_in.clone()
+        self.blk.shared_quant = True
+        ws = self.workspace(Ll)
+        q, k, v = self._qkv_and_exchange(x_loc, ts_loc, pe[0][:, :, t0:t0 + Ll], pe[1][:, :, t0:t0 + Ll], ws)
+        attn = ltx_ops.attention(q, k, v, p.heads_local)
+        amax = attn.float().abs().amax().reshape(1)
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        w.to_out.input_scale = (amax.clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
+
+    def time_attention(self, steps: int, warmup: int = 3) -> float:
+        """Average device time (ms) of this rank's attention kernel (H/P heads over all L tokens)."""
+        Ll = max(self._ws)
+        ws = self._ws[Ll]
+        L = Ll * self.plan.world
+        q, k, v = self.plan.attention_views(ws["recv1"], L)
+        out = ws["send2"].view(1, L, -1)
+        for _ in range(warmup):
+            ltx_ops.attention(q, k, v, self.plan.heads_local, out=out, out_e4m3_scale=self.w.to_out.input_scale)
+        stream = torch.cuda.current_stream(self.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(self.device)
+        e0.record(stream)
+        for _ in range(steps):
+            ltx_ops.attention(q, k, v, self.plan.heads_local, out=out, out_e4m3_scale=self.w.to_out.input_scale)
+        e1.record(stream)
+        torch.cuda.synchronize(self.device)
+        return e0.elapsed_time(e1) / steps
+
+
+__all__ = ["UlyssesPlan", "UlyssesVideoSelfAttention", "DTYPE_BF16"]
