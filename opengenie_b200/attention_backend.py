@@ -1,0 +1,177 @@
+"""Attention-backend switch and block-branch installers with the B200-native path registered.
+
+Mirrors the reference's switch (benchmarks/official_ltx23_benchmark.py:49-63 choices, `_resolve_attention`
+:3746-3759, `_pin_attention` :3667-3703) and adds ``"b200-native"`` next to ``"sdpa-cudnn"``.  The
+reference installs backends by monkey-patching ltx_core classes (`FlashAttention3.__call__`, :3374) or with
+`set_attention_module_op` on the transformer builder; ltx_core is an external package, so the installers
+here patch a class or a module tree handed to them, following the same pattern.
+
+Also provides `video_msa_branch`, the counterpart of `_video_msa_branch_from_ada`
+(ltx_serve/triton_ltx_ops.py:2891-2981): the whole video self-attention branch of a DiT block as one
+fail-closed call that either returns the new residual stream or declines with a recorded reason.
+"""
+
+from __future__ import annotations
+
+import importlib
+from collections import Counter
+
+import torch
+
+from . import ltx_ops
+
+# The reference's choices plus the B200-native backend.
+ATTENTION_CHOICES = (
+    "h100-fa3", "h100-fa4", "automatic", "flash-attn-3", "flash-attn-4",
+    "sdpa-flash", "sdpa-cudnn", "sdpa-efficient", "sdpa-math", "b200-native",
+)
+
+
+def _importable(module: str, attr: str | None = None) -> bool:
+    try:
+        mod = importlib.import_module(module)
+        return attr is None or hasattr(mod, attr)
+    except Exception:
+        return False
+
+
+def resolve_attention(attention: str) -> str:
+    """`_resolve_attention` (official_ltx23_benchmark.py:3746-3759) with ``b200-native`` passed through."""
+    if attention not in ATTENTION_CHOICES:
+        raise ValueError(f"unknown attention backend: {attention}")
+    if attention == "h100-fa3":
+        return "flash-attn-3" if _importable("flash_attn_interface") else resolve_attention("h100-fa4")
+    if attention != "h100-fa4":
+        return attention
+    return "flash-attn-4" if _importable("flash_attn.cute", "flash_attn_func") else "sdpa-cudnn"
+
+
+class B200NativeAttention:
+    """Attention backend callable with the reference's contract: ``(q, k, v, heads) -> out``, q/k/v
+    [B, L, H*d] bf16, d = 128, no mask, scale d^-0.5 (official_ltx23_benchmark.py:3289-3373)."""
+
+    name = "b200-native"
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, mask=None) -> torch.Tensor:
+        if mask is not None:
+            raise ValueError("mask: the b200-native backend is dense bidirectional attention")
+        return ltx_ops.attention(q, k, v, heads)
+
+
+class TorchSdpaAttention:
+    """torch SDPA with a fixed backend (the reference's ``sdpa-*`` names), for side-by-side runs."""
+
+    _BACKENDS = {"sdpa-flash": "FLASH_ATTENTION", "sdpa-cudnn": "CUDNN_ATTENTION",
+                 "sdpa-efficient": "EFFICIENT_ATTENTION", "sdpa-math": "MATH"}
+
+    def __init__(self, name: str):
+        from torch.nn.attention import SDPBackend
+
+        self.name = name
+        self.backend = getattr(SDPBackend, self._BACKENDS[name])
+
+    def __call__(self, q, k, v, heads, mask=None):
+        from torch.nn.attention import sdpa_kernel
+
+        b, L, hd = q.shape
+        qh, kh, vh = (t.reshape(b, -1, heads, hd // heads).transpose(1, 2) for t in (q, k, v))
+        with sdpa_kernel(self.backend):
+            o = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask)
+        return o.transpose(1, 2).reshape(b, -1, hd)
+
+
+def attention_function(attention: str):
+    """The backend callable for a (resolved) backend name."""
+    name = resolve_attention(attention)
+    if name == "b200-native":
+        return B200NativeAttention()
+    if name.startswith("sdpa-"):
+        return TorchSdpaAttention(name)
+    raise ImportError(f"backend {name} needs an external package (flash_attn / ltx_core) that is not installed")
+
+
+def pin_attention(model: torch.nn.Module, attention: str) -> int:
+    """Sets ``attention_function`` on every module of ``model`` that has one (the attention modules),
+    as `_pin_attention`'s module op does for ltx_core's Attention; returns how many were pinned."""
+    fn = attention_function(attention)
+    n = 0
+    for mod in model.modules():
+        if hasattr(mod, "attention_function"):
+            mod.attention_function = fn
+            n += 1
+    return n
+
+
+def install_attention_class(cls, attention: str = "b200-native"):
+    """Replaces ``cls.__call__`` with the backend (the reference's FlashAttention3.__call__ patch,
+    official_ltx23_benchmark.py:3374); returns the previous ``__call__``."""
+    fn = attention_function(attention)
+    previous = cls.__call__
+
+    def _call(self, q, k, v, heads, *args, **kwargs):
+        return fn(q, k, v, heads)
+
+    cls.__call__ = _call
+    return previous
+
+
+# ---------------------------------------------------------------- the whole branch
+_MSA_BRANCH_CALLS = 0
+_MSA_BRANCH_FALLBACK_REASONS: Counter = Counter()
+_MSA_BLOCKS: dict[int, object] = {}
+
+
+def _decline(reason: str):
+    _MSA_BRANCH_FALLBACK_REASONS[reason] += 1
+    return None
+
+
+def video_msa_branch(block, video, vx: torch.Tensor, *, token_counts: set[int] | None = None):
+    """Video self-attention branch of a DiT block on the B200 kernels, or None with a recorded reason.
+
+    Counterpart of `_video_msa_branch_from_ada` (ltx_serve/triton_ltx_ops.py:2891-2981): same
+    fail-closed checks and reason names (`shape`, `token_count`, `mask`, `all_perturbed`,
+    `missing_rope`), then AdaZero(0/1) -> FP8 Q/K/V -> Q/K RMSNorm + RoPE -> attention ->
+    out-projection -> bias + gate(2) + residual as five sm_100a kernels.  ``block`` provides
+    ``scale_shift_table``, ``norm_eps`` and ``attn1`` (FP8 linears ``to_q/to_k/to_v/to_out[0]`` with
+    ``weight``/``weight_scale``/``input_scale``/``bias``, and ``q_norm``/``k_norm`` with ``weight``/``eps``);
+    ``video`` provides ``timesteps`` and ``positional_embeddings`` (cos, sin).
+    """
+    global _MSA_BRANCH_CALLS
+    from .synthetic import BlockWeights, Fp8Linear
+    from .video_block import VideoSelfAttentionBlock
+
+    if vx.ndim != 3 or vx.shape[0] != 1 or vx.shape[-1] != 4096:
+        return _decline("shape")
+    if token_counts is not None and vx.shape[1] not in token_counts:
+        return _decline("token_count")
+    if getattr(video, "self_attention_mask", None) is not None:
+        return _decline("mask")
+    if getattr(video, "self_attn_all_perturbed", False):
+        return _decline("all_perturbed")
+    if getattr(video, "self_attn_perturbation_mask", None) is not None:
+        return _decline("perturbation_mask")
+    pe = getattr(video, "positional_embeddings", None)
+    if pe is None:
+        return _decline("missing_rope")
+    attn = block.attn1
+    if getattr(attn, "to_gate_logits", None) is not None:
+        return _decline("gated_attention")
+    fused = _MSA_BLOCKS.get(id(block))
+    if fused is None:
+        def lin(m):
+            return Fp8Linear(m.weight, m.weight_scale, m.input_scale, m.bias)
+
+        w = BlockWeights(lin(attn.to_q), lin(attn.to_k), lin(attn.to_v), lin(attn.to_out[0]), attn.q_norm.weight,
+                         attn.k_norm.weight, block.scale_shift_table, float(block.norm_eps),
+                         float(getattr(attn.q_norm, "eps", 1e-6)))
+        fused = VideoSelfAttentionBlock(w, vx.device)
+        _MSA_BLOCKS[id(block)] = fused
+    _MSA_BRANCH_CALLS += 1
+    return fused(vx, video.timesteps, (pe[0], pe[1]))
+
+
+def collect_video_msa_branch_stats() -> dict:
+    """Call / decline counters, as `collect_video_msa_branch_stats` (triton_ltx_ops.py:2235-2266)."""
+    return {"calls": _MSA_BRANCH_CALLS, "fallbacks": sum(_MSA_BRANCH_FALLBACK_REASONS.values()),
+            "fallback_reasons": dict(_MSA_BRANCH_FALLBACK_REASONS)}
