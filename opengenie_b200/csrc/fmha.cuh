@@ -70,6 +70,25 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for the share of the exponentials the MUFU unit cannot
+// absorb at tensor-core rate.  x = j + f with j = round(x) taken from the bits of
+// x + 1.5*2^23 and f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted here to
+// 2^f on [-1/2, 1/2] (least squares on Chebyshev nodes with Lawson reweighting
+// towards minimax; max relative error 7.5e-5, far below bf16's 2^-9); 2^j is
+// added to the exponent field.  x is clamped at -126 (P rounds to 0 there).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = x + 12582912.0f;  // 1.5 * 2^23: the low mantissa bits hold round(x)
+  const float f = x - (t - 12582912.0f);
+  float p = fmaf(0.0551716648f, f, 0.2426111251f);
+  p = fmaf(p, f, 0.6932609677f);
+  p = fmaf(p, f, 0.9999280572f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Which 32-column chunks of a score row use ex2_poly instead of the MUFU ex2.
+constexpr uint32_t kPolyChunkMask = 0x8u;
+
 // Q/K/V tensor maps are 4-D {d (128), head, token, batch} with a box of
 // {64, 1, 128, 1}: one 64-column half of a 128-row tile, 128-byte swizzled.
 __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int head, int row0,
@@ -263,14 +282,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t pk[16];
+        const bool poly = (kPolyChunkMask >> cc) & 1u;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(fmaf(sf[cc * 32 + 2 * i], c, -m_use));
-          const float p1 = ex2(fmaf(sf[cc * 32 + 2 * i + 1], c, -m_use));
+          const float a0 = fmaf(sf[cc * 32 + 2 * i], c, -m_use);
+          const float a1 = fmaf(sf[cc * 32 + 2 * i + 1], c, -m_use);
+          const float p0 = poly ? ex2_poly(a0) : ex2(a0);
+          const float p1 = poly ? ex2_poly(a1) : ex2(a1);
+          rowsum += p0 + p1;
           __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-          // the row sum uses the bf16 values the PV product consumes
-          const float2 bf = __bfloat1622float2(b2);
-          rowsum += bf.x + bf.y;
           pk[i] = *reinterpret_cast<uint32_t*>(&b2);
         }
         // P chunk cc -> TMEM columns [16cc, 16cc+16) of S_q (all of S is already in registers)

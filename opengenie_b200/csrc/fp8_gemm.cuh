@@ -8,8 +8,10 @@
 //   warp 1      MMA issuer:   tcgen05.mma kind::f8f6f4, M=128 N=256 K=32,
 //                             fp32 accumulators in TMEM (2 x 256 columns, so
 //                             the epilogue of one tile overlaps the next tile)
-//   warps 2..5  epilogue:     tcgen05.ld -> scale -> bf16 -> bias (-> gate +
-//                             residual) -> global
+//   warps 2..9  epilogue:     tcgen05.ld -> scale -> bf16 -> bias (-> gate +
+//                             residual) -> global; two warps per TMEM lane
+//                             quarter split the tile's columns, 16-byte vector
+//                             loads of bias / gate / timestep / residual
 // Epilogues reproduce the reference's rounding sequence:
 //   EPI_BIAS:     bf16(bf16(acc*s) + bf16(bias))            (scaled_mm, then
 //                 fused_bias_add_bf16, triton_ltx_ops.py:1695-1707)
@@ -33,7 +35,7 @@ constexpr int B_STAGE_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
 
 enum Epilogue : int { EPI_BIAS = 0, EPI_RESIDUAL = 1 };
@@ -74,11 +76,6 @@ struct SharedState {
   int abort;
 };
 
-__device__ __forceinline__ float load_scalar(const void* p, int is_fp32, int64_t i) {
-  return is_fp32 ? __ldg(static_cast<const float*>(p) + i)
-                 : __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
-}
-
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -102,7 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&st.tmem_full[a], 1);
-      mbar_init(&st.tmem_empty[a], 128);
+      mbar_init(&st.tmem_empty[a], 256);
     }
     mbar_init(&st.drained, 1);
     st.abort = 0;
@@ -210,7 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const uint32_t quarter = warp & 3;  // TMEM lanes this warp may access
+    // 8 warps: warp w reads TMEM lane quarter (w % 4) and column half (w - 2) / 4 of the tile.
+    const uint32_t quarter = warp & 3;
+    const int half = (static_cast<int>(warp) - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     const float sa = __ldg(p.scale_a);
     int local = 0;
@@ -220,53 +219,62 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&st.tmem_full[acc], acc_phase, abort)) break;
       tc_fence_after();
       const int m0 = (tile % num_m) * BM;
-      const int n0 = (tile / num_m) * BN;
+      const int n0 = (tile / num_m) * BN + half * (BN / 2);
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
-      const uint32_t taddr_row = tmem_base + ((quarter * 32u) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(taddr_row + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = n0 + c * 32;
-        if (!row_ok || col0 >= p.N) continue;
-        const float scale = sa * __ldg(p.scale_b + col0 / p.n_per_scale);
-        float o[32];
+      const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + half * (BN / 2);
+      uint32_t ra[32], rb[32];
+      tmem_ld32(taddr, ra);
+      tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = bf16_round(__uint_as_float(r[i]) * scale);
-          if (p.bias != nullptr) v = bf16_round(v + bf16_round(load_scalar(p.bias, p.bias_fp32, col0 + i)));
-          o[i] = v;
-        }
-        if (EPI == EPI_RESIDUAL) {
-          const __nv_bfloat16* xr = p.resid_x + static_cast<int64_t>(row) * p.ldx + col0;
-          const int64_t tso = static_cast<int64_t>(row) * p.ts_stride_t + p.gate_index * p.ts_stride_p + col0;
-          const int64_t tbo = p.gate_index * p.table_stride_row + col0;
+      for (int c = 0; c < BN / 2 / 32; ++c) {
+        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+        if (c + 1 < BN / 2 / 32) tmem_ld32(taddr + (c + 1) * 32, nxt);  // in flight while `cur` is processed
+        const int col0 = n0 + c * 32;
+        if (row_ok && col0 < p.N) {
+          const float scale = sa * __ldg(p.scale_b + col0 / p.n_per_scale);
+          __nv_bfloat16* orow = p.out + static_cast<int64_t>(row) * p.ldo + col0;
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
-            float xf[8];
-            unpack8(__ldg(reinterpret_cast<const uint4*>(xr) + v8), xf);
+            const int cb = col0 + v8 * 8;
+            float o[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int cc = v8 * 8 + i;
-              float tg = load_scalar(p.table, p.table_fp32, tbo + cc);
-              const float sg = load_scalar(p.ts, p.ts_fp32, tso + cc);
-              if (p.table_fp32 != p.ts_fp32) tg = bf16_round(tg);
-              float g = tg + sg;
-              if (!p.ts_fp32) g = bf16_round(g);
-              o[cc] = xf[i] + bf16_round(o[cc] * g);
+            for (int i = 0; i < 8; ++i) o[i] = bf16_round(__uint_as_float(cur[v8 * 8 + i]) * scale);
+            if (p.bias != nullptr) {
+              float bb[8];
+              if (p.bias_fp32)
+                load8<float>(static_cast<const float*>(p.bias) + cb, bb);
+              else
+                load8<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(p.bias) + cb, bb);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] = bf16_round(o[i] + bf16_round(bb[i]));
             }
+            if (EPI == EPI_RESIDUAL) {
+              float xf[8], tg[8], sg[8];
+              unpack8(__ldg(reinterpret_cast<const uint4*>(p.resid_x + static_cast<int64_t>(row) * p.ldx + cb)), xf);
+              const int64_t tbo = p.gate_index * p.table_stride_row + cb;
+              const int64_t tso = static_cast<int64_t>(row) * p.ts_stride_t + p.gate_index * p.ts_stride_p + cb;
+              if (p.table_fp32)
+                load8<float>(static_cast<const float*>(p.table) + tbo, tg);
+              else
+                load8<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(p.table) + tbo, tg);
+              if (p.ts_fp32)
+                load8<float>(static_cast<const float*>(p.ts) + tso, sg);
+              else
+                load8<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(p.ts) + tso, sg);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float t = (p.table_fp32 != p.ts_fp32) ? bf16_round(tg[i]) : tg[i];
+                float g = t + sg[i];
+                if (!p.ts_fp32) g = bf16_round(g);
+                o[i] = xf[i] + bf16_round(o[i] * g);
+              }
+            }
+            reinterpret_cast<uint4*>(orow)[v8] = pack8(o);
           }
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(row) * p.ldo + col0);
-#pragma unroll
-        for (int v8 = 0; v8 < 4; ++v8) {
-          float f[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = o[v8 * 8 + i];
-          dst[v8] = pack8(f);
-        }
+        tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(&st.tmem_empty[acc]);

@@ -505,7 +505,9 @@ static int residual_gate_impl(int64_t a_k_block, const void* a, int64_t M, int64
       gate_index < 0)
     return fail(OGX_EINVAL, "ada");
   const int tesz = timestep_dtype == OGX_DTYPE_F32 ? 4 : 2;
-  if (!aligned16(table) || !aligned16(timestep) || (ts_stride_t * tesz) % 16 || (ts_stride_p * tesz) % 16)
+  const int tbsz = table_dtype == OGX_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(table) || !aligned16(timestep) || (ts_stride_t * tesz) % 16 || (ts_stride_p * tesz) % 16 ||
+      (table_stride_row * tbsz) % 16)
     return fail(OGX_EINVAL, "timestep_stride");
   ogx::gemm::Params p{};
   p.M = static_cast<int>(M);
