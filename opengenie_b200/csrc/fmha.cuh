@@ -38,6 +38,14 @@ constexpr int HALF_BYTES = 128 * 64 * 2;  // one 64-column half of a 128-row til
 constexpr int TILE_BYTES = 2 * HALF_BYTES;
 constexpr int SMEM_BYTES = (NQ + 2 * STAGES) * TILE_BYTES + 1024;
 constexpr int kThreads = 384;
+// Register split (setmaxnreg): the kernel is launched with kLaunchRegs per thread (the host checks the
+// built count before launching); warpgroup 0 (TMA / MMA) drops to kRegsProducer and the two softmax
+// warpgroups rise to kRegsSoftmax.  The split must fit in what the launch reserved, or the increase
+// would wait forever: 128 * 96 + 256 * 200 = 63488 <= 384 * 168 = 64512.
+constexpr int kLaunchRegs = 168;
+constexpr uint32_t kRegsProducer = 96;
+constexpr uint32_t kRegsSoftmax = 200;
+static_assert(128 * kRegsProducer + 256 * kRegsSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
 constexpr uint32_t TMEM_COLS = 512;
 // A row's running max only moves when a new score exceeds it by more than
 // this many log2 units, so P <= 2^8 and most tiles need no O rescale.
@@ -86,8 +94,57 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
-// Which 32-column chunks of a score row use ex2_poly instead of the MUFU ex2.
+// Which 32-column chunks of a score row use the polynomial instead of the MUFU ex2.
 constexpr uint32_t kPolyChunkMask = 0x8u;
+
+// Packed two-lane fp32 arithmetic (sm_100 f32x2 instructions): one issue slot for two values.
+struct f2 {
+  float x, y;
+};
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("{.reg .b64 A, B, C, D;\n\t"
+      "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\tmov.b64 C, {%6, %7};\n\t"
+      "fma.rn.f32x2 D, A, B, C;\n\tmov.b64 {%0, %1}, D;}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 d;
+  asm("{.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "add.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 d;
+  asm("{.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "sub.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// ex2_poly on two lanes with packed arithmetic (same polynomial and reduction).
+__device__ __forceinline__ f2 ex2_poly2(f2 x) {
+  const f2 magic{12582912.0f, 12582912.0f};
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const f2 t = add2(x, magic);
+  const f2 f = sub2(x, sub2(t, magic));
+  f2 p = fma2(f2{0.0551716648f, 0.0551716648f}, f, f2{0.2426111251f, 0.2426111251f});
+  p = fma2(p, f, f2{0.6932609677f, 0.6932609677f});
+  p = fma2(p, f, f2{0.9999280572f, 0.9999280572f});
+  return f2{__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+            __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23))};
+}
 
 // Q/K/V tensor maps are 4-D {d (128), head, token, batch} with a box of
 // {64, 1, 128, 1}: one 64-column half of a 128-row tile, 128-byte swizzled.
@@ -145,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &st.abort;
 
   if (warp < 4) {
+    reg_dealloc<kRegsProducer>();
     if (warp == 0 && elect_one()) {
       // ---------------------------------------------------------- TMA producer
       tma_prefetch_desc(&tq);
@@ -239,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&st.drained, 0, nullptr);
     }
   } else {
+    reg_alloc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax + epilogue
     const int q = (warp - 4) >> 2;            // Q tile of this warpgroup
     const uint32_t quarter = warp & 3;        // TMEM lane quarter of this warp
@@ -264,9 +323,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= kv_valid) sf[i] = -INFINITY;
       }
-      float mx = sf[0];
+      float mx = fmaxf(sf[0], sf[127]);
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sf[i]);
+      for (int i = 1; i < 127; i += 2) mx = max3(mx, sf[i], sf[i + 1]);
       const float m_tile = mx * c;
       float m_use = m_run;
       float alpha = 1.f;
@@ -278,24 +337,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         alpha = ex2(m_run - m_tile);
         rescale = true;
       }
-      float rowsum = 0.f;
+      f2 rowsum2{0.f, 0.f};
+      const f2 c2{c, c};
+      const f2 negm{-m_use, -m_use};
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t pk[16];
         const bool poly = (kPolyChunkMask >> cc) & 1u;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float a0 = fmaf(sf[cc * 32 + 2 * i], c, -m_use);
-          const float a1 = fmaf(sf[cc * 32 + 2 * i + 1], c, -m_use);
-          const float p0 = poly ? ex2_poly(a0) : ex2(a0);
-          const float p1 = poly ? ex2_poly(a1) : ex2(a1);
-          rowsum += p0 + p1;
-          __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+          const f2 a = fma2(f2{sf[cc * 32 + 2 * i], sf[cc * 32 + 2 * i + 1]}, c2, negm);
+          const f2 pr = poly ? ex2_poly2(a) : f2{ex2(a.x), ex2(a.y)};
+          rowsum2 = add2(rowsum2, pr);
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(pr.x, pr.y);
           pk[i] = *reinterpret_cast<uint32_t*>(&b2);
         }
         // P chunk cc -> TMEM columns [16cc, 16cc+16) of S_q (all of S is already in registers)
         tmem_st16(s_tmem + cc * 16, pk);
       }
+      const float rowsum = rowsum2.x + rowsum2.y;
       l_run = l_run * alpha + rowsum;
       m_run = m_use;
       if (__any_sync(0xffffffffu, rescale)) {

@@ -457,6 +457,14 @@ int attention_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtenso
   auto kern = ogx::fmha::fmha_fwd_kernel<E4M3>;
   int rc = ensure_smem(kern, ogx::fmha::SMEM_BYTES);
   if (rc) return rc;
+  // The softmax warpgroups raise their register limit with setmaxnreg, drawing on the registers the
+  // launch reserved; only launch a build whose per-thread count is the one the split was sized for.
+  cudaFuncAttributes attr;
+  rc = check_cuda(cudaFuncGetAttributes(&attr, kern), "cudaFuncGetAttributes");
+  if (rc) return rc;
+  if (attr.numRegs != ogx::fmha::kLaunchRegs)
+    return fail(OGX_ECUDA, "fmha kernel built with %d registers per thread, the register split needs %d", attr.numRegs,
+                ogx::fmha::kLaunchRegs);
   const dim3 grid(static_cast<unsigned>((tokens + 255) / 256), static_cast<unsigned>(heads),
                   static_cast<unsigned>(batch));
   kern<<<grid, ogx::fmha::kThreads, ogx::fmha::SMEM_BYTES, s>>>(mq, mk, mv, p);
