@@ -54,7 +54,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.05):
+    def __init__(self, device_index: int, period_s: float = 0.005):
         self.samples: list[int] = []
         self.reasons: set[str] = set()
         self.max_mhz = None
@@ -273,24 +273,33 @@ def main() -> None:
     ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, pg)
     value = attn_flops(L) / (ms * 1e-3) / 1e12
 
-    # ---- e2e: host x (pinned) -> device, block, device -> host output, every step
-    x_host = inp_cpu.x.pin_memory() if world == 1 else blk.local_slice(inp_cpu.x).pin_memory()
-    out_host = torch.empty_like(x_host).pin_memory()
-    x_dev = torch.empty_like(x_host, device=dev)
-    barrier(pg)
+    # ---- e2e: host x (pinned) -> device, block, device -> host output, every step, through the public
+    # API's host pipeline (copy in, compute and copy out of consecutive steps overlap on three streams)
+    from opengenie_b200.streaming import HostPipeline
+
+    x_host = (inp_cpu.x if world == 1 else blk.local_slice(inp_cpu.x)).contiguous().pin_memory()
+    out_hosts = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
+    if world == 1:
+        def host_step(xd, yd):
+            blk(xd, inp.timestep, (inp.cos, inp.sin), out=yd)
+    else:
+        def host_step(xd, yd):
+            blk.forward_local(xd, inp.timestep, (inp.cos, inp.sin), out=yd)
+    pipe = HostPipeline(host_step, tuple(x_host.shape), x_host.dtype, dev)
+    pipe.run([x_host] * 2, out_hosts)  # warm-up
     torch.cuda.synchronize(dev)
+    barrier(pg)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        x_dev.copy_(x_host, non_blocking=True)
-        y = step(x_dev) if world == 1 else blk.forward_local(x_dev, inp.timestep, (inp.cos, inp.sin))
-        out_host.copy_(y, non_blocking=True)
+    pipe.start_after(e0)
+    pipe.run([x_host] * args.steps, [out_hosts[i % 2] for i in range(args.steps)])
+    pipe.wait_streams(stream)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(pg)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, pg)
     h2d = x_host.numel() * x_host.element_size()
-    d2h = out_host.numel() * out_host.element_size()
+    d2h = out_hosts[0].numel() * out_hosts[0].element_size()
 
     # ---- dominant kernel (attention) timed alone on the launching stream
     attn_ms = blk.time_attention(args.steps, args.warmup) if hasattr(blk, "time_attention") else None

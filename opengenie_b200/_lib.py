@@ -11,7 +11,8 @@ import os
 from ctypes import c_float, c_int, c_int64, c_uint, c_void_p
 
 LIB_NAME = "libogx.so"
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+# OPENGENIE_B200_LIB selects another build of the same library (e.g. a tuning variant).
+LIB_PATH = os.environ.get("OPENGENIE_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
 OGX_OK = 0
 DTYPE_BF16 = 0

@@ -133,6 +133,27 @@ __device__ __forceinline__ uint2 quant8(const float (&f)[8], float s, float r) {
   return make_uint2(lo, hi);
 }
 
+// The torch-path quantiser on bf16 input (the hot case), two values per
+// conversion instruction: t = bf16(x * r) by a packed RNE, clamp, packed
+// saturating e4m3 conversion; NaN lanes patched to 0xFF afterwards.
+template <>
+__device__ __forceinline__ uint2 quant8<__nv_bfloat16, kQuantTorch>(const float (&f)[8], float s, float r) {
+  uint32_t w[2] = {0, 0};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float t0 = __fmul_rn(f[2 * i], r), t1 = __fmul_rn(f[2 * i + 1], r);
+    bf16_round2(t0, t1);
+    t0 = fminf(fmaxf(t0, -448.0f), 448.0f);
+    t1 = fminf(fmaxf(t1, -448.0f), 448.0f);
+    const uint32_t c2 = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(t0, t1), __NV_SATFINITE, __NV_E4M3));
+    w[i >> 1] |= (c2 & 0xFFFFu) << (16 * (i & 1));
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (f[i] != f[i]) w[i >> 2] |= 0xFFu << (8 * (i & 3));
+  return make_uint2(w[0], w[1]);
+}
+
 // ----------------------------------------------------------------- AdaZero
 // y = rmsnorm(x) * (1 + scale) + shift in fp32 with one bf16 rounding
 // (the reference's GPU kernel, triton_ltx_ops.py:3359-3427), with
@@ -166,57 +187,97 @@ __device__ __forceinline__ float row_sum(float v, float* red) {
   return red[0] + red[1] + red[2] + red[3];
 }
 
-template <int COLS, typename TableT, typename TsT, bool QUANT, int QMODE>
+constexpr int kAdaRowsPerCta = 8;
+
+// One 128-thread CTA per kAdaRowsPerCta rows.  With a token-uniform timestep
+// (stride 0 over tokens, the uniform-timestep layout) shift/scale are the same
+// for every row, so each thread computes them for its columns once and keeps
+// them in registers; otherwise they are read per row.  The next row's x is
+// loaded before the current row's reduction completes.
+template <int COLS, typename TableT, typename TsT, bool QUANT, int QMODE, bool UNIFORM>
 __global__ void __launch_bounds__(kRowThreads) adazero_from_ada_kernel(AdaArgs a) {
   constexpr int VPT = COLS / 8 / kRowThreads;  // 16-byte vectors per thread
-  __shared__ float red[4];
+  __shared__ float red[2][4];
   const int tid = threadIdx.x;
-  const int64_t row = blockIdx.x;
-  const int64_t b = row / a.tokens;
-  const int64_t t = row - b * a.tokens;
-
-  const uint4* xr = reinterpret_cast<const uint4*>(a.x + row * COLS);
-  uint4 xv[VPT];
-  float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    xv[j] = __ldg(xr + j * kRowThreads + tid);
-    float f[8];
-    unpack8(xv[j], f);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
-  }
-  ss = row_sum(ss, red);
-  const float inv_rms = rsqrtf(ss / static_cast<float>(COLS) + a.eps);
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kAdaRowsPerCta;
+  const int64_t row_end = (row0 + kAdaRowsPerCta < a.rows) ? row0 + kAdaRowsPerCta : a.rows;
 
   const TableT* table = static_cast<const TableT*>(a.table);
-  const TsT* ts = static_cast<const TsT*>(a.ts) + b * a.ts_stride_b + t * a.ts_stride_t;
   const TableT* tshift = table + a.shift_index * a.table_stride_row;
   const TableT* tscale = table + a.scale_index * a.table_stride_row;
-  const TsT* sshift = ts + a.shift_index * a.ts_stride_p;
-  const TsT* sscale = ts + a.scale_index * a.ts_stride_p;
-
   float s = 0.f, r = 0.f;
   if (QUANT) {
     s = __ldg(a.input_scale);
     r = __frcp_rn(s);
   }
+
+  float ushift[UNIFORM ? VPT : 1][8], uscale[UNIFORM ? VPT : 1][8];
+  if (UNIFORM) {
+    const TsT* ts = static_cast<const TsT*>(a.ts);
 #pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int vec = j * kRowThreads + tid;
-    const int col = vec * 8;
-    float f[8], shift[8], scale[8], y[8];
-    unpack8(xv[j], f);
-    ada_values8<TableT, TsT>(tshift + col, sshift + col, shift);
-    ada_values8<TableT, TsT>(tscale + col, sscale + col, scale);
+    for (int j = 0; j < VPT; ++j) {
+      const int col = (j * kRowThreads + tid) * 8;
+      ada_values8<TableT, TsT>(tshift + col, ts + a.shift_index * a.ts_stride_p + col, ushift[j % (UNIFORM ? VPT : 1)]);
+      ada_values8<TableT, TsT>(tscale + col, ts + a.scale_index * a.ts_stride_p + col, uscale[j % (UNIFORM ? VPT : 1)]);
+    }
+  }
+
+  uint4 xn[VPT];
+  if (row0 < row_end) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = fmaf(f[i] * inv_rms, 1.0f + scale[i], shift[i]);
-    const uint4 yv = pack8(y);
-    if (a.y != nullptr) reinterpret_cast<uint4*>(a.y + row * COLS)[vec] = yv;
-    if (QUANT) {
-      float yb[8];
-      unpack8(yv, yb);
-      reinterpret_cast<uint2*>(a.q + row * COLS)[vec] = quant8<__nv_bfloat16, QMODE>(yb, s, r);
+    for (int j = 0; j < VPT; ++j) xn[j] = __ldg(reinterpret_cast<const uint4*>(a.x + row0 * COLS) + j * kRowThreads + tid);
+  }
+  for (int64_t row = row0; row < row_end; ++row) {
+    uint4 xv[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) xv[j] = xn[j];
+    if (row + 1 < row_end) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j)
+        xn[j] = __ldg(reinterpret_cast<const uint4*>(a.x + (row + 1) * COLS) + j * kRowThreads + tid);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      float f[8];
+      unpack8(xv[j], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+    }
+    ss = warp_sum(ss);
+    float* rb = red[row & 1];
+    if ((tid & 31) == 0) rb[tid >> 5] = ss;
+    __syncthreads();
+    ss = rb[0] + rb[1] + rb[2] + rb[3];
+    const float inv_rms = rsqrtf(ss / static_cast<float>(COLS) + a.eps);
+
+    const int64_t b = row / a.tokens;
+    const int64_t t = row - b * a.tokens;
+    const TsT* ts = static_cast<const TsT*>(a.ts) + b * a.ts_stride_b + t * a.ts_stride_t;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int vec = j * kRowThreads + tid;
+      const int col = vec * 8;
+      float f[8], y[8];
+      unpack8(xv[j], f);
+      if (UNIFORM) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = fmaf(f[i] * inv_rms, 1.0f + uscale[j % (UNIFORM ? VPT : 1)][i],
+                                                ushift[j % (UNIFORM ? VPT : 1)][i]);
+      } else {
+        float shift[8], scale[8];
+        ada_values8<TableT, TsT>(tshift + col, ts + a.shift_index * a.ts_stride_p + col, shift);
+        ada_values8<TableT, TsT>(tscale + col, ts + a.scale_index * a.ts_stride_p + col, scale);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = fmaf(f[i] * inv_rms, 1.0f + scale[i], shift[i]);
+      }
+      const uint4 yv = pack8(y);
+      if (a.y != nullptr) reinterpret_cast<uint4*>(a.y + row * COLS)[vec] = yv;
+      if (QUANT) {
+        float yb[8];
+        unpack8(yv, yb);
+        reinterpret_cast<uint2*>(a.q + row * COLS)[vec] = quant8<__nv_bfloat16, QMODE>(yb, s, r);
+      }
     }
   }
 }

@@ -37,6 +37,10 @@ constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
 constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+// EPI_RESIDUAL keeps per-column constants (rounded bias, gate or its table part) for up to
+// RES_MAX_N columns in shared memory after the pipeline stages.
+constexpr int RES_MAX_N = 4096;
+constexpr int SMEM_BYTES_RESIDUAL = SMEM_BYTES + 2 * RES_MAX_N * 4;
 
 enum Epilogue : int { EPI_BIAS = 0, EPI_RESIDUAL = 1 };
 
@@ -65,6 +69,15 @@ struct Params {
   int64_t ts_stride_t, ts_stride_p;
   int gate_index;
 };
+
+// Per-column constants of the residual epilogue, computed once per CTA:
+// bias rounded to bf16, and the Ada gate (token-uniform timestep) or its table
+// part rounded as the reference rounds it (per-token timestep).
+template <typename T>
+__device__ __forceinline__ float ld1(const void* p, int64_t i) {
+  return std::is_same<T, float>::value ? __ldg(static_cast<const float*>(p) + i)
+                                       : __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
 
 struct SharedState {
   uint64_t full[STAGES];
@@ -112,6 +125,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tmem_alloc(&st.tmem_base, TMEM_COLS);
     tmem_relinquish();
+  }
+  float* col_bias = reinterpret_cast<float*>(smem_aligned + STAGES * STAGE_BYTES);
+  float* col_gate = col_bias + RES_MAX_N;
+  const bool gate_uniform = p.ts_stride_t == 0;
+  if (EPI == EPI_RESIDUAL) {
+    for (int n = threadIdx.x; n < p.N; n += blockDim.x) {
+      col_bias[n] = p.bias == nullptr ? 0.f
+                                      : bf16_round(p.bias_fp32 ? ld1<float>(p.bias, n) : ld1<__nv_bfloat16>(p.bias, n));
+      const int64_t tb = p.gate_index * p.table_stride_row + n;
+      float t = p.table_fp32 ? ld1<float>(p.table, tb) : ld1<__nv_bfloat16>(p.table, tb);
+      if (p.table_fp32 != p.ts_fp32) t = bf16_round(t);
+      if (gate_uniform) {
+        const int64_t so = p.gate_index * p.ts_stride_p + n;
+        float g = t + (p.ts_fp32 ? ld1<float>(p.ts, so) : ld1<__nv_bfloat16>(p.ts, so));
+        t = p.ts_fp32 ? g : bf16_round(g);
+      }
+      col_gate[n] = t;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -240,36 +271,55 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int cb = col0 + v8 * 8;
             float o[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = bf16_round(__uint_as_float(cur[v8 * 8 + i]) * scale);
-            if (p.bias != nullptr) {
-              float bb[8];
-              if (p.bias_fp32)
-                load8<float>(static_cast<const float*>(p.bias) + cb, bb);
-              else
-                load8<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(p.bias) + cb, bb);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) o[i] = bf16_round(o[i] + bf16_round(bb[i]));
-            }
+            for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(cur[v8 * 8 + i]) * scale;
             if (EPI == EPI_RESIDUAL) {
-              float xf[8], tg[8], sg[8];
+              // y = bf16(acc*s); yb = bf16(y + bf16(bias)); prod = bf16(yb * gate); out = bf16(x + prod)
+              float xf[8], bb[8], g[8];
               unpack8(__ldg(reinterpret_cast<const uint4*>(p.resid_x + static_cast<int64_t>(row) * p.ldx + cb)), xf);
-              const int64_t tbo = p.gate_index * p.table_stride_row + cb;
-              const int64_t tso = static_cast<int64_t>(row) * p.ts_stride_t + p.gate_index * p.ts_stride_p + cb;
-              if (p.table_fp32)
-                load8<float>(static_cast<const float*>(p.table) + tbo, tg);
-              else
-                load8<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(p.table) + tbo, tg);
-              if (p.ts_fp32)
-                load8<float>(static_cast<const float*>(p.ts) + tso, sg);
-              else
-                load8<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(p.ts) + tso, sg);
+              *reinterpret_cast<float4*>(&bb[0]) = *reinterpret_cast<const float4*>(col_bias + cb);
+              *reinterpret_cast<float4*>(&bb[4]) = *reinterpret_cast<const float4*>(col_bias + cb + 4);
+              *reinterpret_cast<float4*>(&g[0]) = *reinterpret_cast<const float4*>(col_gate + cb);
+              *reinterpret_cast<float4*>(&g[4]) = *reinterpret_cast<const float4*>(col_gate + cb + 4);
+              if (!gate_uniform) {
+                float sg[8];
+                const int64_t tso = static_cast<int64_t>(row) * p.ts_stride_t + p.gate_index * p.ts_stride_p + cb;
+                if (p.ts_fp32)
+                  load8<float>(static_cast<const float*>(p.ts) + tso, sg);
+                else
+                  load8<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(p.ts) + tso, sg);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float t = (p.table_fp32 != p.ts_fp32) ? bf16_round(tg[i]) : tg[i];
-                float g = t + sg[i];
-                if (!p.ts_fp32) g = bf16_round(g);
-                o[i] = xf[i] + bf16_round(o[i] * g);
+                for (int i = 0; i < 8; ++i) g[i] += sg[i];
+                if (!p.ts_fp32) {
+#pragma unroll
+                  for (int i = 0; i < 8; i += 2) bf16_round2(g[i], g[i + 1]);
+                }
               }
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) bf16_round2(o[i], o[i + 1]);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] += bb[i];
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) bf16_round2(o[i], o[i + 1]);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] *= g[i];
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) bf16_round2(o[i], o[i + 1]);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] += xf[i];
+            } else if (p.bias != nullptr) {
+              // out = bf16(bf16(acc*s) + bf16(bias)); the final rounding is the bf16 pack below
+              float bb[8];
+              if (p.bias_fp32) {
+                load8<float>(static_cast<const float*>(p.bias) + cb, bb);
+#pragma unroll
+                for (int i = 0; i < 8; i += 2) bf16_round2(bb[i], bb[i + 1]);
+              } else {
+                load8<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(p.bias) + cb, bb);
+              }
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) bf16_round2(o[i], o[i + 1]);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] += bb[i];
             }
             reinterpret_cast<uint4*>(orow)[v8] = pack8(o);
           }

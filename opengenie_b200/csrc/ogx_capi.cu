@@ -94,16 +94,26 @@ int ensure_smem(K kernel, int bytes) {
 bool dtype_ok(int dt) { return dt == OGX_DTYPE_BF16 || dt == OGX_DTYPE_F32; }
 
 // ------------------------------------------------------------- AdaZero
-template <int COLS, typename TableT, typename TsT>
-void launch_ada_cols(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) {
-  const dim3 grid(static_cast<unsigned>(a.rows));
+template <int COLS, typename TableT, typename TsT, bool UNIFORM>
+void launch_ada_u(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>((a.rows + ogx::kAdaRowsPerCta - 1) / ogx::kAdaRowsPerCta));
   const int threads = ogx::kRowThreads;
   if (!quant)
-    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, false, 0><<<grid, threads, 0, s>>>(a);
+    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, false, 0, UNIFORM><<<grid, threads, 0, s>>>(a);
   else if (qmode == OGX_QUANT_TORCH)
-    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantTorch><<<grid, threads, 0, s>>>(a);
+    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantTorch, UNIFORM><<<grid, threads, 0, s>>>(a);
   else
-    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantSingle><<<grid, threads, 0, s>>>(a);
+    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantSingle, UNIFORM><<<grid, threads, 0, s>>>(a);
+}
+
+template <int COLS, typename TableT, typename TsT>
+void launch_ada_cols(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) {
+  // token-uniform timestep: every row of every batch reads the same Ada slots
+  const bool uniform = a.ts_stride_t == 0 && (a.ts_stride_b == 0 || a.rows <= a.tokens);
+  if (uniform)
+    launch_ada_u<COLS, TableT, TsT, true>(a, quant, qmode, s);
+  else
+    launch_ada_u<COLS, TableT, TsT, false>(a, quant, qmode, s);
 }
 
 template <typename TableT, typename TsT>
@@ -423,11 +433,14 @@ int gemm_common(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
 template <int EPI>
 int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::Params& p, cudaStream_t s) {
   auto kern = ogx::gemm::fp8_gemm_kernel<EPI>;
-  int rc = ensure_smem(kern, ogx::gemm::SMEM_BYTES);
+  const int smem = EPI == ogx::gemm::EPI_RESIDUAL ? ogx::gemm::SMEM_BYTES_RESIDUAL : ogx::gemm::SMEM_BYTES;
+  if (EPI == ogx::gemm::EPI_RESIDUAL && p.N > ogx::gemm::RES_MAX_N)
+    return fail(OGX_EINVAL, "shape: the residual epilogue supports N <= %d", ogx::gemm::RES_MAX_N);
+  int rc = ensure_smem(kern, smem);
   if (rc) return rc;
   const int tiles = ((p.M + ogx::gemm::BM - 1) / ogx::gemm::BM) * ((p.N + ogx::gemm::BN - 1) / ogx::gemm::BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, ogx::gemm::kThreads, ogx::gemm::SMEM_BYTES, s>>>(ma, mb, p);
+  kern<<<grid, ogx::gemm::kThreads, smem, s>>>(ma, mb, p);
   return check_launch("fp8_gemm_kernel");
 }
 

@@ -294,4 +294,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Rounds two values to bf16 (RNE) with one packed conversion; results as fp32.
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const uint32_t p = pack_bf16x2(a, b);
+  a = __uint_as_float(p << 16);
+  b = __uint_as_float(p & 0xFFFF0000u);
+}
+
 }  // namespace ogx

@@ -135,7 +135,8 @@ class UlyssesVideoSelfAttention:
         p.exchange_qkv(send, ws["recv1"])
         return p.attention_views(ws["recv1"], Ll * p.world)
 
-    def forward_local(self, x_loc: torch.Tensor, timestep: torch.Tensor, pe: tuple[torch.Tensor, torch.Tensor]):
+    def forward_local(self, x_loc: torch.Tensor, timestep: torch.Tensor, pe: tuple[torch.Tensor, torch.Tensor], *,
+                      out: torch.Tensor | None = None):
         """x_loc: this rank's tokens [1, L/P, 4096]; timestep and pe span all L tokens."""
         p = self.plan
         w = self.w
@@ -150,10 +151,12 @@ class UlyssesVideoSelfAttention:
         send2 = ws["send2"]
         ltx_ops.attention(q, k, v, p.heads_local, out=send2.view(1, L, -1), out_e4m3_scale=w.to_out.input_scale)
         p.exchange_out(send2, ws["recv2"])
-        out = torch.empty_like(x_loc)
+        if out is None:
+            out = torch.empty_like(x_loc)
         ts_view = ltx_ops._ts_view(x_loc, w.scale_shift_table, ts_loc)
         recv2 = ws["recv2"]
-        if recv2.shape != p.out_send_shape(Ll) or ts_view.shape[1] != Ll or x_loc.shape != out.shape:
+        if (recv2.shape != p.out_send_shape(Ll) or ts_view.shape[1] != Ll or x_loc.shape != out.shape
+                or not out.is_contiguous()):
             raise ValueError("out_projection_shape")
         _lib.call(
             "ogx_fp8_scaled_mm_residual_gate_kblocked",

@@ -169,3 +169,23 @@ def test_block_full_size_vs_fp32_reference_on_gpu(ogx_lib, name):
     assert ours["mean_rel"] <= 1e-2, ours
     assert ours["max_abs"] <= theirs["max_abs"], (ours, theirs)
     assert status_clean()
+
+
+def test_host_pipeline_matches_direct_calls(ogx_lib):
+    """Host-resident inputs through the three-stream pipeline give exactly the direct block outputs."""
+    from opengenie_b200 import synthetic
+    from opengenie_b200.streaming import HostPipeline
+    from opengenie_b200.video_block import VideoSelfAttentionBlock
+
+    cfg = synthetic.small_config(2, 8, 16)
+    inp = synthetic.make_inputs(cfg, seed=71).to("cuda")
+    blk = VideoSelfAttentionBlock(synthetic.make_weights(seed=72), "cuda")
+    blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
+    xs = [(inp.x.float().cpu() * (1 + 0.1 * i)).to(torch.bfloat16).pin_memory() for i in range(5)]
+    outs = [torch.empty_like(x).pin_memory() for x in xs]
+    pipe = HostPipeline(lambda xd, yd: blk(xd, inp.timestep, (inp.cos, inp.sin), out=yd), tuple(xs[0].shape),
+                        torch.bfloat16, "cuda")
+    pipe.run(xs, outs)
+    torch.cuda.synchronize()
+    for x, o in zip(xs, outs):
+        assert torch.equal(o, blk(x.cuda(), inp.timestep, (inp.cos, inp.sin)).cpu())
