@@ -6,21 +6,24 @@
 // [B, L, H, d], scale d^-0.5, no mask).
 //
 // One CTA per (256-query block, head, batch), 12 warps:
-//   warp 0        TMA producer: Q (2 tiles x 128 rows, once), then K/V tiles
-//                 of 128 keys through a 2-deep ring (128-byte swizzle)
-//   warp 1        MMA issuer:   S_q = Q_q K^T (tcgen05 kind::f16, both operands
-//                 in shared memory) and O_q += P_q V (P read straight from
-//                 TMEM, V as an MN-major shared-memory operand)
+//   warp 0        TMA producer: Q (2 tiles x 128 rows, once), then K and V
+//                 tiles of 64 keys through 4-deep rings (128-byte swizzle)
+//   warp 1        MMA issuer:   S_q = Q_q K^T (tcgen05 kind::f16, M=128 N=64,
+//                 both operands in shared memory) and O_q += P_q V (M=128
+//                 N=128, P read straight from TMEM, V an MN-major operand)
 //   warps 4..7    softmax for Q tile 0; warps 8..11 for Q tile 1.  Each thread
-//                 owns one query row: it reads its 128 scores from TMEM, keeps
-//                 a running max/sum, writes P (bf16) back into TMEM over the
-//                 consumed scores, rescales its O row in TMEM when the max grew
-//                 by more than 2^8, and finally normalises O and stores it.
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
-// P_q occupies the first 64 columns of S_q (two bf16 per 32-bit column).
-// The MMA order S0(j+1) after PV0(j) keeps the tensor pipe busy while the
-// other tile's softmax runs; tcgen05.mma operations issued by one thread
-// execute in issue order, which makes writing S0(j+1) over P0(j) safe.
+//                 owns one query row: it reads 64 scores from TMEM, keeps a
+//                 running max/sum, writes P (bf16) back over the consumed
+//                 scores, rescales its O row when the max grew by more than 2^8,
+//                 and finally normalises O and stores it.
+// TMEM (512 columns): O0 [0,128) O1 [128,256), then two 64-column score
+// buffers per Q tile: S0 [256,320) [320,384), S1 [384,448) [448,512); P of a
+// key tile occupies the first 32 columns of its score buffer.  With two score
+// buffers per tile the MMA issues S_q(j+2) right after PV_q(j), so the scores
+// of the next key tile are ready while the softmax of the current one runs and
+// the softmax, not the MMA chain, sets each tile's pace.  tcgen05.mma
+// operations issued by one thread execute in order, which makes writing
+// S_q(j+2) over P_q(j) safe.
 #pragma once
 
 #include "ogx_sm100.cuh"
@@ -32,12 +35,20 @@ namespace fmha {
 constexpr int HD = 128;
 constexpr int BQ = 128;
 constexpr int NQ = 2;
-constexpr int BKV = 128;
-constexpr int STAGES = 2;
-constexpr int HALF_BYTES = 128 * 64 * 2;  // one 64-column half of a 128-row tile
-constexpr int TILE_BYTES = 2 * HALF_BYTES;
-constexpr int SMEM_BYTES = (NQ + 2 * STAGES) * TILE_BYTES + 1024;
+constexpr int BKV = 64;
+constexpr int KV_STAGES = 4;
+constexpr int Q_HALF_BYTES = BQ * 64 * 2;      // 64-column half of a 128-row Q tile
+constexpr int Q_TILE_BYTES = 2 * Q_HALF_BYTES;
+constexpr int KV_HALF_BYTES = BKV * 64 * 2;    // 64-column half of a 64-row K/V tile
+constexpr int KV_TILE_BYTES = 2 * KV_HALF_BYTES;
+constexpr int SMEM_BYTES = NQ * Q_TILE_BYTES + 2 * KV_STAGES * KV_TILE_BYTES + 1024;
 constexpr int kThreads = 384;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t TMEM_O = 0;      // + 128 * q
+constexpr uint32_t TMEM_S = 256;    // + 128 * q + 64 * buffer
+// A row's running max only moves when a new score exceeds it by more than
+// this many log2 units, so P <= 2^8 and most key tiles need no O rescale.
+constexpr float kRescaleThreshold = 8.0f;
 // Register split (setmaxnreg): the kernel is launched with kLaunchRegs per thread (the host checks the
 // built count before launching); warpgroup 0 (TMA / MMA) drops to kRegsProducer and the two softmax
 // warpgroups rise to kRegsSoftmax.  The split must fit in what the launch reserved, or the increase
@@ -46,10 +57,6 @@ constexpr int kLaunchRegs = 168;
 constexpr uint32_t kRegsProducer = 96;
 constexpr uint32_t kRegsSoftmax = 200;
 static_assert(128 * kRegsProducer + 256 * kRegsSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
-constexpr uint32_t TMEM_COLS = 512;
-// A row's running max only moves when a new score exceeds it by more than
-// this many log2 units, so P <= 2^8 and most tiles need no O rescale.
-constexpr float kRescaleThreshold = 8.0f;
 
 struct Params {
   int L;             // tokens (keys == queries)
@@ -62,11 +69,12 @@ struct Params {
 
 struct SharedState {
   uint64_t q_full;
-  uint64_t k_full[STAGES], k_empty[STAGES];
-  uint64_t v_full[STAGES], v_empty[STAGES];
-  uint64_t s_full[NQ];
-  uint64_t p_full[NQ];
-  uint64_t o_done[NQ];
+  uint64_t k_full[KV_STAGES], k_empty[KV_STAGES];
+  uint64_t v_full[KV_STAGES], v_empty[KV_STAGES];
+  uint64_t s_full[NQ][2];  // scores of tile q in buffer b are in TMEM
+  uint64_t p_full[NQ][2];  // P of tile q in buffer b is in TMEM (128 softmax threads arrive)
+  uint64_t o_ready[NQ];    // completes once per PV_q(j)
+  uint64_t o_done[NQ];     // the last PV_q completed
   uint64_t drained;
   uint32_t tmem_base;
   int abort;
@@ -77,25 +85,6 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-
-// 2^x on the FMA pipe, for the share of the exponentials the MUFU unit cannot
-// absorb at tensor-core rate.  x = j + f with j = round(x) taken from the bits of
-// x + 1.5*2^23 and f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted here to
-// 2^f on [-1/2, 1/2] (least squares on Chebyshev nodes with Lawson reweighting
-// towards minimax; max relative error 7.5e-5, far below bf16's 2^-9); 2^j is
-// added to the exponent field.  x is clamped at -126 (P rounds to 0 there).
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = x + 12582912.0f;  // 1.5 * 2^23: the low mantissa bits hold round(x)
-  const float f = x - (t - 12582912.0f);
-  float p = fmaf(0.0551716648f, f, 0.2426111251f);
-  p = fmaf(p, f, 0.6932609677f);
-  p = fmaf(p, f, 0.9999280572f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
-// Which 32-column chunks of a score row use the polynomial instead of the MUFU ex2.
-constexpr uint32_t kPolyChunkMask = 0x8u;
 
 // Packed two-lane fp32 arithmetic (sm_100 f32x2 instructions): one issue slot for two values.
 struct f2 {
@@ -132,7 +121,13 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// ex2_poly on two lanes with packed arithmetic (same polynomial and reduction).
+// 2^x on the FMA pipe (two lanes), for the share of the exponentials the MUFU
+// unit cannot absorb at tensor-core rate.  x = j + f with j = round(x) taken
+// from the bits of x + 1.5*2^23 and f in [-1/2, 1/2]; 2^f by a degree-3
+// polynomial fitted here to 2^f on [-1/2, 1/2] (least squares on Chebyshev
+// nodes with Lawson reweighting towards minimax; max relative error 7.5e-5, far
+// below bf16's 2^-9); 2^j is added to the exponent field.  x is clamped at -126
+// (P rounds to 0 there).
 __device__ __forceinline__ f2 ex2_poly2(f2 x) {
   const f2 magic{12582912.0f, 12582912.0f};
   x.x = fmaxf(x.x, -126.0f);
@@ -146,12 +141,15 @@ __device__ __forceinline__ f2 ex2_poly2(f2 x) {
             __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23))};
 }
 
-// Q/K/V tensor maps are 4-D {d (128), head, token, batch} with a box of
-// {64, 1, 128, 1}: one 64-column half of a 128-row tile, 128-byte swizzled.
-__device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int head, int row0,
-                                          int batch) {
+// Which 16-column chunks of a 64-score row use the polynomial instead of the MUFU ex2.
+constexpr uint32_t kPolyChunkMask = 0x8u;
+
+// Q/K/V tensor maps are 4-D {d (128), head, token, batch}; a box is one
+// 64-column half of a row tile (128 rows for Q, 64 for K/V), 128-byte swizzled.
+__device__ __forceinline__ void load_rows(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int half_bytes, int head,
+                                          int row0, int batch) {
   tma_load_4d(dst, map, bar, 0, head, row0, batch);
-  tma_load_4d(dst + HALF_BYTES, map, bar, 64, head, row0, batch);
+  tma_load_4d(dst + half_bytes, map, bar, 64, head, row0, batch);
 }
 
 template <bool OUT_E4M3>
@@ -162,10 +160,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ SharedState st;
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (smem_base - smem_u32(smem_raw));
-  // [Q0][Q1][K stage 0][K stage 1][V stage 0][V stage 1], TILE_BYTES each
+  // [Q0][Q1][K stages][V stages]
   uint8_t* q_tiles = smem;
-  uint8_t* k_tiles = smem + NQ * TILE_BYTES;
-  uint8_t* v_tiles = smem + (NQ + STAGES) * TILE_BYTES;
+  uint8_t* k_tiles = smem + NQ * Q_TILE_BYTES;
+  uint8_t* v_tiles = k_tiles + KV_STAGES * KV_TILE_BYTES;
 
   const uint32_t warp = warp_idx();
   const uint32_t lane = threadIdx.x & 31;
@@ -176,15 +174,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&st.q_full, 1);
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&st.k_full[s], 1);
       mbar_init(&st.k_empty[s], 1);
       mbar_init(&st.v_full[s], 1);
       mbar_init(&st.v_empty[s], 1);
     }
     for (int q = 0; q < NQ; ++q) {
-      mbar_init(&st.s_full[q], 1);
-      mbar_init(&st.p_full[q], 128);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&st.s_full[q][b], 1);
+        mbar_init(&st.p_full[q][b], 128);
+      }
+      mbar_init(&st.o_ready[q], 1);
       mbar_init(&st.o_done[q], 1);
     }
     mbar_init(&st.drained, 1);
@@ -208,28 +209,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      mbar_arrive_expect_tx(&st.q_full, NQ * TILE_BYTES);
-      for (int q = 0; q < NQ; ++q) load_tile(q_tiles + q * TILE_BYTES, &tq, &st.q_full, head, q_block0 + q * BQ, batch);
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
-        if (!mbar_wait(&st.k_empty[s], ph ^ 1u, abort)) { ok = false; break; }
-        mbar_arrive_expect_tx(&st.k_full[s], TILE_BYTES);
-        load_tile(k_tiles + s * TILE_BYTES, &tk, &st.k_full[s], head, j * BKV, batch);
-        if (!mbar_wait(&st.v_empty[s], ph ^ 1u, abort)) { ok = false; issued = 2 * j + 1; break; }
-        mbar_arrive_expect_tx(&st.v_full[s], TILE_BYTES);
-        load_tile(v_tiles + s * TILE_BYTES, &tv, &st.v_full[s], head, j * BKV, batch);
-        issued = 2 * j + 2;
+      mbar_arrive_expect_tx(&st.q_full, NQ * Q_TILE_BYTES);
+      for (int q = 0; q < NQ; ++q)
+        load_rows(q_tiles + q * Q_TILE_BYTES, &tq, &st.q_full, Q_HALF_BYTES, head, q_block0 + q * BQ, batch);
+      int issued = 0;  // K/V tile loads issued (K of tile j is 2j, V is 2j+1)
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!mbar_wait(&st.k_empty[s], ph ^ 1u, abort)) break;
+        mbar_arrive_expect_tx(&st.k_full[s], KV_TILE_BYTES);
+        load_rows(k_tiles + s * KV_TILE_BYTES, &tk, &st.k_full[s], KV_HALF_BYTES, head, j * BKV, batch);
+        ++issued;
+        if (!mbar_wait(&st.v_empty[s], ph ^ 1u, abort)) break;
+        mbar_arrive_expect_tx(&st.v_full[s], KV_TILE_BYTES);
+        load_rows(v_tiles + s * KV_TILE_BYTES, &tv, &st.v_full[s], KV_HALF_BYTES, head, j * BKV, batch);
+        ++issued;
       }
-      if (!ok) {
+      if (*abort) {
         // let the copies already in flight land before the CTA exits
         mbar_wait(&st.q_full, 0, nullptr);
         const int last_j = (issued - 1) / 2;
-        for (int j = last_j; j >= 0 && j > last_j - STAGES; --j) {
-          const int s = j % STAGES;
-          const uint32_t ph = (j / STAGES) & 1;
+        for (int j = last_j; j >= 0 && j > last_j - KV_STAGES; --j) {
+          const int s = j % KV_STAGES;
+          const uint32_t ph = (j / KV_STAGES) & 1;
           mbar_wait(&st.k_full[s], ph, nullptr);
           if (2 * j + 1 < issued) mbar_wait(&st.v_full[s], ph, nullptr);
         }
@@ -241,56 +243,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t q_addr = smem_u32(q_tiles);
       const uint32_t k_addr = smem_u32(k_tiles);
       const uint32_t v_addr = smem_u32(v_tiles);
-      bool ok = mbar_wait(&st.q_full, 0, abort);
-      auto issue_s = [&](int q, int s) {
-        const uint32_t qa = q_addr + q * TILE_BYTES;
-        const uint32_t ka = k_addr + s * TILE_BYTES;
+      auto issue_s = [&](int q, int j) {  // S_q(j) into score buffer j % 2
+        const uint32_t qa = q_addr + q * Q_TILE_BYTES;
+        const uint32_t ka = k_addr + (j % KV_STAGES) * KV_TILE_BYTES;
+        const uint32_t d = tmem + TMEM_S + q * 128 + (j & 1) * 64;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-          mma_f16_ss(tmem + q * 128, make_sdesc_sw128(qa + off, 16, 1024), make_sdesc_sw128(ka + off, 16, 1024),
-                     idesc_qk, kk > 0 ? 1u : 0u);
+          const uint32_t qoff = (kk >> 2) * Q_HALF_BYTES + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * KV_HALF_BYTES + (kk & 3) * 32;
+          mma_f16_ss(d, make_sdesc_sw128(qa + qoff, 16, 1024), make_sdesc_sw128(ka + koff, 16, 1024), idesc_qk,
+                     kk > 0 ? 1u : 0u);
         }
-        mma_commit(&st.s_full[q]);
+        mma_commit(&st.s_full[q][j & 1]);
       };
-      auto issue_pv = [&](int q, int s, bool accumulate, bool last) {
-        const uint32_t va = v_addr + s * TILE_BYTES;
+      auto issue_pv = [&](int q, int j) {  // O_q += P_q(j) V(j)
+        const uint32_t va = v_addr + (j % KV_STAGES) * KV_TILE_BYTES;
+        const uint32_t pa = tmem + TMEM_S + q * 128 + (j & 1) * 64;
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          mma_f16_ts(tmem + 256 + q * 128, tmem + q * 128 + kk * 8, make_sdesc_sw128(va + kk * 2048, HALF_BYTES, 1024),
-                     idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + TMEM_O + q * 128, pa + kk * 8, make_sdesc_sw128(va + kk * 2048, KV_HALF_BYTES, 1024),
+                     idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        if (last) mma_commit(&st.o_done[q]);  // O_q is final once this fires
+        mma_commit(&st.o_ready[q]);
+        if (j + 1 == nkv) mma_commit(&st.o_done[q]);
       };
-      if (ok && mbar_wait(&st.k_full[0], 0, abort)) {
+      bool ok = mbar_wait(&st.q_full, 0, abort);
+      // prologue: the scores of key tiles 0 and 1
+      for (int j = 0; j < 2 && j < nkv && ok; ++j) {
+        const int s = j % KV_STAGES;
+        if (!mbar_wait(&st.k_full[s], (j / KV_STAGES) & 1, abort)) { ok = false; break; }
         tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        mma_commit(&st.k_empty[0]);
-      } else {
-        ok = false;
+        issue_s(0, j);
+        issue_s(1, j);
+        mma_commit(&st.k_empty[s]);
       }
       for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
-        const int sn = (j + 1) % STAGES;
-        const uint32_t phn = ((j + 1) / STAGES) & 1;
-        const bool has_next = j + 1 < nkv;
-        if (!mbar_wait(&st.v_full[s], ph, abort) || !mbar_wait(&st.p_full[0], j & 1, abort)) { ok = false; break; }
+        const int s = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        const uint32_t pph = (j >> 1) & 1;
+        const int j2 = j + 2;
+        const int s2 = j2 % KV_STAGES;
+        if (!mbar_wait(&st.v_full[s], ph, abort) || !mbar_wait(&st.p_full[0][j & 1], pph, abort)) { ok = false; break; }
         tc_fence_after();
-        issue_pv(0, s, j > 0, !has_next);
-        if (has_next) {
-          if (!mbar_wait(&st.k_full[sn], phn, abort)) { ok = false; break; }
+        issue_pv(0, j);
+        if (j2 < nkv) {
+          if (!mbar_wait(&st.k_full[s2], (j2 / KV_STAGES) & 1, abort)) { ok = false; break; }
           tc_fence_after();
-          issue_s(0, sn);
+          issue_s(0, j2);
         }
-        if (!mbar_wait(&st.p_full[1], j & 1, abort)) { ok = false; break; }
+        if (!mbar_wait(&st.p_full[1][j & 1], pph, abort)) { ok = false; break; }
         tc_fence_after();
-        issue_pv(1, s, j > 0, !has_next);
+        issue_pv(1, j);
         mma_commit(&st.v_empty[s]);
-        if (has_next) {
-          issue_s(1, sn);
-          mma_commit(&st.k_empty[sn]);
+        if (j2 < nkv) {
+          issue_s(1, j2);
+          mma_commit(&st.k_empty[s2]);
         }
       }
       mma_commit(&st.drained);
@@ -303,29 +310,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t quarter = warp & 3;        // TMEM lane quarter of this warp
     const int row = quarter * 32 + lane;      // row within the Q tile
     const uint32_t lane_off = (quarter * 32u) << 16;
-    const uint32_t s_tmem = tmem + lane_off + q * 128;
-    const uint32_t o_tmem = tmem + lane_off + 256 + q * 128;
+    const uint32_t o_tmem = tmem + lane_off + TMEM_O + q * 128;
     const float c = p.scale_log2;
     float m_run = -INFINITY;  // running max, already multiplied by c
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait(&st.s_full[q], j & 1, abort)) { ok = false; break; }
+      const int b = j & 1;
+      const uint32_t s_tmem = tmem + lane_off + TMEM_S + q * 128 + b * 64;
+      if (!mbar_wait(&st.s_full[q][b], (j >> 1) & 1, abort)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sr[128];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) tmem_ld32(s_tmem + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
+      uint32_t sr[64];
+      tmem_ld32(s_tmem, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
       tmem_ld_wait();
       float* sf = reinterpret_cast<float*>(sr);
       const int kv_valid = p.L - j * BKV;
       if (kv_valid < BKV) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
+        for (int i = 0; i < BKV; ++i)
           if (i >= kv_valid) sf[i] = -INFINITY;
       }
-      float mx = fmaxf(sf[0], sf[127]);
+      float mx = fmaxf(sf[0], sf[63]);
 #pragma unroll
-      for (int i = 1; i < 127; i += 2) mx = max3(mx, sf[i], sf[i + 1]);
+      for (int i = 1; i < 63; i += 2) mx = max3(mx, sf[i], sf[i + 1]);
       const float m_tile = mx * c;
       float m_use = m_run;
       float alpha = 1.f;
@@ -342,38 +350,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       const f2 negm{-m_use, -m_use};
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
-        uint32_t pk[16];
+        uint32_t pk[8];
         const bool poly = (kPolyChunkMask >> cc) & 1u;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const f2 a = fma2(f2{sf[cc * 32 + 2 * i], sf[cc * 32 + 2 * i + 1]}, c2, negm);
+        for (int i = 0; i < 8; ++i) {
+          const f2 a = fma2(f2{sf[cc * 16 + 2 * i], sf[cc * 16 + 2 * i + 1]}, c2, negm);
           const f2 pr = poly ? ex2_poly2(a) : f2{ex2(a.x), ex2(a.y)};
           rowsum2 = add2(rowsum2, pr);
-          __nv_bfloat162 b2 = __floats2bfloat162_rn(pr.x, pr.y);
-          pk[i] = *reinterpret_cast<uint32_t*>(&b2);
+          pk[i] = pack_bf16x2(pr.x, pr.y);
         }
-        // P chunk cc -> TMEM columns [16cc, 16cc+16) of S_q (all of S is already in registers)
-        tmem_st16(s_tmem + cc * 16, pk);
+        // P chunk cc -> TMEM columns [8cc, 8cc+8) of this score buffer (all scores are in registers)
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(s_tmem + cc * 8),
+            "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]), "r"(pk[7])
+            : "memory");
       }
-      const float rowsum = rowsum2.x + rowsum2.y;
-      l_run = l_run * alpha + rowsum;
+      l_run = l_run * alpha + (rowsum2.x + rowsum2.y);
       m_run = m_use;
       if (__any_sync(0xffffffffu, rescale)) {
-        // O already holds PV(j-1): S_q(j) was issued after PV_q(j-1), and the commit that
-        // fired s_full tracks every tcgen05 operation issued before it.
+        // O must hold PV_q(j-1) before it is rescaled.  o_ready completes once per PV_q; S_q(j) was
+        // issued after PV_q(j-2), so it is at most one phase behind phase j-1 here.
+        if (!mbar_wait(&st.o_ready[q], (j - 1) & 1, abort)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int oc = 0; oc < 4; ++oc) {
           uint32_t orr[32];
-          tmem_ld32(o_tmem + cc * 32, orr);
+          tmem_ld32(o_tmem + oc * 32, orr);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
-          tmem_st32(o_tmem + cc * 32, orr);
+          tmem_st32(o_tmem + oc * 32, orr);
         }
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&st.p_full[q]);
+      mbar_arrive(&st.p_full[q][b]);
     }
     if (ok && mbar_wait(&st.o_done[q], 0, abort)) {
       tc_fence_after();
@@ -385,14 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         qr = __frcp_rn(qs);
       }
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int oc = 0; oc < 4; ++oc) {
         uint32_t orr[32];
-        tmem_ld32(o_tmem + cc * 32, orr);
+        tmem_ld32(o_tmem + oc * 32, orr);
         tmem_ld_wait();
         if (token < p.L) {
           const int64_t base = static_cast<int64_t>(batch) * p.out_stride_b +
                                static_cast<int64_t>(token) * p.out_stride_t + static_cast<int64_t>(head) * HD +
-                               cc * 32;
+                               oc * 32;
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             float f[8];

@@ -456,12 +456,13 @@ int attention_common(const void* q, const void* k, const void* v, int64_t batch,
   const uint64_t dims[4] = {128, static_cast<uint64_t>(heads), static_cast<uint64_t>(tokens),
                             static_cast<uint64_t>(batch)};
   const uint64_t strides[3] = {256, static_cast<uint64_t>(stride_t) * 2, static_cast<uint64_t>(stride_b) * 2};
-  const uint32_t box[4] = {64, 1, 128, 1};
-  int rc = make_map(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, q, dims, strides, box);
+  const uint32_t qbox[4] = {64, 1, static_cast<uint32_t>(ogx::fmha::BQ), 1};
+  const uint32_t kvbox[4] = {64, 1, static_cast<uint32_t>(ogx::fmha::BKV), 1};
+  int rc = make_map(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, q, dims, strides, qbox);
   if (rc) return rc;
-  rc = make_map(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k, dims, strides, box);
+  rc = make_map(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k, dims, strides, kvbox);
   if (rc) return rc;
-  return make_map(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v, dims, strides, box);
+  return make_map(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v, dims, strides, kvbox);
 }
 
 template <bool E4M3>
