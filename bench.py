@@ -187,14 +187,14 @@ def run_reference_arm(args) -> None:
         "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_block"], "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16/e4m3 (fp32 on CPU)", "data": "synthetic",
-        "config": config_dict(args.config, args.gpus),
+        "config": config_dict(args.config, args.gpus, args.exchange, graph=False),
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def config_dict(name: str, n: int) -> dict:
+def config_dict(name: str, n: int, exchange: str = "nvlink", graph: bool = True) -> dict:
     from opengenie_b200 import synthetic
 
     cfg = synthetic.CONFIGS[name]
@@ -203,8 +203,9 @@ def config_dict(name: str, n: int) -> dict:
         "tokens": cfg.tokens, "latent_grid": [cfg.frames, cfg.grid_h, cfg.grid_w], "hidden": 4096, "heads": 32,
         "head_dim": 128, "batch": 1, "qkv_out_proj": "e4m3 per-tensor scales, fp32 accumulate",
         "attention": "bf16, fp32 softmax/accumulate", "per_token_timestep": cfg.per_token_timestep,
-        "parallelism": "single GPU" if n == 1 else f"ulysses heads {32 // n}/GPU",
+        "parallelism": "single GPU" if n == 1 else f"ulysses heads {32 // n}/GPU, {exchange} exchange",
         "l2": "inputs larger than L2 (x 75 MB + weights 67 MB + cos/sin 75 MB read per block)",
+        "launch": "one CUDA graph replay per step" if graph else "eager launches",
     }
 
 
@@ -217,6 +218,10 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c1_l9216")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="issue each step's launches eagerly")
+    ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
+                    help="N>1: peer stores over NVLink from the producing kernels, or NCCL all-to-alls")
+    ap.add_argument("--phases", action="store_true", help="add a per-stage time breakdown (separate, untimed run)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -239,23 +244,37 @@ def main() -> None:
         blk = VideoSelfAttentionBlock(w, dev)
         blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
         launches_per_step = 5
+        out_dev = torch.empty_like(inp.x)
 
-        def step(x):
-            return blk(x, inp.timestep, (inp.cos, inp.sin))
+        def step():
+            blk(inp.x, inp.timestep, (inp.cos, inp.sin), out=out_dev)
     else:
         from opengenie_b200.ulysses import UlyssesVideoSelfAttention
 
-        blk = UlyssesVideoSelfAttention(w, dev, pg)
+        blk = UlyssesVideoSelfAttention(w, dev, pg, exchange=args.exchange)
         blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
         launches_per_step = blk.kernel_launches_per_step
+        x_loc = blk.local_slice(inp.x)
+        out_dev = torch.empty_like(x_loc)
 
-        def step(x):
-            return blk(x, inp.timestep, (inp.cos, inp.sin))
+        def step():
+            blk.forward_local(x_loc, inp.timestep, (inp.cos, inp.sin), out=out_dev)
 
+    # the step as one CUDA graph replay (NCCL's all-to-alls stay eager)
+    use_graph = not args.no_graph and (world == 1 or args.exchange == "nvlink")
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
-        step(inp.x)
+        step()
     torch.cuda.synchronize(dev)
+    run_step = step
+    if use_graph:
+        from opengenie_b200.graphs import StepGraph
+
+        graph = StepGraph(step, dev)
+        run_step = graph.replay
+        for _ in range(2):
+            run_step()
+        torch.cuda.synchronize(dev)
     if _lib.device_status(clear=True):
         raise SystemExit("device status reported a timed-out wait during warm-up")
 
@@ -266,7 +285,7 @@ def main() -> None:
     with ClockSampler(local) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
-            step(inp.x)
+            run_step()
         ev1.record(stream)
         torch.cuda.synchronize(dev)
     barrier(pg)
@@ -285,7 +304,7 @@ def main() -> None:
     else:
         def host_step(xd, yd):
             blk.forward_local(xd, inp.timestep, (inp.cos, inp.sin), out=yd)
-    pipe = HostPipeline(host_step, tuple(x_host.shape), x_host.dtype, dev)
+    pipe = HostPipeline(host_step, tuple(x_host.shape), x_host.dtype, dev, graphs=use_graph)
     pipe.run([x_host] * 2, out_hosts)  # warm-up
     torch.cuda.synchronize(dev)
     barrier(pg)
@@ -304,6 +323,13 @@ def main() -> None:
     # ---- dominant kernel (attention) timed alone on the launching stream
     attn_ms = blk.time_attention(args.steps, args.warmup) if hasattr(blk, "time_attention") else None
     attn_ms = max_over_ranks(attn_ms, pg) if attn_ms is not None else None
+    phases = None
+    if args.phases and hasattr(blk, "phase_summary"):
+        blk.profile = True
+        for _ in range(5):
+            step()
+        blk.profile = False
+        phases = blk.phase_summary()
     status = _lib.device_status(clear=True)
 
     if rank == 0:
@@ -322,7 +348,7 @@ def main() -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "us_per_block": ms * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 attention / e4m3 projections",
-            "data": "synthetic (seeded inputs, random-init weights)", "config": config_dict(args.config, world),
+            "data": "synthetic (seeded inputs, random-init weights)", "config": config_dict(args.config, world, args.exchange, use_graph),
             "roofline": {
                 "bound": "tensor", "kernel": "fmha_fwd_kernel (attention, dominant)",
                 "achieved": achieved, "peak": peaks.get("bf16_tflops"), "unit": "TFLOP/s",
@@ -337,6 +363,8 @@ def main() -> None:
             "clocks": clk.summary(),
             "device_status": status,
         }
+        if phases is not None:
+            line["phases_ms"] = phases
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_reference(args.config, 2, 0, budget_s=20.0)
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}

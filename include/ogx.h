@@ -172,6 +172,43 @@ int ogx_attention_fwd_e4m3(const void* q, const void* k, const void* v, int64_t 
                            const float* out_scale, void* out_q, int64_t out_stride_b, int64_t out_stride_t,
                            void* stream);
 
+/* ---- Sequence-parallel exchange over NVLink (no reference counterpart: the reference is single-GPU).
+ * Buffers are shared between the ranks' processes with CUDA IPC; the producing kernels store straight
+ * into the destination GPU's receive buffer and a bounded-wait barrier kernel orders producer and
+ * consumer.  No NVLink multicast is used. */
+
+/* IPC handle (64 bytes) of the allocation holding ptr, and ptr's offset in it. */
+int ogx_ipc_get_handle(const void* ptr, void* handle, int64_t* offset);
+/* Maps a peer's allocation into this process; *base + offset addresses the peer's buffer. */
+int ogx_ipc_open_handle(const void* handle, void** base);
+int ogx_ipc_close_handle(void* base);
+
+/* Cross-GPU barrier.  Each rank's signal block is 16 zero-initialised uint32 words in its own memory
+ * ([0,8) arrival slots, [8] the count of barriers passed), mapped into the peers with IPC
+ * (peer_signals[i] = rank i's block).  Barrier e = count + 1: stores e into slot `rank` of every peer's
+ * block and waits, bounded, until every peer's slot in local_signals reaches e, then advances the count.
+ * The arguments are the same on every call, so steps containing barriers can be captured in a CUDA
+ * graph.  All ranks must run the same barriers in the same order.  One 32-thread launch. */
+int ogx_peer_barrier(unsigned int* local_signals, void* const* peer_signals, int rank, int world, void* stream);
+
+/* ogx_video_qkv_rmsnorm_rope_scatter with one destination base per head group (groups = world size):
+ * head h of token t goes to group_bases[h / (32/groups)] + t*out_stride_t + {0, 1, 2}*(32/groups)*128
+ * (q, k, v) + (h % (32/groups))*128, stored over NVLink when the base is a peer's receive buffer;
+ * the kernel fences its stores system-wide before it exits. */
+int ogx_video_qkv_rmsnorm_rope_to_peers(const void* q, const void* k, const void* v, int64_t tokens,
+                                        int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                        int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
+                                        int64_t cs_stride_h, int64_t cs_stride_t, void* const* group_bases,
+                                        int groups, int64_t out_stride_t, void* stream);
+
+/* ogx_attention_fwd_e4m3 (batch 1) whose output row for token t goes to
+ * peer_bases[t / tokens_per_peer] + (t % tokens_per_peer)*out_stride_t + head*128 (the receive buffers
+ * of the head-to-sequence exchange, stored over NVLink); stores are fenced system-wide. */
+int ogx_attention_fwd_e4m3_to_peers(const void* q, const void* k, const void* v, int64_t tokens, int64_t heads,
+                                    int64_t stride_t, float softmax_scale, const float* out_scale,
+                                    void* const* peer_bases, int peers, int64_t tokens_per_peer,
+                                    int64_t out_stride_t, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

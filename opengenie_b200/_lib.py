@@ -69,6 +69,18 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_float,
         c_void_p, c_void_p, c_int64, c_int64, c_void_p,
     ],
+    "ogx_ipc_get_handle": [c_void_p, c_void_p, ctypes.POINTER(c_int64)],
+    "ogx_ipc_open_handle": [c_void_p, ctypes.POINTER(c_void_p)],
+    "ogx_ipc_close_handle": [c_void_p],
+    "ogx_peer_barrier": [c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "ogx_video_qkv_rmsnorm_rope_to_peers": [
+        c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p,
+        c_void_p, c_int, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p,
+    ],
+    "ogx_attention_fwd_e4m3_to_peers": [
+        c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_int, c_int64,
+        c_int64, c_void_p,
+    ],
 }
 
 EXPORTED = tuple(sorted(list(_SIGNATURES) + ["ogx_last_error"]))
@@ -110,8 +122,11 @@ def call(name: str, *args) -> None:
         raise OgxError(f"{name}: {msg}" if msg else f"{name}: error {rc}")
 
 
+OGX_ERR_TIMEOUT = 1  # device status bit: a bounded device-side wait gave up
+
+
 def device_status(clear: bool = True) -> int:
-    """Device status word (bit 1: a bounded device-side wait timed out)."""
+    """Device status word (bit OGX_ERR_TIMEOUT: a bounded device-side wait timed out)."""
     lib = load()
     v = c_uint(0)
     rc = lib.ogx_device_status(ctypes.byref(v), 1 if clear else 0)

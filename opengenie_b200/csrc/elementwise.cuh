@@ -414,11 +414,11 @@ __global__ void __launch_bounds__(256) residual_gate_bias_kernel(ResidualArgs a)
 // One warp per token.  Lane l holds vectors v = 32*j + l (8 columns each); the
 // partner half of the same head sits in lane l ^ 8, reached with a shuffle.
 //
-// Outputs are addressed per (token, head): out + t*out_stride_t +
-// (h / heads_per_group)*out_stride_g + (h % heads_per_group)*128 + d, which
-// is the plain [L, 4096] layout for heads_per_group = 32 and the per-rank
-// send layout of the sequence-to-head exchange otherwise.  V (optional) is
-// copied through the same addressing.
+// Outputs are addressed per (token, head) through a table of group bases:
+// dst[j][h / heads_per_group] + t*out_stride_t + (h % heads_per_group)*128 + d,
+// which is the plain [L, 4096] layout for heads_per_group = 32 and, with one
+// base per GPU, the receive buffers of the sequence-to-head exchange written
+// directly over NVLink.  V (optional) is copied through the same addressing.
 struct RopeArgs {
   const __nv_bfloat16* q;
   const __nv_bfloat16* k;
@@ -431,17 +431,19 @@ struct RopeArgs {
   int64_t cs_stride_h, cs_stride_t;  // elements; innermost stride 1
   int64_t tokens;
   float eps;
-  __nv_bfloat16* q_out;
-  __nv_bfloat16* k_out;
-  __nv_bfloat16* v_out;  // optional
-  int64_t out_stride_t, out_stride_g;
+  // Destination of head h of tensor j (0 q, 1 k, 2 v) for token t:
+  // dst[j][h / heads_per_group] + t * out_stride_t + (h % heads_per_group) * 128.
+  // The group bases may point into other GPUs' memory (peer stores over NVLink).
+  __nv_bfloat16* dst[3][8];
+  int64_t out_stride_t;
   int heads_per_group;
+  int copy_v;        // also copy v (dst[2] valid)
+  int system_fence;  // fence the stores system-wide at exit (peer destinations)
 };
 
 template <typename WT, typename CsT>
 __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* in, const WT* w, const CsT* cosb,
-                                                 const CsT* sinb, const RopeArgs& a, int64_t t, float* red,
-                                                 __nv_bfloat16* outb) {
+                                                 const CsT* sinb, const RopeArgs& a, int64_t t, float* red, int j_out) {
   constexpr int VPT = 4096 / 8 / kRowThreads;  // 4
   const int tid = threadIdx.x;
   uint4 xv[VPT];
@@ -479,7 +481,7 @@ __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* in, const 
       o[i] = second ? fmaf(n[i], c[i], other[i] * s[i]) : fmaf(n[i], c[i], -(other[i] * s[i]));
     const int g = head / a.heads_per_group;
     const int hl = head - g * a.heads_per_group;
-    __nv_bfloat16* dst = outb + t * a.out_stride_t + g * a.out_stride_g + hl * 128 + (col & 127);
+    __nv_bfloat16* dst = a.dst[j_out][g] + t * a.out_stride_t + hl * 128 + (col & 127);
     *reinterpret_cast<uint4*>(dst) = pack8(o);
   }
 }
@@ -491,11 +493,9 @@ __global__ void __launch_bounds__(kRowThreads) qk_rmsnorm_rope_kernel(RopeArgs a
   const int64_t t = blockIdx.x;
   const CsT* cosb = static_cast<const CsT*>(a.cos);
   const CsT* sinb = static_cast<const CsT*>(a.sin);
-  rmsnorm_rope_row<WT, CsT>(a.q + t * a.in_stride_t, static_cast<const WT*>(a.q_weight), cosb, sinb, a, t, red[0],
-                            a.q_out);
-  rmsnorm_rope_row<WT, CsT>(a.k + t * a.in_stride_t, static_cast<const WT*>(a.k_weight), cosb, sinb, a, t, red[1],
-                            a.k_out);
-  if (a.v != nullptr && a.v_out != nullptr) {
+  rmsnorm_rope_row<WT, CsT>(a.q + t * a.in_stride_t, static_cast<const WT*>(a.q_weight), cosb, sinb, a, t, red[0], 0);
+  rmsnorm_rope_row<WT, CsT>(a.k + t * a.in_stride_t, static_cast<const WT*>(a.k_weight), cosb, sinb, a, t, red[1], 1);
+  if (a.copy_v) {
     const __nv_bfloat16* vin = a.v + t * a.in_stride_t;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -505,8 +505,14 @@ __global__ void __launch_bounds__(kRowThreads) qk_rmsnorm_rope_kernel(RopeArgs a
       const int g = head / a.heads_per_group;
       const int hl = head - g * a.heads_per_group;
       const uint4 val = __ldg(reinterpret_cast<const uint4*>(vin) + vec);
-      *reinterpret_cast<uint4*>(a.v_out + t * a.out_stride_t + g * a.out_stride_g + hl * 128 + (col & 127)) = val;
+      *reinterpret_cast<uint4*>(a.dst[2][g] + t * a.out_stride_t + hl * 128 + (col & 127)) = val;
     }
+  }
+  if (a.system_fence) {
+    // one system-scope fence per CTA, after the barrier: fences are cumulative, so it orders every
+    // thread's peer stores before the signal the next kernel releases
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
   }
 }
 

@@ -65,6 +65,11 @@ struct Params {
   uint8_t* out_q;      // e4m3 output (quantised with *out_scale, torch-path semantics)
   const float* out_scale;
   int64_t out_stride_b, out_stride_t;  // elements; the head stride is 128
+  // e4m3 output to other GPUs (sequence-parallel exchange): when peer_tokens > 0,
+  // token t's row goes to out_peer[t / peer_tokens] + (t % peer_tokens) * out_stride_t
+  // over NVLink instead of out_q.
+  uint8_t* out_peer[8];
+  int peer_tokens;
 };
 
 struct SharedState {
@@ -390,32 +395,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int token = q_block0 + q * BQ + row;
       const float inv_l = 1.f / l_run;
-      float qs = 0.f, qr = 0.f;
-      if (OUT_E4M3) {
-        qs = __ldg(p.out_scale);
-        qr = __frcp_rn(qs);
-      }
+      if constexpr (OUT_E4M3) {
+        // e4m3 rows are 128 bytes.  Each thread owns one row, so storing straight from registers
+        // would scatter 32 rows per instruction; instead the warp stages its 32 quantised rows in
+        // its quarter of this Q tile's shared memory (idle now: every S_q MMA completed before
+        // o_done) with 16-byte granules XOR-swizzled by row (conflict-free both ways), then stores
+        // whole rows, 8 lanes per row and 4 rows per instruction.  Full-line stores are what makes
+        // the peer path (NVLink) efficient.
+        const float qs = __ldg(p.out_scale);
+        const float qr = __frcp_rn(qs);
+        uint8_t* stage = q_tiles + q * Q_TILE_BYTES + quarter * 4096u;
 #pragma unroll 1
-      for (int oc = 0; oc < 4; ++oc) {
-        uint32_t orr[32];
-        tmem_ld32(o_tmem + oc * 32, orr);
-        tmem_ld_wait();
-        if (token < p.L) {
-          const int64_t base = static_cast<int64_t>(batch) * p.out_stride_b +
-                               static_cast<int64_t>(token) * p.out_stride_t + static_cast<int64_t>(head) * HD +
-                               oc * 32;
+        for (int oc = 0; oc < 4; ++oc) {
+          uint32_t orr[32];
+          tmem_ld32(o_tmem + oc * 32, orr);
+          tmem_ld_wait();
 #pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            float f[8];
+          for (int h = 0; h < 2; ++h) {
+            uint2 half[2];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(orr[v8 * 8 + i]) * inv_l;
-            const uint4 packed = pack8(f);
-            if (OUT_E4M3) {
-              float fb[8];
-              unpack8(packed, fb);
-              *reinterpret_cast<uint2*>(p.out_q + base + v8 * 8) = quant8<__nv_bfloat16, kQuantTorch>(fb, qs, qr);
+            for (int v8 = 0; v8 < 2; ++v8) {
+              float f[8], fb[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(orr[h * 16 + v8 * 8 + i]) * inv_l;
+              unpack8(pack8(f), fb);  // the attention output is bf16 before it is quantised
+              half[v8] = quant8<__nv_bfloat16, kQuantTorch>(fb, qs, qr);
+            }
+            const uint32_t gi = static_cast<uint32_t>(oc * 2 + h);
+            *reinterpret_cast<uint4*>(stage + lane * 128u + ((gi ^ (lane & 7u)) << 4)) =
+                make_uint4(half[0].x, half[0].y, half[1].x, half[1].y);
+          }
+        }
+        __syncwarp();
+        const uint32_t g = lane & 7u;
+#pragma unroll
+        for (int s8 = 0; s8 < 8; ++s8) {
+          const uint32_t r = static_cast<uint32_t>(s8 * 4) + (lane >> 3);
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 128u + ((g ^ (r & 7u)) << 4));
+          const int tok = q_block0 + q * BQ + static_cast<int>(quarter * 32u + r);
+          if (tok < p.L) {
+            uint8_t* dst;
+            if (p.peer_tokens > 0) {
+              const int d = tok / p.peer_tokens;
+              dst = p.out_peer[d] + static_cast<int64_t>(tok - d * p.peer_tokens) * p.out_stride_t;
             } else {
-              *reinterpret_cast<uint4*>(p.out + base + v8 * 8) = packed;
+              dst = p.out_q + static_cast<int64_t>(batch) * p.out_stride_b + static_cast<int64_t>(tok) * p.out_stride_t;
+            }
+            *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(head) * HD + g * 16u) = v;
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int oc = 0; oc < 4; ++oc) {
+          uint32_t orr[32];
+          tmem_ld32(o_tmem + oc * 32, orr);
+          tmem_ld_wait();
+          if (token < p.L) {
+            const int64_t base = static_cast<int64_t>(batch) * p.out_stride_b +
+                                 static_cast<int64_t>(token) * p.out_stride_t + static_cast<int64_t>(head) * HD +
+                                 oc * 32;
+#pragma unroll
+            for (int v8 = 0; v8 < 4; ++v8) {
+              float f[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(orr[v8 * 8 + i]) * inv_l;
+              *reinterpret_cast<uint4*>(p.out + base + v8 * 8) = pack8(f);
             }
           }
         }
@@ -423,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (OUT_E4M3 && p.peer_tokens > 0) __threadfence_system();  // peer stores visible before any signal
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

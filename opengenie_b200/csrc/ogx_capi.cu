@@ -18,6 +18,7 @@
 #include "elementwise.cuh"
 #include "fmha.cuh"
 #include "fp8_gemm.cuh"
+#include "peer.cuh"
 
 namespace {
 
@@ -58,6 +59,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
   });
   return fn;
 }
@@ -343,7 +357,7 @@ int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void*
   if (cos == nullptr || sin == nullptr) return fail(OGX_EINVAL, "rope_shape");
   if (tokens < 1) return fail(OGX_EINVAL, "empty_tokens");
   if (!dtype_ok(weight_dtype) || !dtype_ok(cs_dtype)) return fail(OGX_EINVAL, "qk_device_or_dtype");
-  if (heads_per_group < 1 || 32 % heads_per_group) return fail(OGX_EINVAL, "heads_per_group");
+  if (heads_per_group < 4 || 32 % heads_per_group) return fail(OGX_EINVAL, "heads_per_group");
   if (in_stride_t % 8 || out_stride_t % 8 || out_stride_g % 8) return fail(OGX_EINVAL, "qk_noncontiguous");
   const int cesz = cs_dtype == OGX_DTYPE_F32 ? 4 : 2;
   if ((cs_stride_h * cesz) % 16 || (cs_stride_t * cesz) % 16) return fail(OGX_EINVAL, "rope_shape");
@@ -364,12 +378,15 @@ int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void*
   a.cs_stride_t = cs_stride_t;
   a.tokens = tokens;
   a.eps = eps;
-  a.q_out = static_cast<__nv_bfloat16*>(q_out);
-  a.k_out = static_cast<__nv_bfloat16*>(k_out);
-  a.v_out = static_cast<__nv_bfloat16*>(v_out);
+  for (int g = 0; g < 32 / heads_per_group && g < 8; ++g) {
+    a.dst[0][g] = static_cast<__nv_bfloat16*>(q_out) + g * out_stride_g;
+    a.dst[1][g] = static_cast<__nv_bfloat16*>(k_out) + g * out_stride_g;
+    a.dst[2][g] = v_out ? static_cast<__nv_bfloat16*>(v_out) + g * out_stride_g : nullptr;
+  }
   a.out_stride_t = out_stride_t;
-  a.out_stride_g = out_stride_g;
   a.heads_per_group = heads_per_group;
+  a.copy_v = (v != nullptr && v_out != nullptr) ? 1 : 0;
+  a.system_fence = 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>(tokens));
   const int threads = ogx::kRowThreads;
@@ -603,8 +620,7 @@ int ogx_attention_fwd_e4m3(const void* q, const void* k, const void* v, int64_t 
   CUtensorMap mq, mk, mv;
   int rc = attention_common(q, k, v, batch, tokens, heads, head_dim, stride_b, stride_t, &mq, &mk, &mv);
   if (rc) return rc;
-  if (out_q == nullptr || out_scale == nullptr || (reinterpret_cast<uintptr_t>(out_q) & 7u) || out_stride_t % 8 ||
-      out_stride_b % 8)
+  if (out_q == nullptr || out_scale == nullptr || !aligned16(out_q) || out_stride_t % 16 || out_stride_b % 16)
     return fail(OGX_EINVAL, "output");
   ogx::fmha::Params p{};
   p.L = static_cast<int>(tokens);
@@ -614,6 +630,129 @@ int ogx_attention_fwd_e4m3(const void* q, const void* k, const void* v, int64_t 
   p.out_stride_b = out_stride_b;
   p.out_stride_t = out_stride_t;
   return attention_launch<true>(mq, mk, mv, batch, tokens, heads, p, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------- peer exchange over NVLink
+extern "C" {
+
+int ogx_ipc_get_handle(const void* ptr, void* handle, int64_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  auto fn = address_range_fn();
+  if (fn == nullptr) return fail(OGX_ECUDA, "cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(OGX_EINVAL, "pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  int rc = check_cuda(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle");
+  if (rc) return rc;
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return OGX_OK;
+}
+
+int ogx_ipc_open_handle(const void* handle, void** base) {
+  if (handle == nullptr || base == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int ogx_ipc_close_handle(void* base) {
+  if (base == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  return check_cuda(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+}
+
+int ogx_peer_barrier(unsigned int* local_signals, void* const* peer_signals, int rank, int world, void* stream) {
+  if (local_signals == nullptr || peer_signals == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (world < 1 || world > 8 || rank < 0 || rank >= world) return fail(OGX_EINVAL, "world");
+  ogx::PeerSignals ps{};
+  for (int i = 0; i < world; ++i) {
+    if (peer_signals[i] == nullptr) return fail(OGX_EINVAL, "null_pointer");
+    ps.slot[i] = static_cast<unsigned int*>(peer_signals[i]);
+  }
+  ogx::peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(local_signals, ps, rank, world);
+  return check_launch("peer_barrier_kernel");
+}
+
+int ogx_video_qkv_rmsnorm_rope_to_peers(const void* q, const void* k, const void* v, int64_t tokens,
+                                        int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                        int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
+                                        int64_t cs_stride_h, int64_t cs_stride_t, void* const* group_bases,
+                                        int groups, int64_t out_stride_t, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || group_bases == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (groups < 1 || groups > 8 || 32 % groups) return fail(OGX_EINVAL, "groups");
+  const int hpg = 32 / groups;
+  if (q_weight == nullptr || k_weight == nullptr) return fail(OGX_EINVAL, "qk_weight_shape");
+  if (cos == nullptr || sin == nullptr) return fail(OGX_EINVAL, "rope_shape");
+  if (tokens < 1) return fail(OGX_EINVAL, "empty_tokens");
+  if (!dtype_ok(weight_dtype) || !dtype_ok(cs_dtype)) return fail(OGX_EINVAL, "qk_device_or_dtype");
+  if (in_stride_t % 8 || out_stride_t % 8 || out_stride_t < 3 * hpg * 128) return fail(OGX_EINVAL, "qk_noncontiguous");
+  const int cesz = cs_dtype == OGX_DTYPE_F32 ? 4 : 2;
+  if ((cs_stride_h * cesz) % 16 || (cs_stride_t * cesz) % 16) return fail(OGX_EINVAL, "rope_shape");
+  ogx::RopeArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.in_stride_t = in_stride_t;
+  a.q_weight = q_weight;
+  a.k_weight = k_weight;
+  a.cos = cos;
+  a.sin = sin;
+  a.cs_stride_h = cs_stride_h;
+  a.cs_stride_t = cs_stride_t;
+  a.tokens = tokens;
+  a.eps = eps;
+  for (int g = 0; g < groups; ++g) {
+    if (group_bases[g] == nullptr || !aligned16(group_bases[g])) return fail(OGX_EINVAL, "alignment");
+    auto* base = static_cast<__nv_bfloat16*>(group_bases[g]);
+    a.dst[0][g] = base;
+    a.dst[1][g] = base + hpg * 128;
+    a.dst[2][g] = base + 2 * hpg * 128;
+  }
+  a.out_stride_t = out_stride_t;
+  a.heads_per_group = hpg;
+  a.copy_v = 1;
+  a.system_fence = 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(tokens));
+  const int threads = ogx::kRowThreads;
+  const bool wf = weight_dtype == OGX_DTYPE_F32;
+  const bool cf = cs_dtype == OGX_DTYPE_F32;
+  if (wf) {
+    if (cf) ogx::qk_rmsnorm_rope_kernel<float, float><<<grid, threads, 0, s>>>(a);
+    else ogx::qk_rmsnorm_rope_kernel<float, __nv_bfloat16><<<grid, threads, 0, s>>>(a);
+  } else {
+    if (cf) ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, float><<<grid, threads, 0, s>>>(a);
+    else ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, s>>>(a);
+  }
+  return check_launch("qk_rmsnorm_rope_kernel");
+}
+
+int ogx_attention_fwd_e4m3_to_peers(const void* q, const void* k, const void* v, int64_t tokens, int64_t heads,
+                                    int64_t stride_t, float softmax_scale, const float* out_scale,
+                                    void* const* peer_bases, int peers, int64_t tokens_per_peer,
+                                    int64_t out_stride_t, void* stream) {
+  CUtensorMap mq, mk, mv;
+  int rc = attention_common(q, k, v, 1, tokens, heads, 128, tokens * stride_t, stride_t, &mq, &mk, &mv);
+  if (rc) return rc;
+  if (peer_bases == nullptr || out_scale == nullptr || peers < 1 || peers > 8) return fail(OGX_EINVAL, "peers");
+  if (tokens_per_peer < 1 || tokens_per_peer * peers != tokens) return fail(OGX_EINVAL, "tokens_per_peer");
+  if (out_stride_t % 16 || out_stride_t < heads * 128) return fail(OGX_EINVAL, "output");
+  ogx::fmha::Params p{};
+  p.L = static_cast<int>(tokens);
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.out_scale = out_scale;
+  p.out_stride_t = out_stride_t;
+  p.peer_tokens = static_cast<int>(tokens_per_peer);
+  for (int i = 0; i < peers; ++i) {
+    if (peer_bases[i] == nullptr || !aligned16(peer_bases[i])) return fail(OGX_EINVAL, "output");
+    p.out_peer[i] = static_cast<uint8_t*>(peer_bases[i]);
+  }
+  p.out_q = p.out_peer[0];
+  return attention_launch<true>(mq, mk, mv, 1, tokens, heads, p, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

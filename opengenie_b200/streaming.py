@@ -17,8 +17,10 @@ import torch
 
 class HostPipeline:
     def __init__(self, fn: Callable[[torch.Tensor, torch.Tensor], torch.Tensor], shape, dtype, device,
-                 depth: int = 2):
-        """``fn(x_dev, out_dev)`` runs one step on the current stream, writing ``out_dev``."""
+                 depth: int = 2, graphs: bool = False):
+        """``fn(x_dev, out_dev)`` runs one step on the current stream, writing ``out_dev``.  With
+        ``graphs``, the step on each of the ``depth`` buffer pairs is captured once as a CUDA graph
+        (after one eager call, which initialises whatever ``fn`` sets up lazily) and replayed."""
         self.fn = fn
         self.device = torch.device(device)
         self.depth = depth
@@ -31,6 +33,15 @@ class HostPipeline:
         self.computed = [torch.cuda.Event() for _ in range(depth)]
         self.out_done = [torch.cuda.Event() for _ in range(depth)]
         self._used = [False] * depth
+        self.graphs = None
+        if graphs:
+            from .graphs import StepGraph
+
+            with torch.cuda.stream(self.comp):
+                for b in range(depth):
+                    self.x[b].zero_()
+                    fn(self.x[b], self.y[b])
+            self.graphs = [StepGraph(lambda b=b: fn(self.x[b], self.y[b]), self.device) for b in range(depth)]
 
     def run(self, inputs: Sequence[torch.Tensor], outputs: Sequence[torch.Tensor]) -> None:
         """Processes pinned host ``inputs[i]`` into pinned host ``outputs[i]``; asynchronous (returns
@@ -46,7 +57,10 @@ class HostPipeline:
                 self.comp.wait_event(self.in_ready[b])
                 if self._used[b]:
                     self.comp.wait_event(self.out_done[b])  # y[b] is free once step i-depth was copied out
-                self.fn(self.x[b], self.y[b])
+                if self.graphs is not None:
+                    self.graphs[b].replay()
+                else:
+                    self.fn(self.x[b], self.y[b])
                 self.computed[b].record(self.comp)
             with torch.cuda.stream(self.d2h):
                 self.d2h.wait_event(self.computed[b])

@@ -22,6 +22,8 @@ this module is the multi-GPU extension the block needs at 2/4/8 GPUs.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -73,20 +75,110 @@ class UlyssesPlan:
         return flat[..., :w], flat[..., w:2 * w], flat[..., 2 * w:]
 
 
+class PeerExchange:
+    """Receive buffers shared between the ranks' processes with CUDA IPC, and the cross-GPU barrier.
+
+    `share(t)` returns, for every rank, a device pointer to that rank's copy of ``t`` (the local
+    pointer for this rank, IPC mappings for the others), so kernels can store straight into a peer's
+    buffer over NVLink.  `barrier()` orders those stores before the peers read them (a bounded-wait
+    signal exchange, one 32-thread kernel on the current stream).
+    """
+
+    def __init__(self, group, device):
+        self._ct = ctypes
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        self._opened: dict[bytes, int] = {}
+        # [0, 8) arrival slots written by the peers, [8] barriers passed (advanced by the kernel)
+        self.signals = torch.zeros(16, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)  # zeroed before any peer can store into it
+        self.signal_ptrs = self.share(self.signals)
+        self._signal_arr = (ctypes.c_void_p * self.world)(*self.signal_ptrs)
+
+    def share(self, t: torch.Tensor) -> list[int]:
+        ct = self._ct
+        handle = (ct.c_char * 64)()
+        off = ct.c_int64(0)
+        _lib.call("ogx_ipc_get_handle", t.data_ptr(), handle, ct.byref(off))
+        gathered: list = [None] * self.world
+        dist.all_gather_object(gathered, (bytes(handle), int(off.value)), group=self.group)
+        ptrs = []
+        for r, (h, o) in enumerate(gathered):
+            if r == self.rank:
+                ptrs.append(t.data_ptr())
+                continue
+            base = self._opened.get(h)
+            if base is None:
+                b = ct.c_void_p()
+                _lib.call("ogx_ipc_open_handle", h, ct.byref(b))
+                base = self._opened[h] = int(b.value)
+            ptrs.append(base + o)
+        return ptrs
+
+    def barrier(self) -> None:
+        """Enqueues the barrier on the current stream (capturable: the epoch lives in device memory)."""
+        _lib.call("ogx_peer_barrier", self.signals.data_ptr(), self._signal_arr, self.rank, self.world,
+                  torch.cuda.current_stream(self.device).cuda_stream)
+
+    def close(self) -> None:
+        for base in self._opened.values():
+            _lib.call("ogx_ipc_close_handle", base)
+        self._opened.clear()
+
+
 class UlyssesVideoSelfAttention:
     """The video self-attention block sharded over the ranks of ``group`` (one GPU each)."""
 
-    kernel_launches_per_step = 5  # adazero+quant, QKV GEMM, RoPE scatter, attention, out-proj GEMM
 
-    def __init__(self, weights: BlockWeights, device, group=None):
+    def __init__(self, weights: BlockWeights, device, group=None, *, exchange: str = "nvlink"):
+        """``exchange``: "nvlink" (producer kernels store into the peers' receive buffers, shared with
+        CUDA IPC) or "nccl" (two all_to_all_single collectives)."""
+        if exchange not in ("nvlink", "nccl"):
+            raise ValueError(exchange)
         self.group = group
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
         self.plan = UlyssesPlan(world, rank, group=group)
+        self.exchange = exchange
+        self.peer = PeerExchange(group, device) if exchange == "nvlink" else None
+        # adazero+quant, QKV GEMM, RoPE, attention, out-proj GEMM (+ two peer barriers over NVLink)
+        self.kernel_launches_per_step = 7 if self.peer is not None else 5
         self.blk = VideoSelfAttentionBlock(weights, device)
         self.w = self.blk.w
         self.device = self.blk.device
         self._ws: dict[int, dict[str, torch.Tensor]] = {}
+        # (name, start, end) CUDA events per stage when profiling (as the reference's
+        # `_profile_video_msa_phase`, ltx_serve/triton_ltx_ops.py:2270-2279)
+        self.profile = False
+        self.phase_events: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+    def _phase(self, name: str):
+        """Context manager recording CUDA events around a stage on the current stream."""
+        blk = self
+
+        class _P:
+            def __enter__(self):
+                if blk.profile:
+                    self.e0 = torch.cuda.Event(enable_timing=True)
+                    self.e0.record()
+
+            def __exit__(self, *exc):
+                if blk.profile:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record()
+                    blk.phase_events.append((name, self.e0, e1))
+
+        return _P()
+
+    def phase_summary(self) -> dict[str, float]:
+        """Average ms per stage over the profiled calls (synchronises)."""
+        torch.cuda.synchronize(self.device)
+        acc: dict[str, list[float]] = {}
+        for name, e0, e1 in self.phase_events:
+            acc.setdefault(name, []).append(e0.elapsed_time(e1))
+        return {k: sum(v) / len(v) for k, v in acc.items()}
 
     # ------------------------------------------------------------------ buffers
     def workspace(self, tokens_local: int) -> dict[str, torch.Tensor]:
@@ -101,6 +193,14 @@ class UlyssesVideoSelfAttention:
                 "send2": torch.empty((L, p.heads_local * p.head_dim), device=self.device, dtype=torch.float8_e4m3fn),
                 "recv2": torch.empty(p.out_send_shape(tokens_local), device=self.device, dtype=torch.float8_e4m3fn),
             }
+            if self.peer is not None:
+                # where this rank's slot starts in every rank's receive buffers
+                slot1 = p.rank * tokens_local * 3 * p.heads_local * p.head_dim * 2
+                slot2 = p.rank * tokens_local * p.heads_local * p.head_dim
+                dst1 = [ptr + slot1 for ptr in self.peer.share(ws["recv1"])]
+                dst2 = [ptr + slot2 for ptr in self.peer.share(ws["recv2"])]
+                ws["recv1_dst"] = (ctypes.c_void_p * p.world)(*dst1)
+                ws["recv2_dst"] = (ctypes.c_void_p * p.world)(*dst2)
             self._ws[tokens_local] = ws
         return ws
 
@@ -113,17 +213,35 @@ class UlyssesVideoSelfAttention:
         w = self.w
         p = self.plan
         Ll = x_loc.shape[1]
-        xq = ltx_ops.fused_adazero_from_ada_fp8(x_loc, w.norm_eps, w.scale_shift_table, ts_loc, w.to_q.input_scale,
-                                                shift_index=0, scale_index=1)
+        with self._phase("adazero_quant"):
+            xq = ltx_ops.fused_adazero_from_ada_fp8(x_loc, w.norm_eps, w.scale_shift_table, ts_loc,
+                                                    w.to_q.input_scale, shift_index=0, scale_index=1)
         qkv = ws["qkv"]
         if qkv.shape != (Ll, 3 * 4096) or not qkv.is_contiguous():
             raise ValueError("qkv workspace shape")
-        ltx_ops.fp8_scaled_mm(xq, self.blk.w_qkv, w.to_q.input_scale, self.blk.s_qkv, bias=self.blk.b_qkv, out=qkv,
-                              n_per_scale=4096)
+        with self._phase("qkv_gemm"):
+            ltx_ops.fp8_scaled_mm(xq, self.blk.w_qkv, w.to_q.input_scale, self.blk.s_qkv, bias=self.blk.b_qkv,
+                                  out=qkv, n_per_scale=4096)
         send = ws["send1"]
         D = 4096
         if cos_loc.shape[2] != Ll or sin_loc.shape != cos_loc.shape or send.shape != p.qkv_send_shape(Ll):
             raise ValueError("rope_shape")
+        if self.peer is not None:
+            with self._phase("rope_to_peers"):
+                bases = ws["recv1_dst"]
+                _lib.call(
+                    "ogx_video_qkv_rmsnorm_rope_to_peers",
+                    qkv.data_ptr(), qkv[:, D:].data_ptr(), qkv[:, 2 * D:].data_ptr(), Ll, qkv.stride(0),
+                    w.q_norm_weight.data_ptr(), w.k_norm_weight.data_ptr(), ltx_ops._code(w.q_norm_weight),
+                    float(w.qk_eps), cos_loc.data_ptr(), sin_loc.data_ptr(), ltx_ops._code(cos_loc),
+                    cos_loc.stride(1), cos_loc.stride(2), bases, p.world, 3 * p.heads_local * p.head_dim,
+                    ltx_ops._stream(qkv),
+                )
+            with self._phase("barrier_seq_to_heads"):
+                self.peer.barrier()
+            return p.attention_views(ws["recv1"], Ll * p.world)
+        self._phase_ctx = self._phase("rope_scatter")
+        self._phase_ctx.__enter__()
         _lib.call(
             "ogx_video_qkv_rmsnorm_rope_scatter",
             qkv.data_ptr(), qkv[:, D:].data_ptr(), qkv[:, 2 * D:].data_ptr(), Ll, qkv.stride(0),
@@ -132,7 +250,9 @@ class UlyssesVideoSelfAttention:
             send[:, :, 0].data_ptr(), send[:, :, 1].data_ptr(), send[:, :, 2].data_ptr(), send.stride(1),
             send.stride(0), p.heads_local, ltx_ops._stream(qkv),
         )
-        p.exchange_qkv(send, ws["recv1"])
+        self._phase_ctx.__exit__(None, None, None)
+        with self._phase("exchange_seq_to_heads"):
+            p.exchange_qkv(send, ws["recv1"])
         return p.attention_views(ws["recv1"], Ll * p.world)
 
     def forward_local(self, x_loc: torch.Tensor, timestep: torch.Tensor, pe: tuple[torch.Tensor, torch.Tensor], *,
@@ -149,8 +269,23 @@ class UlyssesVideoSelfAttention:
         ws = self.workspace(Ll)
         q, k, v = self._qkv_and_exchange(x_loc, ts_loc, cos_loc, sin_loc, ws)
         send2 = ws["send2"]
-        ltx_ops.attention(q, k, v, p.heads_local, out=send2.view(1, L, -1), out_e4m3_scale=w.to_out.input_scale)
-        p.exchange_out(send2, ws["recv2"])
+        if self.peer is not None:
+            with self._phase("attention_to_peers"):
+                bases = ws["recv2_dst"]
+                _lib.call(
+                    "ogx_attention_fwd_e4m3_to_peers",
+                    q.data_ptr(), k.data_ptr(), v.data_ptr(), L, p.heads_local, q.stride(1), 128 ** -0.5,
+                    w.to_out.input_scale.data_ptr(), bases, p.world, Ll, p.heads_local * p.head_dim,
+                    ltx_ops._stream(q),
+                )
+            with self._phase("barrier_heads_to_seq"):
+                self.peer.barrier()
+        else:
+            with self._phase("attention"):
+                ltx_ops.attention(q, k, v, p.heads_local, out=send2.view(1, L, -1),
+                                  out_e4m3_scale=w.to_out.input_scale)
+            with self._phase("exchange_heads_to_seq"):
+                p.exchange_out(send2, ws["recv2"])
         if out is None:
             out = torch.empty_like(x_loc)
         ts_view = ltx_ops._ts_view(x_loc, w.scale_shift_table, ts_loc)
@@ -158,6 +293,8 @@ class UlyssesVideoSelfAttention:
         if (recv2.shape != p.out_send_shape(Ll) or ts_view.shape[1] != Ll or x_loc.shape != out.shape
                 or not out.is_contiguous()):
             raise ValueError("out_projection_shape")
+        self._phase_ctx = self._phase("out_gemm_residual")
+        self._phase_ctx.__enter__()
         _lib.call(
             "ogx_fp8_scaled_mm_residual_gate_kblocked",
             recv2.data_ptr(), Ll, 4096, p.heads_local * p.head_dim, w.to_out.weight.data_ptr(), 4096,
@@ -167,6 +304,7 @@ class UlyssesVideoSelfAttention:
             ts_view.data_ptr(), ltx_ops._code(ts_view), ts_view.stride(1), ts_view.stride(2), 2,
             out.data_ptr(), out.stride(1), ltx_ops._stream(x_loc),
         )
+        self._phase_ctx.__exit__(None, None, None)
         return out
 
     def forward(self, x: torch.Tensor, timestep: torch.Tensor, pe: tuple[torch.Tensor, torch.Tensor]):

@@ -171,8 +171,10 @@ def test_block_full_size_vs_fp32_reference_on_gpu(ogx_lib, name):
     assert status_clean()
 
 
-def test_host_pipeline_matches_direct_calls(ogx_lib):
-    """Host-resident inputs through the three-stream pipeline give exactly the direct block outputs."""
+@pytest.mark.parametrize("graphs", [False, True])
+def test_host_pipeline_matches_direct_calls(ogx_lib, graphs):
+    """Host-resident inputs through the three-stream pipeline (eager launches, or one CUDA graph replay
+    per step) give exactly the direct block outputs."""
     from opengenie_b200 import synthetic
     from opengenie_b200.streaming import HostPipeline
     from opengenie_b200.video_block import VideoSelfAttentionBlock
@@ -184,8 +186,31 @@ def test_host_pipeline_matches_direct_calls(ogx_lib):
     xs = [(inp.x.float().cpu() * (1 + 0.1 * i)).to(torch.bfloat16).pin_memory() for i in range(5)]
     outs = [torch.empty_like(x).pin_memory() for x in xs]
     pipe = HostPipeline(lambda xd, yd: blk(xd, inp.timestep, (inp.cos, inp.sin), out=yd), tuple(xs[0].shape),
-                        torch.bfloat16, "cuda")
+                        torch.bfloat16, "cuda", graphs=graphs)
     pipe.run(xs, outs)
     torch.cuda.synchronize()
     for x, o in zip(xs, outs):
         assert torch.equal(o, blk(x.cuda(), inp.timestep, (inp.cos, inp.sin)).cpu())
+
+
+def test_step_graph_replay_matches_eager(ogx_lib):
+    """The block captured once as a CUDA graph and replayed gives exactly the eager output, on every
+    replay, also after the input buffer's contents change."""
+    from opengenie_b200 import synthetic
+    from opengenie_b200.graphs import StepGraph
+    from opengenie_b200.video_block import VideoSelfAttentionBlock
+
+    cfg = synthetic.small_config(2, 8, 16)
+    inp = synthetic.make_inputs(cfg, seed=73).to("cuda")
+    blk = VideoSelfAttentionBlock(synthetic.make_weights(seed=74), "cuda")
+    blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
+    x = inp.x.clone()
+    out = torch.empty_like(x)
+    blk(x, inp.timestep, (inp.cos, inp.sin), out=out)
+    g = StepGraph(lambda: blk(x, inp.timestep, (inp.cos, inp.sin), out=out), "cuda")
+    for scale in (1.0, 0.5, 1.0):
+        x.copy_((inp.x.float() * scale).to(torch.bfloat16))
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, blk(x, inp.timestep, (inp.cos, inp.sin)))
