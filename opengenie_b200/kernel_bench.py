@@ -1,0 +1,126 @@
+"""Times one kernel of the block alone, at any size: a CLI for sweeps and for profiler captures of a
+single launch on a small case.
+
+    python -m opengenie_b200.kernel_bench attention --tokens 9216 --heads 4 [--e4m3]
+    python -m opengenie_b200.kernel_bench gemm --m 9216 --n 12288 --k 4096 [--residual]
+    python -m opengenie_b200.kernel_bench adazero --tokens 9216
+    python -m opengenie_b200.kernel_bench rope --tokens 9216
+
+Prints one JSON line: the average device time of a launch (CUDA events on the launching stream,
+after warm-up) and the algorithmic rate (TFLOP/s for the contractions, GB/s of unique bytes for the
+memory-bound kernels).  Inputs are seeded random tensors laid out as the block lays them out.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import ltx_ops, synthetic
+
+
+def _time(fn, steps: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def bench_attention(a) -> dict:
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    L, H = a.tokens, a.heads
+    # packed [L][3][H*128] rows, as the QKV projection leaves them
+    qkv = torch.randn((L, 3 * H * 128), device="cuda", generator=g).to(torch.bfloat16)
+    q, k, v = (qkv[:, i * H * 128:(i + 1) * H * 128].unsqueeze(0) for i in range(3))
+    if a.e4m3:
+        out = torch.empty((1, L, H * 128), device="cuda", dtype=torch.float8_e4m3fn)
+        scale = torch.tensor(0.01, device="cuda")
+        fn = lambda: ltx_ops.attention(q, k, v, H, out=out, out_e4m3_scale=scale)  # noqa: E731
+    else:
+        out = torch.empty((1, L, H * 128), device="cuda", dtype=torch.bfloat16)
+        fn = lambda: ltx_ops.attention(q, k, v, H, out=out)  # noqa: E731
+    ms = _time(fn, a.steps, a.warmup)
+    flops = 4.0 * L * L * 128 * H
+    return {"kernel": "fmha_fwd_kernel", "tokens": L, "heads": H, "e4m3_out": a.e4m3, "ms": ms,
+            "tflops": flops / (ms * 1e-3) / 1e12}
+
+
+def bench_gemm(a) -> dict:
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    M, N, K = a.m, a.n, a.k
+    xq = (torch.randn((M, K), device="cuda", generator=g) * 100).clamp(-448, 448).to(torch.float8_e4m3fn)
+    w = (torch.randn((N, K), device="cuda", generator=g) * 100).clamp(-448, 448).to(torch.float8_e4m3fn)
+    s_in = torch.tensor(1e-3, device="cuda")
+    s_w = torch.full((1,), 1e-3, device="cuda")
+    bias = (torch.randn((N,), device="cuda", generator=g) * 0.01).to(torch.bfloat16)
+    if a.residual:
+        x = torch.randn((1, M, N), device="cuda", generator=g).to(torch.bfloat16)
+        table = torch.randn((6, N), device="cuda", generator=g) * 0.02
+        ts = torch.randn((1, 1, 6 * N), device="cuda", generator=g).to(torch.bfloat16).expand(1, M, 6 * N)
+        fn = lambda: ltx_ops.fp8_scaled_mm_residual_gate(xq.view(1, M, K), w, s_in, s_w, bias, x, table, ts,  # noqa: E731
+                                                         gate_index=2)
+    else:
+        out = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+        fn = lambda: ltx_ops.fp8_scaled_mm(xq, w, s_in, s_w, bias=bias, out=out)  # noqa: E731
+    ms = _time(fn, a.steps, a.warmup)
+    return {"kernel": "fp8_gemm_kernel", "m": M, "n": N, "k": K, "residual_epilogue": a.residual, "ms": ms,
+            "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12}
+
+
+def bench_adazero(a) -> dict:
+    cfg = synthetic.small_config(1, 1, a.tokens)
+    inp = synthetic.make_inputs(cfg, seed=a.seed).to("cuda")
+    w = synthetic.make_weights(seed=a.seed + 1).to("cuda")
+    s = torch.tensor(0.01, device="cuda")
+    fn = lambda: ltx_ops.fused_adazero_from_ada_fp8(inp.x, 1e-6, w.scale_shift_table, inp.timestep, s,  # noqa: E731
+                                                    shift_index=0, scale_index=1)
+    ms = _time(fn, a.steps, a.warmup)
+    nbytes = a.tokens * 4096 * 3  # bf16 x read + e4m3 write (the uniform timestep rows stay in cache)
+    return {"kernel": "adazero_from_ada_kernel", "tokens": a.tokens, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9}
+
+
+def bench_rope(a) -> dict:
+    cfg = synthetic.small_config(1, 1, a.tokens)
+    inp = synthetic.make_inputs(cfg, seed=a.seed).to("cuda")
+    w = synthetic.make_weights(seed=a.seed + 1).to("cuda")
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    qkv = torch.randn((a.tokens, 3 * 4096), device="cuda", generator=g).to(torch.bfloat16)
+    q, k = qkv[:, :4096].unsqueeze(0), qkv[:, 4096:8192].unsqueeze(0)
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+    fn = lambda: ltx_ops.fused_video_qk_rmsnorm_rope(q, k, w.q_norm_weight, w.k_norm_weight, 1e-6,  # noqa: E731
+                                                     inp.cos, inp.sin, out=(qo, ko))
+    ms = _time(fn, a.steps, a.warmup)
+    cs = inp.cos.element_size()
+    nbytes = a.tokens * 4096 * 2 * 4 + 2 * a.tokens * 32 * 64 * cs  # q, k read + written; cos, sin read
+    return {"kernel": "qk_rmsnorm_rope_kernel", "tokens": a.tokens, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9}
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("kernel", choices=["attention", "gemm", "adazero", "rope"])
+    ap.add_argument("--tokens", type=int, default=9216)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--e4m3", action="store_true")
+    ap.add_argument("--m", type=int, default=9216)
+    ap.add_argument("--n", type=int, default=12288)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--residual", action="store_true")
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args(argv)
+    fn = {"attention": bench_attention, "gemm": bench_gemm, "adazero": bench_adazero, "rope": bench_rope}[a.kernel]
+    print(json.dumps(fn(a)))
+
+
+if __name__ == "__main__":
+    main()
