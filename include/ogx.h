@@ -191,6 +191,19 @@ int ogx_ipc_close_handle(void* base);
  * graph.  All ranks must run the same barriers in the same order.  One 32-thread launch. */
 int ogx_peer_barrier(unsigned int* local_signals, void* const* peer_signals, int rank, int world, void* stream);
 
+/* No counterpart in the reference (an addition of this library).  ogx_peer_barrier for callers that
+ * cannot allocate device memory, e.g. a runtime driving all of its GPUs from one process with their
+ * memory reserved up front for its own pool.  The signal block is a 64-byte array inside the library,
+ * one per GPU that loads it and held until the process exits; it is zero at load and never cleared
+ * (barrier numbers only grow).  Ranks are GPUs of this process: devices[i] is rank i's device ordinal,
+ * devices[rank] must be the current device, and the caller enables peer access between them
+ * (cudaDeviceEnablePeerAccess) before a call with world > 1.  world is at most 8; larger values are
+ * rejected.  The first call naming a device looks up that device's array address (so make it before
+ * any stream capture).  count_out (device memory, may be NULL) receives the number of barriers this
+ * rank has passed.  Every call on a device shares its array: one barrier group per process, and calls
+ * that overlap on a GPU race.  Allocates nothing. */
+int ogx_peer_barrier_static(int rank, int world, const int* devices, unsigned int* count_out, void* stream);
+
 /* ogx_video_qkv_rmsnorm_rope_scatter with one destination base per head group (groups = world size):
  * head h of token t goes to group_bases[h / (32/groups)] + t*out_stride_t + {0, 1, 2}*(32/groups)*128
  * (q, k, v) + (h % (32/groups))*128, stored over NVLink when the base is a peer's receive buffer;

@@ -756,3 +756,83 @@ int ogx_attention_fwd_e4m3_to_peers(const void* q, const void* k, const void* v,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------
+// Cross-GPU barrier without caller-allocated memory.
+//
+// ogx_peer_barrier needs a 16-word signal block per rank, allocated by the caller.  Some callers
+// cannot allocate device memory: a runtime that drives all of its GPUs from one process and reserves
+// their memory up front for its own pool, so that no cudaMalloc may run once serving has started.
+// For them the signal block lives in this file-scope array instead, one per GPU that loads the
+// library (64 bytes, held until the process exits), and ogx_peer_barrier_static takes the ranks'
+// device ordinals instead of block pointers.  The ranks must be GPUs of this one process with peer
+// access enabled between them (UVA makes each device's copy of the array addressable by the others).
+namespace {
+
+// [0, 8) arrival slots, [8] barriers passed; zero when the library loads and never cleared after:
+// the barrier numbers only grow, so no call needs it zeroed again.
+static __device__ __align__(256) unsigned int g_static_peer_block[ogx::kPeerSignalWords];
+
+constexpr int kMaxDevices = 64;
+
+// Device address of g_static_peer_block on `dev`, looked up once per device with that device current.
+int static_peer_block(int dev, unsigned int** out) {
+  static std::mutex mu;
+  static unsigned int* addr[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return fail(OGX_EINVAL, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    int prev = 0;
+    int rc = check_cuda(cudaGetDevice(&prev), "cudaGetDevice");
+    if (rc) return rc;
+    rc = check_cuda(cudaSetDevice(dev), "cudaSetDevice");
+    if (rc) return rc;
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_peer_block);
+    cudaSetDevice(prev);
+    rc = check_cuda(e, "cudaGetSymbolAddress");
+    if (rc) return rc;
+    addr[dev] = static_cast<unsigned int*>(p);
+  }
+  *out = addr[dev];
+  return OGX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ogx_peer_barrier_static(int rank, int world, const int* devices, unsigned int* count_out, void* stream) {
+  if (devices == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (world < 1 || world > 8)
+    return fail(OGX_EINVAL, "world: the static signal block holds at most 8 ranks (got %d)", world);
+  if (rank < 0 || rank >= world) return fail(OGX_EINVAL, "world: rank %d outside [0, %d)", rank, world);
+  int cur = 0;
+  int rc = check_cuda(cudaGetDevice(&cur), "cudaGetDevice");
+  if (rc) return rc;
+  if (devices[rank] != cur)
+    return fail(OGX_EINVAL, "devices[rank] is %d but the current device is %d", devices[rank], cur);
+  unsigned int* local = nullptr;
+  rc = static_peer_block(cur, &local);
+  if (rc) return rc;
+  ogx::PeerSignals ps{};
+  for (int i = 0; i < world; ++i) {
+    if (devices[i] != cur) {
+      int can = 0;
+      rc = check_cuda(cudaDeviceCanAccessPeer(&can, cur, devices[i]), "cudaDeviceCanAccessPeer");
+      if (rc) return rc;
+      if (!can) return fail(OGX_EINVAL, "device %d cannot access peer device %d", cur, devices[i]);
+    }
+    rc = static_peer_block(devices[i], &ps.slot[i]);
+    if (rc) return rc;
+  }
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ogx::peer_barrier_kernel<<<1, 32, 0, s>>>(local, ps, rank, world);
+  rc = check_launch("peer_barrier_kernel");
+  if (rc || count_out == nullptr) return rc;
+  return check_cuda(cudaMemcpyAsync(count_out, local + ogx::kPeerCountWord, sizeof(unsigned int),
+                                    cudaMemcpyDeviceToDevice, s),
+                    "cudaMemcpyAsync");
+}
+
+}  // extern "C"

@@ -1,0 +1,54 @@
+"""The allocation-free cross-GPU barrier (ogx_peer_barrier_static) against the barrier that takes a
+caller-allocated signal block (ogx_peer_barrier).  Callers that cannot allocate device memory, such
+as a runtime that reserves all of its GPUs' memory for its own pool before serving, use the static
+variant; it must count barriers exactly as the allocated one does.
+
+This file is named to be collected last: the static signal block lives for the whole process, so
+nothing else in the test run touches it before this test."""
+
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_static_barrier_counts_like_allocated_barrier(ogx_lib):
+    from opengenie_b200 import _lib
+
+    stream = torch.cuda.current_stream().cuda_stream
+    dev = torch.cuda.current_device()
+    _lib.device_status(clear=True)
+
+    # the existing entry point, on a signal block the caller allocated
+    sig = torch.zeros(16, dtype=torch.int32, device="cuda")
+    peers = (ctypes.c_void_p * 1)(sig.data_ptr())
+    allocated = []
+    for _ in range(2):
+        assert ogx_lib.ogx_peer_barrier(sig.data_ptr(), peers, 0, 1, stream) == 0
+        torch.cuda.synchronize()
+        allocated.append(int(sig[8].item()))
+
+    # the allocation-free entry point (count_out is an output the caller provides)
+    devices = (ctypes.c_int * 1)(dev)
+    count = torch.zeros(1, dtype=torch.int32, device="cuda")
+    static = []
+    for _ in range(2):
+        assert ogx_lib.ogx_peer_barrier_static(0, 1, devices, count.data_ptr(), stream) == 0, \
+            ogx_lib.ogx_last_error()
+        torch.cuda.synchronize()
+        static.append(int(count.item()))
+
+    assert allocated == [1, 2]
+    assert static == allocated
+    assert _lib.device_status(clear=True) == 0
+
+
+def test_static_barrier_rejects_more_ranks_than_its_block_holds(ogx_lib):
+    dev = torch.cuda.current_device()
+    devices = (ctypes.c_int * 9)(*([dev] * 9))
+    stream = torch.cuda.current_stream().cuda_stream
+    assert ogx_lib.ogx_peer_barrier_static(0, 9, devices, None, stream) != 0
+    assert b"at most 8 ranks" in ogx_lib.ogx_last_error()
+    assert ogx_lib.ogx_peer_barrier_static(1, 1, devices, None, stream) != 0
