@@ -196,6 +196,8 @@ constexpr int kAdaRowsPerCta = 8;
 // loaded before the current row's reduction completes.
 template <int COLS, typename TableT, typename TsT, bool QUANT, int QMODE, bool UNIFORM>
 __global__ void __launch_bounds__(kRowThreads) adazero_from_ada_kernel(AdaArgs a) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int VPT = COLS / 8 / kRowThreads;  // 16-byte vectors per thread
   __shared__ float red[2][4];
   const int tid = threadIdx.x;
@@ -489,6 +491,8 @@ __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* in, const 
 // One 128-thread CTA per token.
 template <typename WT, typename CsT>
 __global__ void __launch_bounds__(kRowThreads) qk_rmsnorm_rope_kernel(RopeArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[2][4];
   const int64_t t = blockIdx.x;
   const CsT* cosb = static_cast<const CsT*>(a.cos);

@@ -161,6 +161,7 @@ template <bool OUT_E4M3>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, Params p) {
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   __shared__ SharedState st;
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -201,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&st.tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
+  pdl_wait();  // everything above touches only this CTA's shared memory and TMEM
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

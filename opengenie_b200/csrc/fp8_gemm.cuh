@@ -93,6 +93,7 @@ template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     Params p) {
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   __shared__ SharedState st;
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -126,6 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&st.tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
+  pdl_wait();  // everything above touches only this CTA's shared memory and TMEM
   float* col_bias = reinterpret_cast<float*>(smem_aligned + STAGES * STAGE_BYTES);
   float* col_gate = col_bias + RES_MAX_N;
   const bool gate_uniform = p.ts_stride_t == 0;

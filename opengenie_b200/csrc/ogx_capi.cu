@@ -13,6 +13,8 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <utility>
+#include <cstdlib>
 
 #include "../../include/ogx.h"
 #include "elementwise.cuh"
@@ -40,6 +42,32 @@ int check_cuda(cudaError_t e, const char* what) {
 }
 
 int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+
+// The block's kernels are launched with programmatic stream serialization (each calls pdl_wait() before
+// touching global memory), so a kernel's set-up overlaps the tail of the one before it in the stream.
+// OGX_PDL=0 in the environment turns it off.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("OGX_PDL");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -113,11 +141,11 @@ void launch_ada_u(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) 
   const dim3 grid(static_cast<unsigned>((a.rows + ogx::kAdaRowsPerCta - 1) / ogx::kAdaRowsPerCta));
   const int threads = ogx::kRowThreads;
   if (!quant)
-    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, false, 0, UNIFORM><<<grid, threads, 0, s>>>(a);
+    launch(ogx::adazero_from_ada_kernel<COLS, TableT, TsT, false, 0, UNIFORM>, grid, threads, 0, s, a);
   else if (qmode == OGX_QUANT_TORCH)
-    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantTorch, UNIFORM><<<grid, threads, 0, s>>>(a);
+    launch(ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantTorch, UNIFORM>, grid, threads, 0, s, a);
   else
-    ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantSingle, UNIFORM><<<grid, threads, 0, s>>>(a);
+    launch(ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantSingle, UNIFORM>, grid, threads, 0, s, a);
 }
 
 template <int COLS, typename TableT, typename TsT>
@@ -393,11 +421,11 @@ int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void*
   const bool wf = weight_dtype == OGX_DTYPE_F32;
   const bool cf = cs_dtype == OGX_DTYPE_F32;
   if (wf) {
-    if (cf) ogx::qk_rmsnorm_rope_kernel<float, float><<<grid, threads, 0, s>>>(a);
-    else ogx::qk_rmsnorm_rope_kernel<float, __nv_bfloat16><<<grid, threads, 0, s>>>(a);
+    if (cf) launch(ogx::qk_rmsnorm_rope_kernel<float, float>, grid, threads, 0, s, a);
+    else launch(ogx::qk_rmsnorm_rope_kernel<float, __nv_bfloat16>, grid, threads, 0, s, a);
   } else {
-    if (cf) ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, float><<<grid, threads, 0, s>>>(a);
-    else ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, s>>>(a);
+    if (cf) launch(ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, float>, grid, threads, 0, s, a);
+    else launch(ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, __nv_bfloat16>, grid, threads, 0, s, a);
   }
   return check_launch("qk_rmsnorm_rope_kernel");
 }
@@ -457,7 +485,7 @@ int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::P
   if (rc) return rc;
   const int tiles = ((p.M + ogx::gemm::BM - 1) / ogx::gemm::BM) * ((p.N + ogx::gemm::BN - 1) / ogx::gemm::BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, ogx::gemm::kThreads, smem, s>>>(ma, mb, p);
+  launch(kern, grid, ogx::gemm::kThreads, smem, s, ma, mb, p);
   return check_launch("fp8_gemm_kernel");
 }
 
@@ -498,7 +526,7 @@ int attention_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtenso
                 ogx::fmha::kLaunchRegs);
   const dim3 grid(static_cast<unsigned>((tokens + 255) / 256), static_cast<unsigned>(heads),
                   static_cast<unsigned>(batch));
-  kern<<<grid, ogx::fmha::kThreads, ogx::fmha::SMEM_BYTES, s>>>(mq, mk, mv, p);
+  launch(kern, grid, ogx::fmha::kThreads, ogx::fmha::SMEM_BYTES, s, mq, mk, mv, p);
   return check_launch("fmha_fwd_kernel");
 }
 
@@ -673,7 +701,7 @@ int ogx_peer_barrier(unsigned int* local_signals, void* const* peer_signals, int
     if (peer_signals[i] == nullptr) return fail(OGX_EINVAL, "null_pointer");
     ps.slot[i] = static_cast<unsigned int*>(peer_signals[i]);
   }
-  ogx::peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(local_signals, ps, rank, world);
+  launch(ogx::peer_barrier_kernel, 1, 32, 0, static_cast<cudaStream_t>(stream), local_signals, ps, rank, world);
   return check_launch("peer_barrier_kernel");
 }
 
@@ -722,11 +750,11 @@ int ogx_video_qkv_rmsnorm_rope_to_peers(const void* q, const void* k, const void
   const bool wf = weight_dtype == OGX_DTYPE_F32;
   const bool cf = cs_dtype == OGX_DTYPE_F32;
   if (wf) {
-    if (cf) ogx::qk_rmsnorm_rope_kernel<float, float><<<grid, threads, 0, s>>>(a);
-    else ogx::qk_rmsnorm_rope_kernel<float, __nv_bfloat16><<<grid, threads, 0, s>>>(a);
+    if (cf) launch(ogx::qk_rmsnorm_rope_kernel<float, float>, grid, threads, 0, s, a);
+    else launch(ogx::qk_rmsnorm_rope_kernel<float, __nv_bfloat16>, grid, threads, 0, s, a);
   } else {
-    if (cf) ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, float><<<grid, threads, 0, s>>>(a);
-    else ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, s>>>(a);
+    if (cf) launch(ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, float>, grid, threads, 0, s, a);
+    else launch(ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, __nv_bfloat16>, grid, threads, 0, s, a);
   }
   return check_launch("qk_rmsnorm_rope_kernel");
 }

@@ -31,6 +31,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialization may start
+// while the previous kernel in its stream is still running: pdl_trigger() lets the next kernel's CTAs be
+// launched once every CTA of this one has started, and pdl_wait() blocks until the previous kernel has
+// completed and its memory is visible.  Every kernel here that may be launched that way calls pdl_wait()
+// before its first global-memory access; both are no-ops for an ordinary launch.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -29,6 +29,8 @@ constexpr int kPeerCountWord = 8;
 
 __global__ void __launch_bounds__(32) peer_barrier_kernel(unsigned int* local, PeerSignals peers, int rank,
                                                           int world) {
+  pdl_trigger();
+  pdl_wait();  // the producing kernel has completed (its peer stores were fenced system-wide)
   const int i = threadIdx.x;
   const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(local + kPeerCountWord) + 1u;
   if (i < world && i != rank) {
