@@ -209,6 +209,155 @@ def config_dict(name: str, n: int, exchange: str = "nvlink", graph: bool = True)
     }
 
 
+# --------------------------------------------------------------------------- the video FFN branch
+FFN_METRIC = "video FFN branch µs & TFLOP/s (FP8 projections 4096->16384->4096) at L=9216, 1/2/4/8 B200"
+
+
+def ffn_flops(L: int, dim: int = 4096, hidden: int = 16384) -> float:
+    return 4.0 * L * dim * hidden
+
+
+def run_ffn(args) -> None:
+    """``--branch ffn``: the same layer's video feed-forward branch (sequence-local: at N GPUs each rank
+    runs its L/N tokens, no exchange).  Same timing rules as the attention block."""
+    from opengenie_b200 import _lib, synthetic
+    from opengenie_b200.graphs import StepGraph
+    from opengenie_b200.streaming import HostPipeline
+    from opengenie_b200.video_ffn import VideoFeedForward
+    from oracle import ltx_block_oracle as O
+
+    rank, world, local, pg = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    cfg = synthetic.CONFIGS[args.config]
+    L = cfg.tokens
+    if L % world:
+        raise SystemExit(f"{L} tokens do not split over {world} ranks")
+    Ll = L // world
+    inp_cpu = synthetic.make_inputs(cfg, seed=1)
+    ts_full = inp_cpu.timestep
+    x_loc_cpu = inp_cpu.x[:, rank * Ll:(rank + 1) * Ll].contiguous()
+    ts_loc_cpu = ts_full[:, rank * Ll:(rank + 1) * Ll]
+    x_loc = x_loc_cpu.to(dev)
+    ts_loc = (ts_loc_cpu[:, :1].to(dev).expand(ts_loc_cpu.shape) if ts_loc_cpu.stride(1) == 0
+              else ts_loc_cpu.contiguous().to(dev))
+    ffn = VideoFeedForward(synthetic.make_ffn_weights(seed=0), dev)
+    inp_dev = inp_cpu.to(dev)
+    ffn.calibrate_input_scales(inp_dev.x, inp_dev.timestep)  # static scales from all L tokens
+    del inp_dev
+    out_dev = torch.empty_like(x_loc)
+
+    def step():
+        ffn(x_loc, ts_loc, out=out_dev)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    run_step = step
+    if not args.no_graph:
+        graph = StepGraph(step, dev)
+        run_step = graph.replay
+        for _ in range(2):
+            run_step()
+        torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    barrier(pg)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            run_step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(pg)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, pg)
+
+    # e2e: pinned host x in, output back, through the host pipeline
+    x_host = x_loc_cpu.pin_memory()
+    out_hosts = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(lambda xd, yd: ffn(xd, ts_loc, out=yd), tuple(x_host.shape), x_host.dtype, dev,
+                        graphs=not args.no_graph)
+    pipe.run([x_host] * 2, out_hosts)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    pipe.start_after(e0)
+    pipe.run([x_host] * args.steps, [out_hosts[i % 2] for i in range(args.steps)])
+    pipe.wait_streams(stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, pg)
+
+    # dominant kernel: the GELU-epilogue GEMM (4096 -> 16384) timed alone
+    from opengenie_b200 import ltx_ops
+
+    w = ffn.w
+    xq = ltx_ops.fused_adazero_from_ada_fp8(x_loc, w.norm_eps, w.scale_shift_table, ts_loc, w.proj.input_scale,
+                                            shift_index=3, scale_index=4)
+    hq = torch.empty((Ll, ffn.hidden), device=dev, dtype=torch.float8_e4m3fn)
+
+    def gemm1():
+        ltx_ops.fp8_scaled_mm_gelu_e4m3(xq, w.proj.weight, w.proj.input_scale, w.proj.weight_scale,
+                                        w.out.input_scale, bias=w.proj.bias, out=hq)
+
+    for _ in range(args.warmup):
+        gemm1()
+    torch.cuda.synchronize(dev)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for _ in range(args.steps):
+        gemm1()
+    k1.record(stream)
+    torch.cuda.synchronize(dev)
+    gemm_ms = max_over_ranks(k0.elapsed_time(k1) / args.steps, pg)
+    status = _lib.device_status(clear=True)
+
+    if rank == 0:
+        peaks, peak_kind = measured_peaks()
+        fp8_peak = 2.0 * peaks["bf16_tflops"]
+        g_flops = 2.0 * Ll * 4096 * 16384
+        achieved = g_flops / (gemm_ms * 1e-3) / 1e12
+        line = {
+            "metric": FFN_METRIC, "value": ffn_flops(L) / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_block": ms * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 projections, fp32 accumulate",
+            "data": "synthetic (seeded inputs, random-init weights)",
+            "config": {"workload": f"LTX-2.3 video FFN branch, {args.config}", "tokens": L, "hidden": 4096,
+                       "ffn_hidden": 16384, "batch": 1, "per_token_timestep": cfg.per_token_timestep,
+                       "parallelism": "single GPU" if world == 1 else f"tokens split over {world} GPUs",
+                       "l2": "inputs larger than L2 (x 75 MB + weights 134 MB per branch)",
+                       "launch": "eager launches" if args.no_graph else "one CUDA graph replay per step"},
+            "roofline": {"bound": "tensor", "kernel": "fp8_gemm_kernel<EPI_GELU_QUANT> (4096 -> 16384, dominant)",
+                         "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
+                         "peak_kind": f"2 x {peak_kind} bf16 dense (burst): tcgen05 kind::f8f6f4 runs at twice the "
+                                      "kind::f16 rate", "algorithmic_flops_per_launch": g_flops,
+                         "kernel_ms": gemm_ms, "traffic": None},
+            "e2e": {"value": ffn_flops(L) / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": x_host.numel() * 2 * world, "d2h_bytes_per_step": x_host.numel() * 2 * world},
+            "gpu_launches": VideoFeedForward.kernel_launches_per_step * args.steps,
+            "clocks": clk.summary(), "device_status": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            ts_view = inp_cpu.timestep.reshape(1, L, 6, 4096)
+            threads = len(os.sched_getaffinity(0))
+            torch.set_num_threads(threads)
+            fw_cpu = ffn.w.to("cpu")
+            t0 = time.perf_counter()
+            with torch.no_grad():
+                O.video_ffn_cpu_fp32(inp_cpu.x, ts_view, fw_cpu)
+            per = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": ffn_flops(L) / per / 1e12, "unit": UNIT, "cores": threads,
+                                    "kind": "port", "sample": f"1 full FFN branch (L={L}) in torch fp32 on the host; "
+                                                              f"{per * 1e3:.0f} ms"}
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -222,8 +371,13 @@ def main() -> None:
     ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
                     help="N>1: peer stores over NVLink from the producing kernels, or NCCL all-to-alls")
     ap.add_argument("--phases", action="store_true", help="add a per-stage time breakdown (separate, untimed run)")
+    ap.add_argument("--branch", choices=["attention", "ffn"], default="attention",
+                    help="the video self-attention block (the headline) or the same layer's video FFN branch")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.branch == "ffn" and args.impl == "ours":
+        run_ffn(args)
+        return
 
     if args.impl == "reference":
         run_reference_arm(args)

@@ -75,6 +75,14 @@ int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int6
 int ogx_fp8_quantize_e4m3(const void* x, int x_dtype, int64_t n, const float* input_scale, int quant_mode, void* q,
                           void* stream);
 
+/* GELU (tanh approximation) fused with the per-tensor E4M3 quantiser:
+ * q = quant(round_to_x_dtype(gelu(x))); gelu_out (may be NULL) receives the rounded GELU values.
+ * x: bf16 or f16, n elements contiguous; input_scale: device f32 scalar.
+ * Replaces fused_gelu_tanh_fp8_quantize_e4m3, ltx_serve/triton_ltx_ops.py:164-182 (torch path
+ * :166-169; Triton kernel :3535-3550). */
+int ogx_gelu_tanh_fp8_quantize_e4m3(const void* x, int x_dtype, int64_t n, const float* input_scale, void* q,
+                                    void* gelu_out, void* stream);
+
 /* out = bf16(x + bf16(bias)); x bf16 [rows, cols] contiguous, bias [cols].
  * Replaces fused_bias_add_bf16, ltx_serve/triton_ltx_ops.py:185-201. */
 int ogx_bias_add_bf16(const void* x, int64_t rows, int64_t cols, const void* bias, int bias_dtype, void* out,
@@ -124,6 +132,17 @@ int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void*
 int ogx_fp8_scaled_mm(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                       const float* scale_a, const float* scale_b, int64_t n_per_scale, const void* bias,
                       int bias_dtype, void* out, int64_t ldo, void* stream);
+
+/* The FFN's first projection with GELU and the next projection's input quantiser in the epilogue:
+ * out_q = quant_{q_scale}(bf16(gelu(bf16(bf16(a @ w^T * scale_a * scale_b) + bf16(bias))))), e4m3
+ * [M, N] with row stride ldq (a multiple of 16).  Equals ogx_fp8_scaled_mm followed by
+ * ogx_gelu_tanh_fp8_quantize_e4m3 on its bf16 output, without the bf16 hidden tensor in HBM.
+ * Replaces the video FFN's FeedForward net[0] (FP8Linear.forward :1695-1707 + gelu tanh) and the
+ * quantiser of net[2] (fp8_linear_without_bias :770-771; _feedforward_without_out_bias :2796-2807). */
+int ogx_fp8_scaled_mm_gelu_e4m3(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
+                                int64_t ldw, const float* scale_a, const float* scale_b, int64_t n_per_scale,
+                                const void* bias, int bias_dtype, const float* q_scale, void* out_q, int64_t ldq,
+                                void* stream);
 
 /* FP8 scaled matmul fused with the block's output epilogue:
  *   y = bf16(bf16(acc * scale_a * scale_b) + bf16(bias)),

@@ -73,6 +73,11 @@ _SIGNATURES: dict[str, list] = {
     "ogx_ipc_open_handle": [c_void_p, ctypes.POINTER(c_void_p)],
     "ogx_ipc_close_handle": [c_void_p],
     "ogx_peer_barrier": [c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "ogx_gelu_tanh_fp8_quantize_e4m3": [c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
+    "ogx_fp8_scaled_mm_gelu_e4m3": [
+        c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
+        c_void_p, c_int, c_void_p, c_void_p, c_int64, c_void_p,
+    ],
     "ogx_peer_barrier_static": [c_int, c_int, c_void_p, c_void_p, c_void_p],
     "ogx_video_qkv_rmsnorm_rope_to_peers": [
         c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p,

@@ -33,7 +33,7 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return v;
 }
 
-// Loads 8 consecutive values of type T (bf16 or fp32) as fp32.
+// Loads 8 consecutive values of type T (bf16, fp16 or fp32) as fp32.
 template <typename T>
 __device__ __forceinline__ void load8(const T* p, float (&f)[8]);
 
@@ -48,6 +48,18 @@ __device__ __forceinline__ void load8<float>(const float* p, float (&f)[8]) {
   const float4 b = reinterpret_cast<const float4*>(p)[1];
   f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
   f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&f)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __half22float2(h[i]);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -336,6 +348,66 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(const InT* __restrict
         f = __half2float(reinterpret_cast<const __half*>(x)[i]);
         q[i] = ((hb & 0x7C00u) == 0x7C00u && (hb & 0x03FFu) != 0u) ? static_cast<uint8_t>(0x7Fu | ((hb >> 8) & 0x80u))
                                                                   : quant_one<InT, MODE>(f, s, r);
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------- GELU (tanh) + quantiser
+// gelu(x) = 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3): the GELU the reference's FFN uses
+// (torch.nn.functional.gelu(approximate="tanh"), triton_ltx_ops.py:166, and its Triton kernel
+// :3546-3548).  Evaluated through the identity 0.5 (1 + tanh(u)) = 1 / (1 + e^(-2u)) with the hardware
+// ex2 and reciprocal approximations: a few instructions instead of a tanh, and no cancellation for
+// x << 0 where 1 + tanh(u) loses the digits of a tiny result.  Infinities and NaN propagate as in the
+// tanh form (gelu(+inf) = +inf, gelu(-inf) = NaN).
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float u = 0.7978845608028654f * (x + 0.044715f * (x * x * x));
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-2.8853900817779268f * u));  // e^(-2u) = 2^(-2u log2 e)
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return x * r;
+}
+
+// q = quant(round_to_input_dtype(gelu(x))) with the torch-path quantiser (the reference's torch path
+// rounds the GELU output to the input dtype, then multiplies by 1/s in that dtype:
+// triton_ltx_ops.py:164-169).  gelu_out (may be null) receives the rounded GELU values.
+template <typename InT>
+__global__ void __launch_bounds__(256) gelu_tanh_quantize_kernel(const InT* __restrict__ x, int64_t n,
+                                                                 const float* __restrict__ input_scale,
+                                                                 uint8_t* __restrict__ q, InT* __restrict__ gelu_out) {
+  const float s = __ldg(input_scale);
+  const float r = __frcp_rn(s);
+  const int64_t nvec = n >> 3;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    float f[8];
+    load8<InT>(x + v * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = round_to<InT>(gelu_tanh(f[i]));
+    reinterpret_cast<uint2*>(q)[v] = quant8<InT, kQuantTorch>(f, s, r);
+    if (gelu_out != nullptr) {
+      if (std::is_same<InT, __nv_bfloat16>::value) {
+        reinterpret_cast<uint4*>(gelu_out)[v] = pack8(f);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) reinterpret_cast<__half*>(gelu_out)[v * 8 + i] = __float2half_rn(f[i]);
+      }
+    }
+  }
+  if (blockIdx.x == 0) {
+    for (int64_t i = (nvec << 3) + threadIdx.x; i < n; i += blockDim.x) {
+      float f;
+      if (std::is_same<InT, __nv_bfloat16>::value)
+        f = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
+      else
+        f = __half2float(reinterpret_cast<const __half*>(x)[i]);
+      f = round_to<InT>(gelu_tanh(f));
+      q[i] = quant_one<InT, kQuantTorch>(f, s, r);
+      if (gelu_out != nullptr) {
+        if (std::is_same<InT, __nv_bfloat16>::value)
+          reinterpret_cast<__nv_bfloat16*>(gelu_out)[i] = __float2bfloat16_rn(f);
+        else
+          reinterpret_cast<__half*>(gelu_out)[i] = __float2half_rn(f);
       }
     }
   }

@@ -18,6 +18,11 @@
 //   EPI_RESIDUAL: bf16(x + bf16(bf16(bf16(acc*s) + bf16(bias)) * gate))
 //                 (fp8_linear_without_bias :762-781 then
 //                 fused_residual_gate_bias_from_ada :204-262)
+//   EPI_GELU_QUANT: e4m3 quant(bf16(gelu(bf16(bf16(acc*s) + bf16(bias)))))
+//                 (the FFN's first projection, GELU and the second
+//                 projection's input quantiser: FP8Linear.forward :1695-1707,
+//                 gelu(approximate="tanh"), fused_fp8_quantize_e4m3 :144-161
+//                 as fp8_linear_without_bias :770-771 applies it)
 #pragma once
 
 #include "ogx_sm100.cuh"
@@ -42,7 +47,7 @@ constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
 constexpr int RES_MAX_N = 4096;
 constexpr int SMEM_BYTES_RESIDUAL = SMEM_BYTES + 2 * RES_MAX_N * 4;
 
-enum Epilogue : int { EPI_BIAS = 0, EPI_RESIDUAL = 1 };
+enum Epilogue : int { EPI_BIAS = 0, EPI_RESIDUAL = 1, EPI_GELU_QUANT = 2 };
 
 struct Params {
   int M, N, K;
@@ -68,6 +73,10 @@ struct Params {
   int ts_fp32;
   int64_t ts_stride_t, ts_stride_p;
   int gate_index;
+  // EPI_GELU_QUANT only: e4m3 output [M, N] (row stride ldq) and its device scalar scale
+  uint8_t* out_q;
+  int64_t ldq;
+  const float* q_scale;
 };
 
 // Per-column constants of the residual epilogue, computed once per CTA:
@@ -245,6 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (static_cast<int>(warp) - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     const float sa = __ldg(p.scale_a);
+    const float qs = EPI == EPI_GELU_QUANT ? __ldg(p.q_scale) : 1.f;
+    const float qr = __frcp_rn(qs);
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -323,7 +334,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 8; ++i) o[i] += bb[i];
             }
-            reinterpret_cast<uint4*>(orow)[v8] = pack8(o);
+            if (EPI == EPI_GELU_QUANT) {
+              float h[8];
+              unpack8(pack8(o), h);  // the bf16 hidden activation
+#pragma unroll
+              for (int i = 0; i < 8; ++i) h[i] = gelu_tanh(h[i]);
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) bf16_round2(h[i], h[i + 1]);
+              *reinterpret_cast<uint2*>(p.out_q + static_cast<int64_t>(row) * p.ldq + cb) =
+                  quant8<__nv_bfloat16, kQuantTorch>(h, qs, qr);
+            } else {
+              reinterpret_cast<uint4*>(orow)[v8] = pack8(o);
+            }
           }
         }
         tmem_ld_wait();

@@ -306,6 +306,27 @@ int ogx_fp8_quantize_e4m3(const void* x, int x_dtype, int64_t n, const float* in
   return check_launch("fp8_quantize_kernel");
 }
 
+int ogx_gelu_tanh_fp8_quantize_e4m3(const void* x, int x_dtype, int64_t n, const float* input_scale, void* q,
+                                    void* gelu_out, void* stream) {
+  if (x_dtype != OGX_DTYPE_BF16 && x_dtype != OGX_DTYPE_F16) return fail(OGX_EINVAL, "x_dtype");
+  if (n < 0) return fail(OGX_EINVAL, "numel");
+  if (n == 0) return OGX_OK;
+  if (x == nullptr || q == nullptr || input_scale == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u) || (gelu_out != nullptr && !aligned16(gelu_out)))
+    return fail(OGX_EINVAL, "alignment");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for((n >> 3) > 0 ? (n >> 3) : 1);
+  if (x_dtype == OGX_DTYPE_BF16)
+    ogx::gelu_tanh_quantize_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), n, input_scale, static_cast<uint8_t*>(q),
+        static_cast<__nv_bfloat16*>(gelu_out));
+  else
+    ogx::gelu_tanh_quantize_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), n, input_scale,
+                                                                static_cast<uint8_t*>(q),
+                                                                static_cast<__half*>(gelu_out));
+  return check_launch("gelu_tanh_quantize_kernel");
+}
+
 int ogx_bias_add_bf16(const void* x, int64_t rows, int64_t cols, const void* bias, int bias_dtype, void* out,
                       void* stream) {
   if (x == nullptr || bias == nullptr || out == nullptr) return fail(OGX_EINVAL, "null_pointer");
@@ -554,6 +575,31 @@ int ogx_fp8_scaled_mm(const void* a, int64_t M, int64_t K, int64_t lda, const vo
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
   return gemm_launch<ogx::gemm::EPI_BIAS>(ma, mb, p, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_fp8_scaled_mm_gelu_e4m3(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,
+                                int64_t ldw, const float* scale_a, const float* scale_b, int64_t n_per_scale,
+                                const void* bias, int bias_dtype, const float* q_scale, void* out_q, int64_t ldq,
+                                void* stream) {
+  CUtensorMap ma, mb;
+  int rc = gemm_common(a, M, K, lda, w, N, ldw, scale_a, scale_b, n_per_scale, &ma, &mb);
+  if (rc || M == 0) return rc;
+  if (out_q == nullptr || q_scale == nullptr || !aligned16(out_q) || ldq % 16 || ldq < N)
+    return fail(OGX_EINVAL, "output");
+  if (bias != nullptr && (!dtype_ok(bias_dtype) || !aligned16(bias))) return fail(OGX_EINVAL, "bias");
+  ogx::gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.scale_a = scale_a;
+  p.scale_b = scale_b;
+  p.n_per_scale = static_cast<int>(n_per_scale);
+  p.bias = bias;
+  p.bias_fp32 = bias_dtype == OGX_DTYPE_F32;
+  p.out_q = static_cast<uint8_t*>(out_q);
+  p.ldq = ldq;
+  p.q_scale = q_scale;
+  return gemm_launch<ogx::gemm::EPI_GELU_QUANT>(ma, mb, p, static_cast<cudaStream_t>(stream));
 }
 
 static int residual_gate_impl(int64_t a_k_block, const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N,

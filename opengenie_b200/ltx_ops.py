@@ -178,6 +178,28 @@ def fused_fp8_quantize_e4m3(x: torch.Tensor, input_scale: torch.Tensor, *, quant
     return q
 
 
+def fused_gelu_tanh_fp8_quantize_e4m3(x: torch.Tensor, input_scale: torch.Tensor, *,
+                                      return_gelu: bool = False):
+    """GELU (tanh approximation) fused with the per-tensor E4M3 quantiser.
+
+    Reference: fused_gelu_tanh_fp8_quantize_e4m3, ltx_serve/triton_ltx_ops.py:164-182; its torch path
+    (:166-169) is ``clamp(gelu(x, approximate="tanh") * input_scale.reciprocal(), -448, 448).to(e4m3)``.
+    With ``return_gelu`` the rounded GELU values are returned too, ``(q, gelu)``.
+    """
+    _require_cuda(x, input_scale)
+    if not x.is_contiguous() or input_scale.numel() != 1 or x.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("fp8_quantize_input")
+    if input_scale.dtype != torch.float32:
+        raise ValueError("input_scale")
+    q = torch.empty_strided(x.shape, x.stride(), device=x.device, dtype=torch.float8_e4m3fn)
+    gelu = torch.empty_like(x) if return_gelu else None
+    _lib.call(
+        "ogx_gelu_tanh_fp8_quantize_e4m3",
+        x.data_ptr(), _code(x), x.numel(), input_scale.data_ptr(), q.data_ptr(), _ptr(gelu), _stream(x),
+    )
+    return (q, gelu) if return_gelu else q
+
+
 # ---------------------------------------------------------------- bias add / residual
 def fused_bias_add_bf16(x: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
     """``x + bias.to(bf16)``; reference ltx_serve/triton_ltx_ops.py:185-201."""
@@ -347,6 +369,50 @@ def fp8_scaled_mm(
         scale_a.data_ptr(), scale_b.contiguous().data_ptr(), nps,
         _ptr(bias.contiguous()) if bias is not None else None, _code(bias) if bias is not None else DTYPE_BF16,
         out.data_ptr(), out.stride(0), _stream(qinput),
+    )
+    return out if given else out.reshape(*qinput.shape[:-1], N)
+
+
+def fp8_scaled_mm_gelu_e4m3(
+    qinput: torch.Tensor,
+    weight: torch.Tensor,
+    scale_a: torch.Tensor,
+    scale_b: torch.Tensor,
+    q_scale: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """The FFN's first projection with GELU and the next projection's quantiser in its epilogue:
+    ``fused_gelu_tanh_fp8_quantize_e4m3(fp8_scaled_mm(qinput, weight, scale_a, scale_b, bias=bias), q_scale)``
+    without the bf16 hidden activation in memory (ltx_serve/triton_ltx_ops.py:1695-1707, :164-169, as
+    ``_feedforward_without_out_bias`` :2796-2807 and ``fp8_linear_without_bias`` :770-771 chain them).
+    Returns e4m3 [..., N] (or the caller's [M, N] ``out``)."""
+    _require_cuda(qinput, weight, scale_a, scale_b, q_scale)
+    if qinput.dtype != torch.float8_e4m3fn or weight.dtype != torch.float8_e4m3fn:
+        raise ValueError("fp8_dtype")
+    a2 = qinput.reshape(-1, qinput.shape[-1])
+    if a2.stride(-1) != 1 or weight.stride(-1) != 1 or weight.ndim != 2 or weight.shape[1] != a2.shape[1]:
+        raise ValueError("fp8_shape")
+    M, K = a2.shape
+    N = weight.shape[0]
+    if scale_a.numel() != 1 or scale_a.dtype != torch.float32 or scale_b.dtype != torch.float32:
+        raise ValueError("scale")
+    if scale_b.numel() != 1:
+        raise ValueError("scale")
+    given = out is not None
+    if out is None:
+        out = torch.empty((M, N), device=qinput.device, dtype=torch.float8_e4m3fn)
+    if out.dtype != torch.float8_e4m3fn or out.ndim != 2 or out.shape != (M, N) or out.stride(1) != 1:
+        raise ValueError("out_shape: out must be a [M, N] e4m3 matrix with unit column stride")
+    if bias is not None and (bias.ndim != 1 or bias.shape[0] != N):
+        raise ValueError("bias_shape")
+    _lib.call(
+        "ogx_fp8_scaled_mm_gelu_e4m3",
+        a2.data_ptr(), M, K, a2.stride(0), weight.data_ptr(), N, weight.stride(0),
+        scale_a.data_ptr(), scale_b.contiguous().data_ptr(), N,
+        _ptr(bias.contiguous()) if bias is not None else None, _code(bias) if bias is not None else DTYPE_BF16,
+        _scale_ptr(q_scale), out.data_ptr(), out.stride(0), _stream(qinput),
     )
     return out if given else out.reshape(*qinput.shape[:-1], N)
 

@@ -150,6 +150,41 @@ def make_weights(seed: int = 0, *, dim: int = DIM, qkv_input_scale: float = 1.0,
     return BlockWeights(to_q, to_k, to_v, to_out, q_norm, k_norm, table.to(torch.float32))
 
 
+FFN_HIDDEN = 4 * DIM
+
+
+@dataclass
+class FfnWeights:
+    """The video feed-forward branch of the same layer: ``ff.net[0].proj`` (D -> 4D, with bias), GELU
+    (tanh), ``ff.net[2]`` (4D -> D, bias applied with the gated residual), and the layer's Ada table
+    (slots 3/4 for the AdaZero shift/scale, 5 for the gate)."""
+
+    proj: Fp8Linear
+    out: Fp8Linear
+    scale_shift_table: torch.Tensor
+    norm_eps: float = 1e-6
+
+    def to(self, device) -> "FfnWeights":
+        return FfnWeights(self.proj.to(device), self.out.to(device), self.scale_shift_table.to(device), self.norm_eps)
+
+
+def make_ffn_weights(seed: int = 0, *, dim: int = DIM, hidden: int = FFN_HIDDEN) -> FfnWeights:
+    """Random-init FFN weights (CPU): W ~ N(0, 0.02) pre-quantised to e4m3 with amax/448 scales, biases
+    ~ N(0, 0.01), table ~ N(0, 0.02).  Input scales are placeholders until calibrated."""
+    g = torch.Generator().manual_seed(seed)
+
+    def linear(n_out: int, n_in: int) -> Fp8Linear:
+        w = torch.randn((n_out, n_in), generator=g) * 0.02
+        q, s = quantize_weight_e4m3(w)
+        b = (torch.randn((n_out,), generator=g) * 0.01).to(torch.bfloat16)
+        return Fp8Linear(q, s, torch.tensor(1.0, dtype=torch.float32), b)
+
+    proj = linear(hidden, dim)
+    out = linear(dim, hidden)
+    table = torch.randn((ADA_SLOTS, dim), generator=g) * 0.02
+    return FfnWeights(proj, out, table.to(torch.float32))
+
+
 @dataclass
 class BlockInputs:
     x: torch.Tensor  # bf16 [1, L, D]

@@ -124,6 +124,21 @@ def quantize_e4m3(x, input_scale: float, *, in_dtype: str = "bf16", mode: str = 
     return f32_to_e4m3(t)
 
 
+def gelu_tanh(x, *, in_dtype: str = "bf16") -> np.ndarray:
+    """``torch.nn.functional.gelu(x, approximate="tanh")`` on a bf16 (or fp16) tensor on the CPU, as the
+    reference's torch path evaluates it (ltx_serve/triton_ltx_ops.py:166): fp32 math, one rounding to the
+    input dtype.  Returned as float32 values exactly representable in ``in_dtype``."""
+    dt = torch.bfloat16 if in_dtype == "bf16" else torch.float16
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(dt)
+    return torch.nn.functional.gelu(t, approximate="tanh").float().numpy()
+
+
+def gelu_tanh_quantize_e4m3(x, input_scale: float, *, in_dtype: str = "bf16") -> np.ndarray:
+    """``fused_gelu_tanh_fp8_quantize_e4m3`` torch path (ltx_serve/triton_ltx_ops.py:164-169): GELU (tanh)
+    rounded to the input dtype, then the torch-path quantiser on that tensor."""
+    return quantize_e4m3(gelu_tanh(x, in_dtype=in_dtype), input_scale, in_dtype=in_dtype)
+
+
 # ----------------------------------------------------------------------------- Ada / elementwise
 
 
@@ -365,3 +380,75 @@ def video_block_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, cos: torc
     gate = ada(2)
     yb = r16(y + r16(w.to_out.bias.float()))
     return r16(xf + r16(yb * gate))
+
+
+# ----------------------------------------------------------------------------- the video FFN branch
+
+
+def video_ffn(x, timestep_view, fw, *, eps: float = 1e-6, return_intermediates: bool = False):
+    """The video feed-forward branch in the reference's order and rounding points.
+
+    ltx_serve/triton_ltx_ops.py:3224-3258 with the production flags: AdaZero idx 3/4
+    (``fused_adazero_from_ada``) -> ``ff.net[0]``: E4M3 quant + FP8 proj + bias (FP8Linear.forward
+    :1676-1716) and GELU tanh -> ``ff.net[2]`` without bias (``_feedforward_without_out_bias``
+    :2796-2807: ``fp8_linear_without_bias`` :762-781) -> bias + gate (idx 5) + residual
+    (``fused_residual_gate_bias_from_ada`` :204-262).  ``fw`` carries the synthetic FfnWeights.
+    """
+    table = fw.scale_shift_table
+    tab_bf16 = table.dtype == torch.bfloat16
+    ts_bf16 = timestep_view.dtype == torch.bfloat16
+    norm = adazero_from_ada(x, eps, table, timestep_view, shift_index=3, scale_index=4, table_is_bf16=tab_bf16,
+                            ts_is_bf16=ts_bf16)
+    s1 = float(fw.proj.input_scale)
+    xq = quantize_e4m3(norm, s1)
+    hidden = fp8_linear(xq, s1, fw.proj.weight.view(torch.uint8).numpy(), float(fw.proj.weight_scale),
+                        _np(fw.proj.bias))
+    g = gelu_tanh(hidden)
+    s2 = float(fw.out.input_scale)
+    hq = quantize_e4m3(g, s2)
+    y = fp8_linear(hq, s2, fw.out.weight.view(torch.uint8).numpy(), float(fw.out.weight_scale))
+    out = residual_gate_bias_from_ada(x, y, _np(fw.out.bias), table, timestep_view, gate_index=5,
+                                      table_is_bf16=tab_bf16, ts_is_bf16=ts_bf16)
+    if return_intermediates:
+        return out, {"norm": norm, "xq": xq, "hidden": hidden, "gelu": g, "hq": hq, "y": y}
+    return out
+
+
+def video_ffn_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, fw, *, eps: float = 1e-6) -> torch.Tensor:
+    """The same branch with every contraction in fp32 torch (on the tensors' device): the timed CPU
+    baseline and the fp32 reference of the full-size GPU tolerance test.  Same stages and rounding
+    points as ``video_ffn``; the quantisers keep the reference's torch-path semantics (activations are
+    FP8 in the model), with 1/s kept in fp32 as the reference's CPU path computes it."""
+    dev = x.device
+
+    def r16(t):
+        return t.to(torch.bfloat16).float()
+
+    table = fw.scale_shift_table.to(dev).float()
+    if (fw.scale_shift_table.dtype == torch.bfloat16) != (timestep_view.dtype == torch.bfloat16):
+        table = r16(table)
+    ts = timestep_view.to(dev).float()
+
+    def ada(idx):
+        v = table[idx].view(1, 1, -1) + ts[:, :, idx, :]
+        return r16(v) if timestep_view.dtype == torch.bfloat16 else v
+
+    xf = x.float()
+    norm = r16(xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1 + ada(4)) + ada(3))
+
+    def quant(t, s):
+        r = torch.tensor(1.0, dtype=torch.float32, device=dev) / s.to(dev).float()
+        return torch.clamp(r16(t * r), -FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+
+    def lin(tq, s_in, l, bias=True):
+        acc = tq.reshape(-1, tq.shape[-1]).float() @ l.weight.to(dev).float().T
+        y = r16(acc * (s_in.to(dev).float() * l.weight_scale.to(dev).float()))
+        if bias:
+            y = r16(y + r16(l.bias.to(dev).float()))
+        return y.view(*tq.shape[:-1], -1)
+
+    hidden = lin(quant(norm, fw.proj.input_scale), fw.proj.input_scale, fw.proj)
+    g = torch.nn.functional.gelu(hidden.to(torch.bfloat16), approximate="tanh").float()
+    y = lin(quant(g, fw.out.input_scale), fw.out.input_scale, fw.out, bias=False)
+    yb = r16(y + r16(fw.out.bias.to(dev).float()))
+    return r16(xf + r16(yb * ada(5))).to(torch.bfloat16)

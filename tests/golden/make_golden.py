@@ -16,7 +16,11 @@ seeded inputs:
   split-RoPE restatement (tests/test_triton_ltx_ops.py:232-249);
 - block.npz: the video self-attention block composed from those functions with
   CPU ``torch._scaled_mm`` (the FP8 linears) and fp32 SDPA, for a 16-token input
-  with the synthetic weights of ``opengenie_b200.synthetic.make_weights(seed=7)``.
+  with the synthetic weights of ``opengenie_b200.synthetic.make_weights(seed=7)``;
+- gelu_quant.npz: ``fused_gelu_tanh_fp8_quantize_e4m3`` (:164-169) on every bf16 /
+  fp16 bit pattern, and the GELU it quantises;
+- ffn.npz: the video FFN branch (:3224-3258) composed the same way, 16 tokens,
+  ``opengenie_b200.synthetic.make_ffn_weights(seed=9)``.
 
 Inputs that are cheap to regenerate (seeded ``torch.Generator``) are stored too so
 the tests do not depend on regeneration.
@@ -149,6 +153,56 @@ def make_block(ops, rope_ref) -> None:
     )
 
 
+GELU_SCALES_BF16 = [1.0, 0.0371, 1.0 / 448.0]
+GELU_SCALES_F16 = [1.0, 0.0371]
+
+
+def make_gelu(ops) -> None:
+    """``fused_gelu_tanh_fp8_quantize_e4m3`` (torch path, triton_ltx_ops.py:164-169) on every bf16 and
+    fp16 bit pattern, and the GELU it quantises (the reference's own expression, :166)."""
+    allbits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    out = {}
+    for tag, dt, scales in (("bf16", torch.bfloat16, GELU_SCALES_BF16), ("f16", torch.float16, GELU_SCALES_F16)):
+        x = torch.from_numpy(allbits.view(np.int16)).view(dt).reshape(256, 256)
+        out[f"{tag}_gelu"] = bits(torch.nn.functional.gelu(x, approximate="tanh")).reshape(-1)
+        codes = [ops.fused_gelu_tanh_fp8_quantize_e4m3(x, torch.tensor(s, dtype=torch.float32))
+                 .view(torch.uint8).reshape(-1).numpy().copy() for s in scales]
+        out[f"{tag}_scales"] = np.array(scales, np.float32)
+        out[f"{tag}_codes"] = np.stack(codes)
+    np.savez_compressed(os.path.join(HERE, "gelu_quant.npz"), **out)
+
+
+def make_ffn(ops) -> None:
+    """The video FFN branch (triton_ltx_ops.py:3224-3258, production flags) composed from the reference's
+    CPU functions with CPU ``torch._scaled_mm``, for 16 tokens with the synthetic FFN weights of
+    ``opengenie_b200.synthetic.make_ffn_weights(seed=9)``."""
+    from opengenie_b200 import synthetic
+
+    cfg = synthetic.small_config(1, 2, 8)
+    inp = synthetic.make_inputs(cfg, seed=13)
+    fw = synthetic.make_ffn_weights(seed=9)
+    x, ts, table = inp.x, inp.timestep, fw.scale_shift_table
+    norm = ops.fused_adazero_from_ada(x, 1e-6, table, ts, shift_index=3, scale_index=4)
+    s1 = (norm.float().abs().amax() / 448.0).to(torch.float32)
+
+    def mm(q, s_a, lin):
+        return torch._scaled_mm(q.reshape(-1, q.shape[-1]), lin.weight.t(), scale_a=s_a, scale_b=lin.weight_scale,
+                                out_dtype=torch.bfloat16, use_fast_accum=True)
+
+    xq = ops.fused_fp8_quantize_e4m3(norm, s1)
+    hidden = ops.fused_bias_add_bf16(mm(xq, s1, fw.proj), fw.proj.bias)
+    gelu = torch.nn.functional.gelu(hidden, approximate="tanh")
+    s2 = (gelu.float().abs().amax() / 448.0).to(torch.float32)
+    hq = ops.fused_gelu_tanh_fp8_quantize_e4m3(hidden, s2)
+    y = mm(hq, s2, fw.out).reshape(1, -1, x.shape[-1])
+    out = ops.fused_residual_gate_bias_from_ada(x, y, fw.out.bias, table, ts, gate_index=5)
+    np.savez_compressed(
+        os.path.join(HERE, "ffn.npz"),
+        s1=s1.numpy(), s2=s2.numpy(), x=bits(x), out=bits(out), hidden=bits(hidden), xq=xq.view(torch.uint8).numpy(),
+        hq=hq.view(torch.uint8).numpy(), y=bits(y), seed_inputs=np.array(13), seed_weights=np.array(9),
+    )
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the plugyawn/opengenie checkout")
@@ -158,6 +212,8 @@ def main() -> None:
     make_quant(ops)
     make_ops(ops, rope_ref)
     make_block(ops, rope_ref)
+    make_gelu(ops)
+    make_ffn(ops)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))
