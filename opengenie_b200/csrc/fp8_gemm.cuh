@@ -3,7 +3,14 @@
 // A is the quantised activation [M, K] and W the quantised weight [N, K]
 // (nn.Linear layout), both K-major, which is exactly torch._scaled_mm(A, W.t()).
 //
-// Persistent kernel, one CTA per SM, 128x256 output tiles:
+// Persistent kernel, one CTA per SM, 128x256 output tiles (PAIR = false), or
+// CTA pairs (clusters of two) computing 256x256 tiles with tcgen05 cta_group::2
+// (PAIR = true): each CTA of the pair loads its 128 rows of A and half (128
+// rows) of the B tile, the pair's first CTA issues M=256 N=256 MMAs that read
+// both CTAs' shared memory, and each CTA receives its 128 rows of the result
+// in its own TMEM.  Per SM that halves the B bytes moved per FLOP, which is
+// what the single-CTA tiles are short of (L2 -> shared-memory traffic and
+// bytes in flight), and leaves room for a 6-deep ring.  Layout per CTA:
 //   warp 0      TMA producer: A/W tiles (128-byte swizzle) into a 4-stage ring
 //   warp 1      MMA issuer:   tcgen05.mma kind::f8f6f4, M=128 N=256 K=32,
 //                             fp32 accumulators in TMEM (2 x 256 columns, so
@@ -31,13 +38,19 @@
 namespace ogx {
 namespace gemm {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BM = 128;  // A rows per CTA
+constexpr int BN = 256;  // output columns per tile
 constexpr int BK = 128;  // fp8 elements = bytes per row of a stage
-constexpr int STAGES = 4;
 constexpr int A_STAGE_BYTES = BM * BK;
-constexpr int B_STAGE_BYTES = BN * BK;
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+// B rows a CTA loads per stage, ring depth and stage size: single CTAs load all 256 B rows (4 stages of
+// 48 KB), pairs 128 each (6 stages of 32 KB); both rings take 192 KB.
+__host__ __device__ constexpr int b_rows(bool pair) { return pair ? BN / 2 : BN; }
+__host__ __device__ constexpr int stages(bool pair) { return pair ? 6 : 4; }
+__host__ __device__ constexpr int stage_bytes(bool pair) { return A_STAGE_BYTES + b_rows(pair) * BK; }
+constexpr int MAX_STAGES = 6;
+constexpr int STAGE_BYTES = stage_bytes(false);
+constexpr int STAGES = stages(false);
+static_assert(stages(true) * stage_bytes(true) == STAGES * STAGE_BYTES, "both rings take the same shared memory");
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
 constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
@@ -89,8 +102,8 @@ __device__ __forceinline__ float ld1(const void* p, int64_t i) {
 }
 
 struct SharedState {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[MAX_STAGES];   // (pairs: the first CTA's counts both CTAs' bytes)
+  uint64_t empty[MAX_STAGES];
   uint64_t tmem_full[NUM_ACC];
   uint64_t tmem_empty[NUM_ACC];
   uint64_t drained;
@@ -98,7 +111,7 @@ struct SharedState {
   int abort;
 };
 
-template <int EPI>
+template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     Params p) {
@@ -108,21 +121,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem_aligned = smem_raw + (smem_base - smem_u32(smem_raw));
 
+  constexpr int NST = stages(PAIR);
+  constexpr int SBYTES = stage_bytes(PAIR);
+  constexpr int TM = PAIR ? 2 * BM : BM;  // output rows per tile
   const uint32_t warp = warp_idx();
   const uint32_t lane = threadIdx.x & 31;
-  const int num_m = (p.M + BM - 1) / BM;
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;  // 0: the pair's first CTA (issues the MMAs)
+  const int num_m = (p.M + TM - 1) / TM;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_k = (p.K + BK - 1) / BK;
+  const int tile0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tile_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&st.full[s], 1);
       mbar_init(&st.empty[s], 1);
     }
     for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&st.tmem_full[a], 1);
-      mbar_init(&st.tmem_empty[a], 256);
+      // single CTA: every epilogue thread arrives; pairs: one arrival per epilogue warp of both CTAs
+      mbar_init(&st.tmem_empty[a], PAIR ? 16 : 256);
     }
     mbar_init(&st.drained, 1);
     st.abort = 0;
@@ -133,11 +153,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_b);
   }
   if (warp == 1) {
-    tmem_alloc(&st.tmem_base, TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(&st.tmem_base, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&st.tmem_base, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   pdl_wait();  // everything above touches only this CTA's shared memory and TMEM
-  float* col_bias = reinterpret_cast<float*>(smem_aligned + STAGES * STAGE_BYTES);
+  float* col_bias = reinterpret_cast<float*>(smem_aligned + NST * SBYTES);
   float* col_gate = col_bias + RES_MAX_N;
   const bool gate_uniform = p.ts_stride_t == 0;
   if (EPI == EPI_RESIDUAL) {
@@ -157,6 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
   tc_fence_after();
   const uint32_t tmem_base = st.tmem_base;
   volatile int* abort = &st.abort;
@@ -168,36 +194,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % num_m) * BM;
-        const int n0 = (tile / num_m) * BN;
+      for (int tile = tile0; tile < num_tiles && ok; tile += tile_step) {
+        const int m0 = (tile % num_m) * TM + static_cast<int>(crank) * BM;  // this CTA's A rows
+        const int n0 = (tile / num_m) * BN + static_cast<int>(crank) * b_rows(PAIR);  // this CTA's B rows
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&st.empty[stage], phase ^ 1u, abort)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem_aligned + stage * STAGE_BYTES;
+          uint8_t* sa = smem_aligned + stage * SBYTES;
           uint8_t* sb = sa + A_STAGE_BYTES;
-          mbar_arrive_expect_tx(&st.full[stage], STAGE_BYTES);
-          if (p.a_k_block > 0)
-            tma_load_3d(sa, &tmap_a, &st.full[stage], (kb * BK) % p.a_k_block, m0, (kb * BK) / p.a_k_block);
-          else
-            tma_load_2d(sa, &tmap_a, &st.full[stage], kb * BK, m0);
-          tma_load_2d(sb, &tmap_b, &st.full[stage], kb * BK, n0);
+          if (PAIR) {
+            // both CTAs' copies complete on the first CTA's barrier, which expects both
+            const uint32_t fb = cluster_addr(&st.full[stage], 0);
+            if (crank == 0) mbar_arrive_expect_tx(&st.full[stage], 2 * SBYTES);
+            if (p.a_k_block > 0)
+              tma_load_3d_pair(sa, &tmap_a, fb, (kb * BK) % p.a_k_block, m0, (kb * BK) / p.a_k_block);
+            else
+              tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, m0);
+            tma_load_2d_pair(sb, &tmap_b, fb, kb * BK, n0);
+          } else {
+            mbar_arrive_expect_tx(&st.full[stage], SBYTES);
+            if (p.a_k_block > 0)
+              tma_load_3d(sa, &tmap_a, &st.full[stage], (kb * BK) % p.a_k_block, m0, (kb * BK) / p.a_k_block);
+            else
+              tma_load_2d(sa, &tmap_a, &st.full[stage], kb * BK, m0);
+            tma_load_2d(sb, &tmap_b, &st.full[stage], kb * BK, n0);
+          }
           ++issued;
-          if (++stage == STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      if (!ok) {
-        // Let the copies already in flight land before the CTA exits.
-        for (int i = 0; i < STAGES && i < issued; ++i) {
+      if (!ok && (!PAIR || crank == 0)) {
+        // Let the copies already in flight land before the CTA exits (a pair's first CTA counts the
+        // second's copies too, and the pair leaves together through the closing cluster barrier).
+        for (int i = 0; i < NST && i < issued; ++i) {
           int s = stage - 1 - i;
           uint32_t ph = phase;
           if (s < 0) {
-            s += STAGES;
+            s += NST;
             ph ^= 1u;
           }
           mbar_wait(&st.full[s], ph, nullptr);
@@ -206,13 +244,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
-      constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, BM, BN);
+    if ((!PAIR || crank == 0) && elect_one()) {
+      constexpr uint32_t idesc = make_idesc(0, 0, 0, 0, TM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = tile0; tile < num_tiles && ok; tile += tile_step, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&st.tmem_empty[acc], acc_phase ^ 1u, abort)) {
@@ -227,24 +265,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_base + stage * STAGE_BYTES;
+          const uint32_t sa = smem_base + stage * SBYTES;
           const uint32_t sb = sa + A_STAGE_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint64_t adesc = make_sdesc_sw128(sa + kk * 32, 16, 1024);
             const uint64_t bdesc = make_sdesc_sw128(sb + kk * 32, 16, 1024);
-            mma_f8_ss(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if (PAIR)
+              mma_f8_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              mma_f8_ss(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          mma_commit(&st.empty[stage]);
-          if (++stage == STAGES) {
+          if (PAIR) {  // both CTAs' producers refill this stage
+            mma_commit_pair(cluster_addr(&st.empty[stage], 0));
+            mma_commit_pair(cluster_addr(&st.empty[stage], 1));
+          } else {
+            mma_commit(&st.empty[stage]);
+          }
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) mma_commit(&st.tmem_full[acc]);
+        if (ok) {
+          if (PAIR) {
+            mma_commit_pair(cluster_addr(&st.tmem_full[acc], 0));
+            mma_commit_pair(cluster_addr(&st.tmem_full[acc], 1));
+          } else {
+            mma_commit(&st.tmem_full[acc]);
+          }
+        }
       }
       // every MMA issued above has completed once `drained` fires
-      mma_commit(&st.drained);
+      if (PAIR)
+        mma_commit_pair(cluster_addr(&st.drained, 0));
+      else
+        mma_commit(&st.drained);
       mbar_wait(&st.drained, 0, nullptr);
     }
   } else {
@@ -257,12 +313,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float qs = EPI == EPI_GELU_QUANT ? __ldg(p.q_scale) : 1.f;
     const float qr = __frcp_rn(qs);
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = tile0; tile < num_tiles; tile += tile_step, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&st.tmem_full[acc], acc_phase, abort)) break;
       tc_fence_after();
-      const int m0 = (tile % num_m) * BM;
+      const int m0 = (tile % num_m) * TM + static_cast<int>(crank) * BM;
       const int n0 = (tile / num_m) * BN + half * (BN / 2);
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
@@ -351,15 +407,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
       }
       tc_fence_before();
-      mbar_arrive(&st.tmem_empty[acc]);
+      if (PAIR) {
+        // one arrival per warp on the first CTA's barrier, once all of the warp's TMEM reads are done
+        __syncwarp();
+        if (lane == 0) {
+          if (crank == 0)
+            mbar_arrive(&st.tmem_empty[acc]);
+          else
+            mbar_arrive_remote(cluster_addr(&st.tmem_empty[acc], 0));
+        }
+      } else {
+        mbar_arrive(&st.tmem_empty[acc]);
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // neither CTA leaves (or frees TMEM) while the other may still signal it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 

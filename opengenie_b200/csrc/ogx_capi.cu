@@ -54,19 +54,37 @@ bool pdl_enabled() {
   return on;
 }
 
+// cluster_x > 1 launches clusters of that many CTAs along x (the GEMM's CTA pairs).
 template <typename... KArgs, typename... Args>
-void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+void launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, unsigned cluster_x,
+                    Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = n;
   cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  launch_cluster(kernel, grid, block, smem, s, 1u, std::forward<Args>(args)...);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -464,6 +482,26 @@ int ogx_video_qk_rmsnorm_rope(const void* q, const void* k, int64_t tokens, int6
 
 namespace {
 
+// CTA pairs (256x256 tiles, tcgen05 cta_group::2) or single CTAs (128x256 tiles), whichever the
+// persistent schedule finishes sooner: the number of tiles the busiest pair or CTA computes, a pair
+// tile taking 0.89 of a single-CTA tile's time per SM (measured: 334 vs 375 us at 9216x12288x4096).
+// Pairs lose where their coarser tiles leave a short last round (the 1152-row slices of 8 GPUs).
+// OGX_GEMM_PAIRS=0 keeps single CTAs.
+bool gemm_use_pairs(int64_t M, int64_t N) {
+  static const bool on = [] {
+    const char* e = getenv("OGX_GEMM_PAIRS");
+    return e == nullptr || e[0] != '0';
+  }();
+  if (!on || M <= ogx::gemm::BM) return false;
+  const int64_t nn = (N + ogx::gemm::BN - 1) / ogx::gemm::BN;
+  const int64_t single = (M + ogx::gemm::BM - 1) / ogx::gemm::BM * nn;
+  const int64_t pair = (M + 2 * ogx::gemm::BM - 1) / (2 * ogx::gemm::BM) * nn;
+  const int64_t ctas = sm_count(), pairs = sm_count() / 2;
+  const double t_single = static_cast<double>((single + ctas - 1) / ctas);
+  const double t_pair = 0.89 * static_cast<double>((pair + pairs - 1) / pairs);
+  return t_pair < t_single;
+}
+
 int gemm_common(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                 const float* scale_a, const float* scale_b, int64_t n_per_scale, CUtensorMap* ma, CUtensorMap* mb,
                 int64_t a_k_block = 0) {
@@ -492,19 +530,52 @@ int gemm_common(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
   if (rc) return rc;
   const uint64_t db[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
   const uint64_t sb[1] = {static_cast<uint64_t>(ldw)};
-  const uint32_t bb[2] = {static_cast<uint32_t>(ogx::gemm::BK), static_cast<uint32_t>(ogx::gemm::BN)};
+  const uint32_t bb[2] = {static_cast<uint32_t>(ogx::gemm::BK),
+                         static_cast<uint32_t>(ogx::gemm::b_rows(gemm_use_pairs(M, N)))};
   return make_map(mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, db, sb, bb);
 }
 
 template <int EPI>
 int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::Params& p, cudaStream_t s) {
-  auto kern = ogx::gemm::fp8_gemm_kernel<EPI>;
   const int smem = EPI == ogx::gemm::EPI_RESIDUAL ? ogx::gemm::SMEM_BYTES_RESIDUAL : ogx::gemm::SMEM_BYTES;
   if (EPI == ogx::gemm::EPI_RESIDUAL && p.N > ogx::gemm::RES_MAX_N)
     return fail(OGX_EINVAL, "shape: the residual epilogue supports N <= %d", ogx::gemm::RES_MAX_N);
+  const int num_n = (p.N + ogx::gemm::BN - 1) / ogx::gemm::BN;
+  if (gemm_use_pairs(p.M, p.N)) {  // the same choice gemm_common made for the B tensor map
+    auto kern = ogx::gemm::fp8_gemm_kernel<EPI, true>;
+    int rc = ensure_smem(kern, smem);
+    if (rc) return rc;
+    const int tiles = ((p.M + 2 * ogx::gemm::BM - 1) / (2 * ogx::gemm::BM)) * num_n;
+    // a persistent grid of pairs no larger than what can be resident at once (an SM left without a
+    // partner in its GPC cannot host a pair)
+    static int resident[3] = {0, 0, 0};
+    int& pairs = resident[EPI];
+    if (pairs == 0) {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(2 * (sm_count() / 2));
+      cfg.blockDim = dim3(ogx::gemm::kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      rc = check_cuda(cudaOccupancyMaxActiveClusters(&n, kern, &cfg), "cudaOccupancyMaxActiveClusters");
+      if (rc) return rc;
+      if (n < 1) return fail(OGX_ECUDA, "no CTA pair of the GEMM fits on this GPU");
+      pairs = n < sm_count() / 2 ? n : sm_count() / 2;
+    }
+    const int grid = 2 * (tiles < pairs ? tiles : pairs);
+    launch_cluster(kern, grid, ogx::gemm::kThreads, smem, s, 2u, ma, mb, p);
+    return check_launch("fp8_gemm_kernel (CTA pairs)");
+  }
+  auto kern = ogx::gemm::fp8_gemm_kernel<EPI, false>;
   int rc = ensure_smem(kern, smem);
   if (rc) return rc;
-  const int tiles = ((p.M + ogx::gemm::BM - 1) / ogx::gemm::BM) * ((p.N + ogx::gemm::BN - 1) / ogx::gemm::BN);
+  const int tiles = ((p.M + ogx::gemm::BM - 1) / ogx::gemm::BM) * num_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
   launch(kern, grid, ogx::gemm::kThreads, smem, s, ma, mb, p);
   return check_launch("fp8_gemm_kernel");

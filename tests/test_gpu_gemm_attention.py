@@ -115,6 +115,38 @@ def test_fp8_gemm_residual_epilogue_vs_oracle(ops):
     assert ok, worst
 
 
+@pytest.mark.parametrize("M,blocks", [(4608, 2), (1152, 8), (300, 4)])
+def test_fp8_gemm_residual_kblocked_equals_plain(ops, M, blocks):
+    """The out-projection reading A as `blocks` column blocks [blocks][M][K/blocks] (the Ulysses receive
+    buffer, through a 3-D tensor map) equals the same GEMM on the assembled [M, K] operand, bit for bit,
+    for shapes that run as CTA pairs (M = 4608) and as single CTAs."""
+    from opengenie_b200 import _lib, ltx_ops
+
+    K, N = 4096, 4096
+    kb = K // blocks
+    g = torch.Generator(device="cuda").manual_seed(M + blocks)
+    a = (torch.randn((M, K), device="cuda", generator=g) * 64).clamp(-448, 448).to(torch.float8_e4m3fn)
+    w = (torch.randn((N, K), device="cuda", generator=g) * 64).clamp(-448, 448).to(torch.float8_e4m3fn)
+    sa, sw = torch.tensor(2e-4, device="cuda"), torch.tensor(1e-3, device="cuda")
+    bias = (torch.randn((N,), device="cuda", generator=g) * 0.01).to(torch.bfloat16)
+    x = torch.randn((1, M, N), device="cuda", generator=g).to(torch.bfloat16)
+    table = torch.randn((6, N), device="cuda", generator=g) * 0.02
+    ts = torch.randn((1, 1, 6 * N), device="cuda", generator=g).to(torch.bfloat16).expand(1, M, 6 * N)
+    plain = ops.fp8_scaled_mm_residual_gate(a.view(1, M, K), w, sa, sw, bias, x, table, ts, gate_index=2)
+    a_blocked = a.view(M, blocks, kb).transpose(0, 1).contiguous()  # [blocks][M][kb]
+    ts_view = ltx_ops._ts_view(x, table, ts)
+    out = torch.empty_like(x)
+    _lib.call(
+        "ogx_fp8_scaled_mm_residual_gate_kblocked",
+        a_blocked.data_ptr(), M, K, kb, w.data_ptr(), N, w.stride(0), sa.data_ptr(), sw.data_ptr(), N,
+        bias.data_ptr(), ltx_ops._code(bias), x.data_ptr(), x.stride(1), table.data_ptr(), ltx_ops._code(table),
+        table.stride(0), ts_view.data_ptr(), ltx_ops._code(ts_view), ts_view.stride(1), ts_view.stride(2), 2,
+        out.data_ptr(), out.stride(1), ltx_ops._stream(x),
+    )
+    assert torch.equal(out, plain)
+    assert status_clean()
+
+
 def _qkv(B, L, H, seed, packed=False):
     g = torch.Generator().manual_seed(seed)
     if packed:
