@@ -12,6 +12,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <atomic>
 #include <unordered_map>
 #include <utility>
 #include <cstdlib>
@@ -548,8 +549,13 @@ int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::P
     const int tiles = ((p.M + 2 * ogx::gemm::BM - 1) / (2 * ogx::gemm::BM)) * num_n;
     // a persistent grid of pairs no larger than what can be resident at once (an SM left without a
     // partner in its GPC cannot host a pair)
-    static int resident[3] = {0, 0, 0};
-    int& pairs = resident[EPI];
+    // looked up once per (epilogue, device); concurrent first calls compute the same value
+    static std::atomic<int> resident[3][64];
+    int dev = 0;
+    rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= 64) return fail(OGX_EINVAL, "device ordinal %d out of range", dev);
+    int pairs = resident[EPI][dev].load(std::memory_order_relaxed);
     if (pairs == 0) {
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = dim3(2 * (sm_count() / 2));
@@ -567,6 +573,7 @@ int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::P
       if (rc) return rc;
       if (n < 1) return fail(OGX_ECUDA, "no CTA pair of the GEMM fits on this GPU");
       pairs = n < sm_count() / 2 ? n : sm_count() / 2;
+      resident[EPI][dev].store(pairs, std::memory_order_relaxed);
     }
     const int grid = 2 * (tiles < pairs ? tiles : pairs);
     launch_cluster(kern, grid, ogx::gemm::kThreads, smem, s, 2u, ma, mb, p);
