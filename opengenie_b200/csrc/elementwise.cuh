@@ -560,9 +560,11 @@ __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* in, const 
   }
 }
 
-// One 128-thread CTA per token.
+// One 128-thread CTA per token.  Register budget for 8 CTAs (1024 threads) per SM: more tokens in
+// flight beat fewer, spill-free ones (79.6 vs 84.5 us at L=9216; batching both rows' loads ahead of one
+// barrier at 163 registers: 106 us).
 template <typename WT, typename CsT>
-__global__ void __launch_bounds__(kRowThreads) qk_rmsnorm_rope_kernel(RopeArgs a) {
+__global__ void __launch_bounds__(kRowThreads, 8) qk_rmsnorm_rope_kernel(RopeArgs a) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[2][4];
