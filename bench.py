@@ -358,6 +358,71 @@ def run_ffn(args) -> None:
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------- a stack of layers
+def layer_flops(L: int) -> float:
+    """Attention (bf16) + Q/K/V, out-projection and FFN projections (FP8) of one layer's video branches."""
+    return attn_flops(L) + 2.0 * L * 4096 * (3 * 4096 + 4096) + ffn_flops(L)
+
+
+def run_layers(args) -> None:
+    """``--branch layers``: the video branches (self-attention then FFN) of ``--layers`` DiT layers, one
+    denoising step through the stack per timed step, captured as one CUDA graph (1 GPU).  Layers cycle
+    through ``--distinct-weights`` random weight sets (every layer still holds its own device copy)."""
+    from opengenie_b200 import _lib, synthetic
+    from opengenie_b200.graphs import StepGraph
+    from opengenie_b200.video_layer import VideoLayer, VideoLayerStack
+
+    rank, world, local, pg = dist_setup(args.gpus)
+    if world != 1:
+        raise SystemExit("--branch layers runs on one GPU")
+    dev = torch.device("cuda", local)
+    cfg = synthetic.CONFIGS[args.config]
+    L = cfg.tokens
+    inp = synthetic.make_inputs(cfg, seed=1).to(dev)
+    sets = [(synthetic.make_weights(seed=100 + i), synthetic.make_ffn_weights(seed=200 + i))
+            for i in range(max(1, args.distinct_weights))]
+    stack = VideoLayerStack([VideoLayer(*sets[i % len(sets)], dev) for i in range(args.layers)])
+    pe = (inp.cos, inp.sin)
+    stack.calibrate_input_scales(inp.x, inp.timestep, pe)
+    out = torch.empty_like(inp.x)
+
+    def step():
+        stack(inp.x, inp.timestep, pe, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    graph = StepGraph(step, dev)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    status = _lib.device_status(clear=True)
+    finite = bool(torch.isfinite(out.float()).all())
+    per_layer = layer_flops(L)
+    line = {
+        "metric": f"video branches of {args.layers} DiT layers (self-attention + FFN) ms per denoising step at L={L}, 1 B200",
+        "value": args.layers * per_layer / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3 / args.layers, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 attention / e4m3 projections",
+        "data": "synthetic (seeded inputs, random-init weights)",
+        "config": {"workload": f"LTX-2.3 video DiT layers (self-attention + FFN), {args.config}", "tokens": L,
+                   "layers": args.layers, "distinct_weight_sets": len(sets),
+                   "flops_per_layer": per_layer, "launch": "one CUDA graph replay per step",
+                   "scope": "text and audio cross-attention branches of the layer are not included"},
+        "gpu_launches": stack.kernel_launches_per_step * args.steps, "clocks": clk.summary(),
+        "device_status": status, "output_finite": finite,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -371,12 +436,18 @@ def main() -> None:
     ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
                     help="N>1: peer stores over NVLink from the producing kernels, or NCCL all-to-alls")
     ap.add_argument("--phases", action="store_true", help="add a per-stage time breakdown (separate, untimed run)")
-    ap.add_argument("--branch", choices=["attention", "ffn"], default="attention",
-                    help="the video self-attention block (the headline) or the same layer's video FFN branch")
+    ap.add_argument("--branch", choices=["attention", "ffn", "layers"], default="attention",
+                    help="the video self-attention block (the headline), the same layer's video FFN branch, or "
+                         "a stack of layers' video branches")
+    ap.add_argument("--layers", type=int, default=48, help="--branch layers: layers in the stack")
+    ap.add_argument("--distinct-weights", type=int, default=2, help="--branch layers: random weight sets")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.branch == "ffn" and args.impl == "ours":
         run_ffn(args)
+        return
+    if args.branch == "layers" and args.impl == "ours":
+        run_layers(args)
         return
 
     if args.impl == "reference":
