@@ -258,6 +258,31 @@ def fused_residual_gate_bias_from_ada(
     return out
 
 
+_ZERO_BIAS: dict[tuple[torch.device, int], torch.Tensor] = {}
+
+
+def fused_residual_gate_from_ada(
+    x: torch.Tensor,
+    y: torch.Tensor,
+    scale_shift_table: torch.Tensor,
+    timestep: torch.Tensor,
+    *,
+    gate_index: int,
+    count_video_ada: bool = True,
+) -> torch.Tensor:
+    """``x + y * gate`` with the gate from the table + timestep and bf16 rounding after the product.
+
+    Reference: fused_residual_gate_from_ada, ltx_serve/triton_ltx_ops.py:640-694 (kernel :3612-3661):
+    ``bf16(x + bf16(y * gate))``.  That is the bias kernel with a zero bias (``bf16(y + 0) = y`` for bf16 y).
+    """
+    key = (x.device, x.shape[-1])
+    zero = _ZERO_BIAS.get(key)
+    if zero is None:
+        zero = _ZERO_BIAS[key] = torch.zeros(x.shape[-1], device=x.device, dtype=torch.bfloat16)
+    return fused_residual_gate_bias_from_ada(x, y, zero, scale_shift_table, timestep, gate_index=gate_index,
+                                             count_video_ada=count_video_ada)
+
+
 # ---------------------------------------------------------------- Q/K RMSNorm + split RoPE
 def fused_video_qk_rmsnorm_rope_guard_reason(
     q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor
@@ -315,6 +340,40 @@ def fused_video_qk_rmsnorm_rope(
         q_out.data_ptr(), k_out.data_ptr(), q_out.stride(1), _stream(q),
     )
     return q_out, k_out
+
+
+def fused_video_qkv_rmsnorm_rope_pack(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    q_weight: torch.Tensor,
+    k_weight: torch.Tensor,
+    eps: float,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+) -> torch.Tensor:
+    """Q/K RMSNorm + split RoPE as ``fused_video_qk_rmsnorm_rope``, packed with V into qkv [1, L, 3, 32, 128]
+    (the FlashAttention qkvpacked layout).
+
+    Reference: fused_video_qkv_rmsnorm_rope_pack, ltx_serve/triton_ltx_ops.py:381-429 (kernel :3980-4061).
+    q, k and v share their token stride.
+    """
+    reason = fused_video_qk_rmsnorm_rope_guard_reason(q, k, q_weight, k_weight, cos, sin)
+    if reason is not None:
+        raise ValueError(reason)
+    if v.shape != q.shape or v.dtype != torch.bfloat16 or not v.is_cuda or v.stride(-1) != 1 or v.stride(1) != q.stride(1):
+        raise ValueError("qkv_shape")
+    L = q.shape[1]
+    qkv = torch.empty((1, L, 3, 32, 128), device=q.device, dtype=torch.bfloat16)
+    _lib.call(
+        "ogx_video_qkv_rmsnorm_rope_scatter",
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), L, q.stride(1),
+        q_weight.contiguous().data_ptr(), k_weight.contiguous().data_ptr(), _code(q_weight), float(eps),
+        cos.data_ptr(), sin.data_ptr(), _code(cos), cos.stride(1), cos.stride(2),
+        qkv[:, :, 0].data_ptr(), qkv[:, :, 1].data_ptr(), qkv[:, :, 2].data_ptr(), qkv.stride(1), 0, 32,
+        _stream(q),
+    )
+    return qkv
 
 
 # ---------------------------------------------------------------- FP8 linears

@@ -20,7 +20,8 @@ seeded inputs:
 - gelu_quant.npz: ``fused_gelu_tanh_fp8_quantize_e4m3`` (:164-169) on every bf16 /
   fp16 bit pattern, and the GELU it quantises;
 - ffn.npz: the video FFN branch (:3224-3258) composed the same way, 16 tokens,
-  ``opengenie_b200.synthetic.make_ffn_weights(seed=9)``.
+  ``opengenie_b200.synthetic.make_ffn_weights(seed=9)``;
+- residual_nobias.npz: ``fused_residual_gate_from_ada`` (:640-694).
 
 Inputs that are cheap to regenerate (seeded ``torch.Generator``) are stored too so
 the tests do not depend on regeneration.
@@ -153,6 +154,19 @@ def make_block(ops, rope_ref) -> None:
     )
 
 
+def make_residual_nobias(ops) -> None:
+    """``fused_residual_gate_from_ada`` (:640-694, residual mode "triton_simple_bf16_round") on a
+    [1, 9, 2048] case with an fp32 table of 9 slots, gate idx 8."""
+    g = torch.Generator().manual_seed(2025)
+    x = torch.randn((1, 9, 2048), generator=g).to(torch.bfloat16)
+    y = torch.randn((1, 9, 2048), generator=g).to(torch.bfloat16)
+    table = torch.randn((9, 2048), generator=g)
+    ts = torch.randn((1, 9, 9 * 2048), generator=g).to(torch.bfloat16)
+    r = ops.fused_residual_gate_from_ada(x, y, table, ts, gate_index=8)
+    np.savez_compressed(os.path.join(HERE, "residual_nobias.npz"), x=bits(x), y=bits(y), table=table.numpy(),
+                        ts=bits(ts), out=bits(r))
+
+
 GELU_SCALES_BF16 = [1.0, 0.0371, 1.0 / 448.0]
 GELU_SCALES_F16 = [1.0, 0.0371]
 
@@ -214,6 +228,7 @@ def main() -> None:
     make_block(ops, rope_ref)
     make_gelu(ops)
     make_ffn(ops)
+    make_residual_nobias(ops)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

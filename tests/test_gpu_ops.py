@@ -222,3 +222,27 @@ def test_qkv_rope_scatter_layout(ops, world):
         got = send[:, :, j].permute(1, 0, 2, 3).reshape(1, 24, 4096)
         assert torch.equal(got, ref)
     assert status_clean()
+
+
+def test_qkv_rmsnorm_rope_pack_layout(ops):
+    """fused_video_qkv_rmsnorm_rope_pack: [1, L, 3, 32, 128] holding the roped q and k and the untouched v,
+    bit for bit the separate op's q/k."""
+    q, k, qw, kw, cos, sin = _rope_case(37, 9)
+    v = torch.randn((1, 37, 4096), generator=torch.Generator().manual_seed(10)).to(torch.bfloat16)
+    q, k, v, qw, kw, cos, sin = (t.cuda() for t in (q, k, v, qw, kw, cos, sin))
+    qkv = ops.fused_video_qkv_rmsnorm_rope_pack(q, k, v, qw, kw, 1e-6, cos, sin)
+    assert qkv.shape == (1, 37, 3, 32, 128)
+    rq, rk = ops.fused_video_qk_rmsnorm_rope(q, k, qw, kw, 1e-6, cos, sin)
+    for j, ref in enumerate((rq, rk, v)):
+        assert torch.equal(qkv[:, :, j].reshape(1, 37, 4096), ref)
+    with pytest.raises(ValueError, match="qkv_shape"):
+        ops.fused_video_qkv_rmsnorm_rope_pack(q, k, v[:, :36], qw, kw, 1e-6, cos, sin)
+    assert status_clean()
+
+
+def test_residual_gate_without_bias_bitwise_vs_golden(ops):
+    d = np.load(os.path.join(GOLD, "residual_nobias.npz"))
+    out = ops.fused_residual_gate_from_ada(from_bits(d["x"]), from_bits(d["y"]), torch.from_numpy(d["table"]).cuda(),
+                                           from_bits(d["ts"]), gate_index=8)
+    assert np.array_equal(bf16_bits(out).reshape(-1), d["out"].reshape(-1))
+    assert status_clean()

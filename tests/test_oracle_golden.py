@@ -228,3 +228,12 @@ def test_ffn_cpu_fp32_baseline_agrees_with_oracle():
     diff = np.abs(a - b)
     assert diff.sum() / np.abs(a).sum() <= 1e-3
     assert diff.max() <= 0.125
+
+
+def test_residual_gate_without_bias_oracle_bitwise():
+    """``fused_residual_gate_from_ada`` (:640-694) is the bias residual with a zero bias, bit for bit."""
+    d = g("residual_nobias.npz")
+    x, y = bf(d["x"]).reshape(1, 9, 2048), bf(d["y"]).reshape(1, 9, 2048)
+    ts = bf(d["ts"]).reshape(1, 9, 9, 2048)
+    out = O.residual_gate_bias_from_ada(x, y, np.zeros(2048, np.float32), d["table"], ts, gate_index=8)
+    assert np.array_equal(out.reshape(-1), bf(d["out"]).reshape(-1))
