@@ -58,6 +58,14 @@ int ogx_adazero_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t c
                          int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
                          int scale_index, float eps, void* y, void* stream);
 
+/* The AdaLN affine without the norm: y = bf16(bf16(x * bf16(1 + scale)) + shift), shift/scale from
+ * table + timestep as for ogx_adazero_from_ada (arguments likewise, no eps).
+ * Replaces fused_adaln_affine_from_ada, ltx_serve/triton_ltx_ops.py:94-141 (kernel :3469-3534). */
+int ogx_adaln_affine_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                              int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                              int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
+                              int scale_index, void* y, void* stream);
+
 /* Same, fused with the per-tensor E4M3 activation quantiser: q = quant(y)
  * (y itself is written only when y != NULL).  The codes equal
  * ogx_fp8_quantize_e4m3 applied to the bf16 y.

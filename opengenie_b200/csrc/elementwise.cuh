@@ -296,6 +296,31 @@ __global__ void __launch_bounds__(kRowThreads) adazero_from_ada_kernel(AdaArgs a
   }
 }
 
+// ----------------------------------------------------------------- AdaLN affine
+// y = bf16(bf16(x * bf16(1 + scale)) + shift), shift/scale from table + timestep (rounded as in
+// ada_values8): the reference's GPU kernel for fused_adaln_affine_from_ada (triton_ltx_ops.py:3469-3534),
+// which rounds after each op.  Eight columns per thread and iteration.
+template <typename TableT, typename TsT>
+__global__ void __launch_bounds__(256) adaln_affine_from_ada_kernel(AdaArgs a, int64_t cols) {
+  const TableT* table = static_cast<const TableT*>(a.table);
+  const TsT* ts = static_cast<const TsT*>(a.ts);
+  const int64_t nvec = a.rows * cols / 8;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    const int64_t row = v * 8 / cols;
+    const int64_t col = v * 8 - row * cols;
+    const int64_t b = row / a.tokens;
+    const TsT* tsr = ts + b * a.ts_stride_b + (row - b * a.tokens) * a.ts_stride_t + col;
+    float sh[8], sc[8], xf[8], o[8];
+    ada_values8<TableT, TsT>(table + a.shift_index * a.table_stride_row + col, tsr + a.shift_index * a.ts_stride_p, sh);
+    ada_values8<TableT, TsT>(table + a.scale_index * a.table_stride_row + col, tsr + a.scale_index * a.ts_stride_p, sc);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(a.x) + v), xf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = bf16_round(xf[i] * bf16_round(1.0f + sc[i])) + sh[i];
+    reinterpret_cast<uint4*>(a.y)[v] = pack8(o);
+  }
+}
+
 // ----------------------------------------------------------------- quantiser
 template <typename InT, int MODE>
 __global__ void __launch_bounds__(256) fp8_quantize_kernel(const InT* __restrict__ x, int64_t n,

@@ -266,6 +266,42 @@ int ogx_adazero_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t c
   return ada_dispatch(a, cols, table_dtype, timestep_dtype, false, 0, static_cast<cudaStream_t>(stream));
 }
 
+int ogx_adaln_affine_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                              int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                              int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
+                              int scale_index, void* y, void* stream) {
+  int rc = ada_guard(x, batch, tokens, cols, table, table_dtype, timestep, timestep_dtype, ts_stride_b, ts_stride_t,
+                     ts_stride_p, shift_index, scale_index);
+  if (rc) return rc;
+  if (y == nullptr || !aligned16(y)) return fail(OGX_EINVAL, "output");
+  ogx::AdaArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.table = table;
+  a.ts = timestep;
+  a.ts_stride_b = ts_stride_b;
+  a.ts_stride_t = ts_stride_t;
+  a.ts_stride_p = ts_stride_p;
+  a.table_stride_row = table_stride_row;
+  a.rows = batch * tokens;
+  a.tokens = tokens > 0 ? tokens : 1;
+  a.shift_index = shift_index;
+  a.scale_index = scale_index;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  if (a.rows == 0) return OGX_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(a.rows * cols / 8);
+  const bool tf = table_dtype == OGX_DTYPE_F32, sf = timestep_dtype == OGX_DTYPE_F32;
+  if (tf && sf)
+    ogx::adaln_affine_from_ada_kernel<float, float><<<grid, 256, 0, s>>>(a, cols);
+  else if (tf)
+    ogx::adaln_affine_from_ada_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>(a, cols);
+  else if (sf)
+    ogx::adaln_affine_from_ada_kernel<__nv_bfloat16, float><<<grid, 256, 0, s>>>(a, cols);
+  else
+    ogx::adaln_affine_from_ada_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>(a, cols);
+  return check_launch("adaln_affine_from_ada_kernel");
+}
+
 int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
                               int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
                               int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,

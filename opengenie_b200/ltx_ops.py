@@ -116,6 +116,36 @@ def fused_adazero_from_ada(
     return y
 
 
+def fused_adaln_affine_from_ada(
+    x: torch.Tensor,
+    scale_shift_table: torch.Tensor,
+    timestep: torch.Tensor,
+    *,
+    shift_index: int,
+    scale_index: int,
+) -> torch.Tensor:
+    """`x*(1+scale)+shift` (no norm) with shift/scale from the table + timestep, bf16 rounding after each op.
+
+    Reference: fused_adaln_affine_from_ada, ltx_serve/triton_ltx_ops.py:94-141 (GPU kernel :3469-3534).
+    """
+    global _VIDEO_TEXT_ADALN_CALLS
+    reason = ada_from_table_guard_reason(x, scale_shift_table, timestep)
+    if reason is not None:
+        raise ValueError(reason)
+    _check_index(scale_shift_table, shift_index, scale_index)
+    _VIDEO_TEXT_ADALN_CALLS += 1
+    ts_view = _ts_view(x, scale_shift_table, timestep)
+    y = torch.empty_like(x)
+    _lib.call(
+        "ogx_adaln_affine_from_ada",
+        x.data_ptr(), x.shape[0], x.shape[1], x.shape[2],
+        scale_shift_table.data_ptr(), _code(scale_shift_table), scale_shift_table.stride(0),
+        ts_view.data_ptr(), _code(ts_view), ts_view.stride(0), ts_view.stride(1), ts_view.stride(2),
+        shift_index, scale_index, y.data_ptr(), _stream(x),
+    )
+    return y
+
+
 def fused_adazero_from_ada_fp8(
     x: torch.Tensor,
     eps: float,

@@ -173,6 +173,16 @@ def adazero_from_ada(x, eps, table, ts_view, *, shift_index: int, scale_index: i
     return bf16_round(y.astype(np.float32))
 
 
+def adaln_affine_from_ada(x, table, ts_view, *, shift_index: int, scale_index: int, table_is_bf16=False,
+                          ts_is_bf16=True) -> np.ndarray:
+    """``fused_adaln_affine_from_ada``, ltx_serve/triton_ltx_ops.py:94-141 (kernel :3469-3534):
+    bf16(bf16(x * bf16(1 + scale)) + shift), Ada values rounded as in ``ada_value``."""
+    shift = ada_value(table, ts_view, shift_index, table_is_bf16=table_is_bf16, ts_is_bf16=ts_is_bf16)
+    scale = ada_value(table, ts_view, scale_index, table_is_bf16=table_is_bf16, ts_is_bf16=ts_is_bf16)
+    factor = bf16_round(np.float32(1.0) + scale)
+    return bf16_round(bf16_round(_np(x).astype(np.float32) * factor) + shift)
+
+
 def bias_add_bf16(x, bias) -> np.ndarray:
     """bf16(x + bf16(bias)); ltx_serve/triton_ltx_ops.py:3446-3464."""
     return bf16_round(_np(x) + bf16_round(_np(bias)))

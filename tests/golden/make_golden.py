@@ -21,7 +21,8 @@ seeded inputs:
   fp16 bit pattern, and the GELU it quantises;
 - ffn.npz: the video FFN branch (:3224-3258) composed the same way, 16 tokens,
   ``opengenie_b200.synthetic.make_ffn_weights(seed=9)``;
-- residual_nobias.npz: ``fused_residual_gate_from_ada`` (:640-694).
+- residual_nobias.npz: ``fused_residual_gate_from_ada`` (:640-694);
+- adaln_affine.npz: ``fused_adaln_affine_from_ada`` (:94-141).
 
 Inputs that are cheap to regenerate (seeded ``torch.Generator``) are stored too so
 the tests do not depend on regeneration.
@@ -167,6 +168,22 @@ def make_residual_nobias(ops) -> None:
                         ts=bits(ts), out=bits(r))
 
 
+def make_adaln_affine(ops) -> None:
+    """``fused_adaln_affine_from_ada`` (:94-141) on [1, 7, 4096] (fp32 table, bf16 timestep, idx 6/7) and
+    [1, 5, 2048] (bf16 table, idx 0/1): the reference's torch path there rounds after each op, like its
+    kernel (:3469-3534)."""
+    g = torch.Generator().manual_seed(2026)
+    out = {}
+    for tag, cols, rows, tdt, sh, sc in (("a", 4096, 7, torch.float32, 6, 7), ("b", 2048, 5, torch.bfloat16, 0, 1)):
+        x = torch.randn((1, rows, cols), generator=g).to(torch.bfloat16)
+        table = (torch.randn((9, cols), generator=g) * 0.5).to(tdt)
+        ts = torch.randn((1, rows, 9 * cols), generator=g).to(torch.bfloat16)
+        y = ops.fused_adaln_affine_from_ada(x, table, ts, shift_index=sh, scale_index=sc)
+        out.update({f"{tag}_x": bits(x), f"{tag}_table": table.float().numpy(), f"{tag}_table_bf16": np.array(tdt == torch.bfloat16),
+                    f"{tag}_ts": bits(ts), f"{tag}_idx": np.array([sh, sc]), f"{tag}_y": bits(y)})
+    np.savez_compressed(os.path.join(HERE, "adaln_affine.npz"), **out)
+
+
 GELU_SCALES_BF16 = [1.0, 0.0371, 1.0 / 448.0]
 GELU_SCALES_F16 = [1.0, 0.0371]
 
@@ -229,6 +246,7 @@ def main() -> None:
     make_gelu(ops)
     make_ffn(ops)
     make_residual_nobias(ops)
+    make_adaln_affine(ops)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

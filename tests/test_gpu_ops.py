@@ -246,3 +246,30 @@ def test_residual_gate_without_bias_bitwise_vs_golden(ops):
                                            from_bits(d["ts"]), gate_index=8)
     assert np.array_equal(bf16_bits(out).reshape(-1), d["out"].reshape(-1))
     assert status_clean()
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_adaln_affine_bitwise_vs_golden(ops, tag):
+    d = np.load(os.path.join(GOLD, "adaln_affine.npz"))
+    table = torch.from_numpy(d[f"{tag}_table"])
+    if bool(d[f"{tag}_table_bf16"]):
+        table = table.to(torch.bfloat16)
+    sh, sc = (int(i) for i in d[f"{tag}_idx"])
+    out = ops.fused_adaln_affine_from_ada(from_bits(d[f"{tag}_x"]), table.cuda(), from_bits(d[f"{tag}_ts"]),
+                                          shift_index=sh, scale_index=sc)
+    assert np.array_equal(bf16_bits(out), d[f"{tag}_y"])
+    assert status_clean()
+
+
+@pytest.mark.parametrize("table_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("ts_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("uniform", [False, True])
+def test_adaln_affine_bitwise_vs_oracle(ops, table_dtype, ts_dtype, uniform):
+    x, table, ts = _ada_case(13, 4096, table_dtype, ts_dtype, uniform, seed=21)
+    out = ops.fused_adaln_affine_from_ada(x.cuda(), table.cuda(), ts.cuda() if not uniform else
+                                          ts[:, :1].cuda().expand(ts.shape), shift_index=6 % table.shape[0],
+                                          scale_index=1)
+    ref = O.adaln_affine_from_ada(x, table, ts.reshape(1, 13, table.shape[0], 4096), shift_index=6 % table.shape[0],
+                                  scale_index=1, table_is_bf16=table_dtype == torch.bfloat16,
+                                  ts_is_bf16=ts_dtype == torch.bfloat16)
+    assert np.array_equal(to_np(out), ref)

@@ -237,3 +237,16 @@ def test_residual_gate_without_bias_oracle_bitwise():
     ts = bf(d["ts"]).reshape(1, 9, 9, 2048)
     out = O.residual_gate_bias_from_ada(x, y, np.zeros(2048, np.float32), d["table"], ts, gate_index=8)
     assert np.array_equal(out.reshape(-1), bf(d["out"]).reshape(-1))
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_adaln_affine_oracle_bitwise(tag):
+    """``fused_adaln_affine_from_ada`` (:94-141): the oracle equals the reference's torch path bit for bit."""
+    d = g("adaln_affine.npz")
+    x = bf(d[f"{tag}_x"])
+    rows, cols = x.shape[1], x.shape[2]
+    ts = bf(d[f"{tag}_ts"]).reshape(1, rows, 9, cols)
+    sh, sc = (int(i) for i in d[f"{tag}_idx"])
+    out = O.adaln_affine_from_ada(x, d[f"{tag}_table"], ts, shift_index=sh, scale_index=sc,
+                                  table_is_bf16=bool(d[f"{tag}_table_bf16"]))
+    assert np.array_equal(out, bf(d[f"{tag}_y"]))
