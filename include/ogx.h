@@ -58,6 +58,13 @@ int ogx_adazero_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t c
                          int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
                          int scale_index, float eps, void* y, void* stream);
 
+/* Optional per-head gate of the attention output: y = bf16(x * gates[row, col / dim_head]); x, y bf16
+ * [rows, heads * dim_head] contiguous (dim_head a multiple of 8), gates bf16 with element strides
+ * gate_stride_row, gate_stride_head.  Replaces fused_head_gate_mul_bf16,
+ * ltx_serve/triton_ltx_ops.py:614-637 (kernel :3584-3609). */
+int ogx_head_gate_mul_bf16(const void* x, int64_t rows, int64_t heads, int64_t dim_head, const void* gates,
+                           int64_t gate_stride_row, int64_t gate_stride_head, void* y, void* stream);
+
 /* The AdaLN affine without the norm: y = bf16(bf16(x * bf16(1 + scale)) + shift), shift/scale from
  * table + timestep as for ogx_adazero_from_ada (arguments likewise, no eps).
  * Replaces fused_adaln_affine_from_ada, ltx_serve/triton_ltx_ops.py:94-141 (kernel :3469-3534). */

@@ -296,6 +296,28 @@ __global__ void __launch_bounds__(kRowThreads) adazero_from_ada_kernel(AdaArgs a
   }
 }
 
+// ----------------------------------------------------------------- per-head gate
+// y = bf16(x * gate[row, col / dim_head]) for bf16 x [rows, cols] and bf16 gates: the optional gated
+// attention of the video self-attention branch (fused_head_gate_mul_bf16, triton_ltx_ops.py:614-637,
+// kernel :3584-3609).  dim_head is a multiple of 8, so the 8 columns of a vector share one gate.
+__global__ void __launch_bounds__(256) head_gate_mul_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                             int64_t cols, const __nv_bfloat16* __restrict__ gates,
+                                                             int64_t gate_stride_row, int64_t gate_stride_head,
+                                                             int dim_head, __nv_bfloat16* __restrict__ y) {
+  const int64_t nvec = rows * cols / 8;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    const int64_t row = v * 8 / cols;
+    const int64_t col = v * 8 - row * cols;
+    const float g = __bfloat162float(gates[row * gate_stride_row + (col / dim_head) * gate_stride_head]);
+    float f[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(x) + v), f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] *= g;
+    reinterpret_cast<uint4*>(y)[v] = pack8(f);
+  }
+}
+
 // ----------------------------------------------------------------- AdaLN affine
 // y = bf16(bf16(x * bf16(1 + scale)) + shift), shift/scale from table + timestep (rounded as in
 // ada_values8): the reference's GPU kernel for fused_adaln_affine_from_ada (triton_ltx_ops.py:3469-3534),

@@ -302,6 +302,20 @@ int ogx_adaln_affine_from_ada(const void* x, int64_t batch, int64_t tokens, int6
   return check_launch("adaln_affine_from_ada_kernel");
 }
 
+int ogx_head_gate_mul_bf16(const void* x, int64_t rows, int64_t heads, int64_t dim_head, const void* gates,
+                           int64_t gate_stride_row, int64_t gate_stride_head, void* y, void* stream) {
+  if (x == nullptr || gates == nullptr || y == nullptr) return fail(OGX_EINVAL, "null_pointer");
+  if (rows < 0 || heads < 1 || dim_head < 8 || dim_head % 8) return fail(OGX_EINVAL, "shape");
+  if (!aligned16(x) || !aligned16(y) || (reinterpret_cast<uintptr_t>(gates) & 1u)) return fail(OGX_EINVAL, "alignment");
+  if (rows == 0) return OGX_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t cols = heads * dim_head;
+  ogx::head_gate_mul_kernel<<<grid_for(rows * cols / 8), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(x), rows, cols, static_cast<const __nv_bfloat16*>(gates), gate_stride_row,
+      gate_stride_head, static_cast<int>(dim_head), static_cast<__nv_bfloat16*>(y));
+  return check_launch("head_gate_mul_kernel");
+}
+
 int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
                               int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
                               int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,

@@ -186,6 +186,26 @@ def fused_adazero_from_ada_fp8(
     return (q, y) if return_bf16 else q
 
 
+def fused_head_gate_mul_bf16(out: torch.Tensor, gates: torch.Tensor, heads: int, dim_head: int) -> torch.Tensor:
+    """``out.view(B, L, H, d) * gates[..., None]`` (bf16): the optional per-head gate of the attention output.
+
+    Reference: fused_head_gate_mul_bf16, ltx_serve/triton_ltx_ops.py:614-637 (kernel :3584-3609; guard
+    ``_can_use_fused_head_gate_mul`` :1612-1623).
+    """
+    _require_cuda(out, gates)
+    if out.dtype != torch.bfloat16 or not out.is_contiguous() or out.ndim != 3 or out.shape[-1] != heads * dim_head:
+        raise ValueError("out_shape")
+    if gates.dtype != torch.bfloat16 or gates.shape != (out.shape[0], out.shape[1], heads):
+        raise ValueError("gates_shape")
+    g2 = gates.reshape(-1, heads)
+    y = torch.empty_like(out)
+    _lib.call(
+        "ogx_head_gate_mul_bf16", out.data_ptr(), out.numel() // out.shape[-1], heads, dim_head, g2.data_ptr(),
+        g2.stride(0), g2.stride(1), y.data_ptr(), _stream(out),
+    )
+    return y
+
+
 # ---------------------------------------------------------------- quantiser
 def fused_fp8_quantize_e4m3(x: torch.Tensor, input_scale: torch.Tensor, *, quant_mode: int = QUANT_TORCH) -> torch.Tensor:
     """Per-tensor E4M3 quantisation, bit-exact to the reference's torch path.

@@ -173,6 +173,14 @@ def adazero_from_ada(x, eps, table, ts_view, *, shift_index: int, scale_index: i
     return bf16_round(y.astype(np.float32))
 
 
+def head_gate_mul_bf16(out, gates, heads: int, dim_head: int) -> np.ndarray:
+    """``fused_head_gate_mul_bf16``, ltx_serve/triton_ltx_ops.py:614-637: bf16(out * gate[head])."""
+    o = _np(out).astype(np.float32)
+    B, L, _ = o.shape
+    g = _np(gates).astype(np.float32).reshape(B, L, heads, 1)
+    return bf16_round(o.reshape(B, L, heads, dim_head) * g).reshape(B, L, heads * dim_head)
+
+
 def adaln_affine_from_ada(x, table, ts_view, *, shift_index: int, scale_index: int, table_is_bf16=False,
                           ts_is_bf16=True) -> np.ndarray:
     """``fused_adaln_affine_from_ada``, ltx_serve/triton_ltx_ops.py:94-141 (kernel :3469-3534):

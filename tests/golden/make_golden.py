@@ -22,7 +22,8 @@ seeded inputs:
 - ffn.npz: the video FFN branch (:3224-3258) composed the same way, 16 tokens,
   ``opengenie_b200.synthetic.make_ffn_weights(seed=9)``;
 - residual_nobias.npz: ``fused_residual_gate_from_ada`` (:640-694);
-- adaln_affine.npz: ``fused_adaln_affine_from_ada`` (:94-141).
+- adaln_affine.npz: ``fused_adaln_affine_from_ada`` (:94-141);
+- head_gate.npz: ``fused_head_gate_mul_bf16`` (:614-637).
 
 Inputs that are cheap to regenerate (seeded ``torch.Generator``) are stored too so
 the tests do not depend on regeneration.
@@ -184,6 +185,15 @@ def make_adaln_affine(ops) -> None:
     np.savez_compressed(os.path.join(HERE, "adaln_affine.npz"), **out)
 
 
+def make_head_gate(ops) -> None:
+    """``fused_head_gate_mul_bf16`` (:614-637, torch path there) on [1, 11, 32 x 128] with gates 2*sigmoid."""
+    g = torch.Generator().manual_seed(2027)
+    out = torch.randn((1, 11, 4096), generator=g).to(torch.bfloat16)
+    gates = (2.0 * torch.sigmoid(torch.randn((1, 11, 32), generator=g))).to(torch.bfloat16)
+    y = ops.fused_head_gate_mul_bf16(out, gates, 32, 128)
+    np.savez_compressed(os.path.join(HERE, "head_gate.npz"), out=bits(out), gates=bits(gates), y=bits(y))
+
+
 GELU_SCALES_BF16 = [1.0, 0.0371, 1.0 / 448.0]
 GELU_SCALES_F16 = [1.0, 0.0371]
 
@@ -247,6 +257,7 @@ def main() -> None:
     make_ffn(ops)
     make_residual_nobias(ops)
     make_adaln_affine(ops)
+    make_head_gate(ops)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

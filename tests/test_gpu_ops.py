@@ -273,3 +273,15 @@ def test_adaln_affine_bitwise_vs_oracle(ops, table_dtype, ts_dtype, uniform):
                                   scale_index=1, table_is_bf16=table_dtype == torch.bfloat16,
                                   ts_is_bf16=ts_dtype == torch.bfloat16)
     assert np.array_equal(to_np(out), ref)
+
+
+def test_head_gate_mul_bitwise_vs_golden(ops):
+    d = np.load(os.path.join(GOLD, "head_gate.npz"))
+    y = ops.fused_head_gate_mul_bf16(from_bits(d["out"]), from_bits(d["gates"]), 32, 128)
+    assert np.array_equal(bf16_bits(y), d["y"])
+    g = torch.Generator().manual_seed(3)
+    out = torch.randn((1, 300, 16 * 64), generator=g).to(torch.bfloat16)
+    gates = torch.rand((1, 300, 16), generator=g).to(torch.bfloat16)
+    y2 = ops.fused_head_gate_mul_bf16(out.cuda(), gates.cuda(), 16, 64)
+    assert np.array_equal(to_np(y2), O.head_gate_mul_bf16(out, gates, 16, 64))
+    assert status_clean()

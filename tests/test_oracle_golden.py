@@ -250,3 +250,9 @@ def test_adaln_affine_oracle_bitwise(tag):
     out = O.adaln_affine_from_ada(x, d[f"{tag}_table"], ts, shift_index=sh, scale_index=sc,
                                   table_is_bf16=bool(d[f"{tag}_table_bf16"]))
     assert np.array_equal(out, bf(d[f"{tag}_y"]))
+
+
+def test_head_gate_oracle_bitwise():
+    d = g("head_gate.npz")
+    out = O.head_gate_mul_bf16(bf(d["out"]), bf(d["gates"]), 32, 128)
+    assert np.array_equal(out, bf(d["y"]))
