@@ -73,6 +73,13 @@ int ogx_adaln_affine_from_ada(const void* x, int64_t batch, int64_t tokens, int6
                               int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
                               int scale_index, void* y, void* stream);
 
+/* y = bf16(x * gate), gate = the Ada value of slot gate_index (table + timestep, arguments as for
+ * ogx_adazero_from_ada).  Replaces fused_mul_from_ada, ltx_serve/triton_ltx_ops.py:695-741
+ * (kernel :3723-3771). */
+int ogx_mul_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table, int table_dtype,
+                     int64_t table_stride_row, const void* timestep, int timestep_dtype, int64_t ts_stride_b,
+                     int64_t ts_stride_t, int64_t ts_stride_p, int gate_index, void* y, void* stream);
+
 /* Same, fused with the per-tensor E4M3 activation quantiser: q = quant(y)
  * (y itself is written only when y != NULL).  The codes equal
  * ogx_fp8_quantize_e4m3 applied to the bf16 y.

@@ -30,6 +30,10 @@ _SIGNATURES: dict[str, list] = {
         c_int64, c_int64, c_int64, c_int, c_int, c_float, c_void_p, c_void_p,
     ],
     "ogx_head_gate_mul_bf16": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p],
+    "ogx_mul_from_ada": [
+        c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p, c_int,
+        c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p,
+    ],
     "ogx_adaln_affine_from_ada": [
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p, c_int,
         c_int64, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p,

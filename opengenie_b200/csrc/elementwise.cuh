@@ -318,11 +318,12 @@ __global__ void __launch_bounds__(256) head_gate_mul_kernel(const __nv_bfloat16*
   }
 }
 
-// ----------------------------------------------------------------- AdaLN affine
-// y = bf16(bf16(x * bf16(1 + scale)) + shift), shift/scale from table + timestep (rounded as in
-// ada_values8): the reference's GPU kernel for fused_adaln_affine_from_ada (triton_ltx_ops.py:3469-3534),
-// which rounds after each op.  Eight columns per thread and iteration.
-template <typename TableT, typename TsT>
+// ----------------------------------------------------------------- AdaLN affine / Ada multiply
+// MUL = false: y = bf16(bf16(x * bf16(1 + scale)) + shift), shift/scale from table + timestep (rounded as
+// in ada_values8): the reference's GPU kernel for fused_adaln_affine_from_ada (triton_ltx_ops.py:3469-3534),
+// which rounds after each op.  MUL = true: y = bf16(x * gate), gate = the Ada value of slot shift_index
+// (fused_mul_from_ada, :695-741, kernel :3723-3771).  Eight columns per thread and iteration.
+template <typename TableT, typename TsT, bool MUL>
 __global__ void __launch_bounds__(256) adaln_affine_from_ada_kernel(AdaArgs a, int64_t cols) {
   const TableT* table = static_cast<const TableT*>(a.table);
   const TsT* ts = static_cast<const TsT*>(a.ts);
@@ -335,10 +336,16 @@ __global__ void __launch_bounds__(256) adaln_affine_from_ada_kernel(AdaArgs a, i
     const TsT* tsr = ts + b * a.ts_stride_b + (row - b * a.tokens) * a.ts_stride_t + col;
     float sh[8], sc[8], xf[8], o[8];
     ada_values8<TableT, TsT>(table + a.shift_index * a.table_stride_row + col, tsr + a.shift_index * a.ts_stride_p, sh);
-    ada_values8<TableT, TsT>(table + a.scale_index * a.table_stride_row + col, tsr + a.scale_index * a.ts_stride_p, sc);
     unpack8(__ldg(reinterpret_cast<const uint4*>(a.x) + v), xf);
+    if (MUL) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = bf16_round(xf[i] * bf16_round(1.0f + sc[i])) + sh[i];
+      for (int i = 0; i < 8; ++i) o[i] = xf[i] * sh[i];
+    } else {
+      ada_values8<TableT, TsT>(table + a.scale_index * a.table_stride_row + col, tsr + a.scale_index * a.ts_stride_p,
+                               sc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = bf16_round(xf[i] * bf16_round(1.0f + sc[i])) + sh[i];
+    }
     reinterpret_cast<uint4*>(a.y)[v] = pack8(o);
   }
 }

@@ -266,12 +266,12 @@ int ogx_adazero_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t c
   return ada_dispatch(a, cols, table_dtype, timestep_dtype, false, 0, static_cast<cudaStream_t>(stream));
 }
 
-int ogx_adaln_affine_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
-                              int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
-                              int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
-                              int scale_index, void* y, void* stream) {
+static int ada_elementwise(bool mul, const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                    int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                    int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int idx0, int idx1, void* y,
+                    void* stream) {
   int rc = ada_guard(x, batch, tokens, cols, table, table_dtype, timestep, timestep_dtype, ts_stride_b, ts_stride_t,
-                     ts_stride_p, shift_index, scale_index);
+                     ts_stride_p, idx0, idx1);
   if (rc) return rc;
   if (y == nullptr || !aligned16(y)) return fail(OGX_EINVAL, "output");
   ogx::AdaArgs a{};
@@ -284,22 +284,34 @@ int ogx_adaln_affine_from_ada(const void* x, int64_t batch, int64_t tokens, int6
   a.table_stride_row = table_stride_row;
   a.rows = batch * tokens;
   a.tokens = tokens > 0 ? tokens : 1;
-  a.shift_index = shift_index;
-  a.scale_index = scale_index;
+  a.shift_index = idx0;
+  a.scale_index = idx1;
   a.y = static_cast<__nv_bfloat16*>(y);
   if (a.rows == 0) return OGX_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = grid_for(a.rows * cols / 8);
   const bool tf = table_dtype == OGX_DTYPE_F32, sf = timestep_dtype == OGX_DTYPE_F32;
+#define OGX_ADA_EW(T, S)                                                                   \
+  (mul ? ogx::adaln_affine_from_ada_kernel<T, S, true><<<grid, 256, 0, s>>>(a, cols)       \
+       : ogx::adaln_affine_from_ada_kernel<T, S, false><<<grid, 256, 0, s>>>(a, cols))
   if (tf && sf)
-    ogx::adaln_affine_from_ada_kernel<float, float><<<grid, 256, 0, s>>>(a, cols);
+    OGX_ADA_EW(float, float);
   else if (tf)
-    ogx::adaln_affine_from_ada_kernel<float, __nv_bfloat16><<<grid, 256, 0, s>>>(a, cols);
+    OGX_ADA_EW(float, __nv_bfloat16);
   else if (sf)
-    ogx::adaln_affine_from_ada_kernel<__nv_bfloat16, float><<<grid, 256, 0, s>>>(a, cols);
+    OGX_ADA_EW(__nv_bfloat16, float);
   else
-    ogx::adaln_affine_from_ada_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, s>>>(a, cols);
-  return check_launch("adaln_affine_from_ada_kernel");
+    OGX_ADA_EW(__nv_bfloat16, __nv_bfloat16);
+#undef OGX_ADA_EW
+  return check_launch(mul ? "mul_from_ada" : "adaln_affine_from_ada_kernel");
+}
+
+int ogx_adaln_affine_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                              int table_dtype, int64_t table_stride_row, const void* timestep, int timestep_dtype,
+                              int64_t ts_stride_b, int64_t ts_stride_t, int64_t ts_stride_p, int shift_index,
+                              int scale_index, void* y, void* stream) {
+  return ada_elementwise(false, x, batch, tokens, cols, table, table_dtype, table_stride_row, timestep,
+                         timestep_dtype, ts_stride_b, ts_stride_t, ts_stride_p, shift_index, scale_index, y, stream);
 }
 
 int ogx_head_gate_mul_bf16(const void* x, int64_t rows, int64_t heads, int64_t dim_head, const void* gates,
@@ -314,6 +326,13 @@ int ogx_head_gate_mul_bf16(const void* x, int64_t rows, int64_t heads, int64_t d
       static_cast<const __nv_bfloat16*>(x), rows, cols, static_cast<const __nv_bfloat16*>(gates), gate_stride_row,
       gate_stride_head, static_cast<int>(dim_head), static_cast<__nv_bfloat16*>(y));
   return check_launch("head_gate_mul_kernel");
+}
+
+int ogx_mul_from_ada(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table, int table_dtype,
+                     int64_t table_stride_row, const void* timestep, int timestep_dtype, int64_t ts_stride_b,
+                     int64_t ts_stride_t, int64_t ts_stride_p, int gate_index, void* y, void* stream) {
+  return ada_elementwise(true, x, batch, tokens, cols, table, table_dtype, table_stride_row, timestep,
+                         timestep_dtype, ts_stride_b, ts_stride_t, ts_stride_p, gate_index, gate_index, y, stream);
 }
 
 int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,

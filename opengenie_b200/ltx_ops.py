@@ -146,6 +146,79 @@ def fused_adaln_affine_from_ada(
     return y
 
 
+def fused_mul_from_ada(
+    x: torch.Tensor,
+    scale_shift_table: torch.Tensor,
+    timestep: torch.Tensor,
+    *,
+    gate_index: int,
+) -> torch.Tensor:
+    """``x * gate`` (bf16) with the gate from the table + timestep.
+
+    Reference: fused_mul_from_ada, ltx_serve/triton_ltx_ops.py:695-741 (GPU kernel :3723-3771).
+    """
+    global _VIDEO_TEXT_ADALN_CALLS
+    reason = ada_from_table_guard_reason(x, scale_shift_table, timestep)
+    if reason is not None:
+        raise ValueError(reason)
+    _check_index(scale_shift_table, gate_index)
+    _VIDEO_TEXT_ADALN_CALLS += 1
+    ts_view = _ts_view(x, scale_shift_table, timestep)
+    y = torch.empty_like(x)
+    _lib.call(
+        "ogx_mul_from_ada",
+        x.data_ptr(), x.shape[0], x.shape[1], x.shape[2],
+        scale_shift_table.data_ptr(), _code(scale_shift_table), scale_shift_table.stride(0),
+        ts_view.data_ptr(), _code(ts_view), ts_view.stride(0), ts_view.stride(1), ts_view.stride(2),
+        gate_index, y.data_ptr(), _stream(x),
+    )
+    return y
+
+
+def _row_broadcast(v: torch.Tensor, batch: int, tokens: int, reason: str) -> torch.Tensor:
+    """[S, D] per-row values (S = 1, batch or batch*tokens, the row mapping of the reference's explicit-value
+    kernels) as a [batch, tokens, ..., D]-indexable view without copying."""
+    D = v.shape[-1]
+    flat = v.reshape(-1, *v.shape[-2:]) if v.ndim >= 3 and v.shape[-2] != D else v.reshape(-1, D)
+    S = flat.shape[0]
+    if S == 1:
+        return flat.reshape(1, 1, *flat.shape[1:]).expand(batch, tokens, *flat.shape[1:])
+    if S == batch:
+        return flat.reshape(batch, 1, *flat.shape[1:]).expand(batch, tokens, *flat.shape[1:])
+    if S == batch * tokens:
+        return flat.reshape(batch, tokens, *flat.shape[1:])
+    raise ValueError(reason)
+
+
+def fused_adazero(x: torch.Tensor, eps: float, scale: torch.Tensor, shift: torch.Tensor) -> torch.Tensor:
+    """``rmsnorm(x)*(1+scale)+shift`` with explicit scale/shift (fp32 math, one bf16 rounding).
+
+    Reference: fused_adazero, ltx_serve/triton_ltx_ops.py:8-37 (kernel :3319-3357): scale/shift hold 1,
+    batch or batch*tokens rows of D values.  Runs the table kernel with a zero table and scale/shift as the
+    two timestep slots (``0 + v = v`` exactly).
+    """
+    _require_cuda(x, scale, shift)
+    if x.dtype != torch.bfloat16 or x.ndim < 2 or x.shape[-1] not in (2048, 4096) or not x.is_contiguous():
+        raise ValueError("x_shape")
+    D = x.shape[-1]
+    if scale.shape[-1] != D or shift.shape[-1] != D or scale.numel() != shift.numel() or scale.numel() % D:
+        raise ValueError("scale_shape")
+    x3 = x.reshape(-1, x.shape[-2], D) if x.ndim >= 3 else x.reshape(1, -1, D)
+    B, L = x3.shape[0], x3.shape[1]
+    dt = torch.float32 if torch.float32 in (scale.dtype, shift.dtype) else torch.bfloat16
+    slots = torch.stack([shift.reshape(-1, D).to(dt), scale.reshape(-1, D).to(dt)], dim=1)  # [S, 2, D]
+    ts = _row_broadcast(slots, B, L, "scale_shape")  # [B, L, 2, D]
+    table = torch.zeros((2, D), device=x.device, dtype=dt)
+    y = torch.empty_like(x3)
+    _lib.call(
+        "ogx_adazero_from_ada",
+        x3.data_ptr(), B, L, D, table.data_ptr(), _code(table), table.stride(0),
+        ts.data_ptr(), _code(ts), ts.stride(0), ts.stride(1), ts.stride(2), 0, 1, float(eps), y.data_ptr(),
+        _stream(x),
+    )
+    return y.reshape(x.shape)
+
+
 def fused_adazero_from_ada_fp8(
     x: torch.Tensor,
     eps: float,
@@ -331,6 +404,33 @@ def fused_residual_gate_from_ada(
         zero = _ZERO_BIAS[key] = torch.zeros(x.shape[-1], device=x.device, dtype=torch.bfloat16)
     return fused_residual_gate_bias_from_ada(x, y, zero, scale_shift_table, timestep, gate_index=gate_index,
                                              count_video_ada=count_video_ada)
+
+
+def fused_residual_gate_bf16(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    """``bf16(x + bf16(y * gate))`` with an explicit bf16 gate of 1, batch or batch*tokens rows.
+
+    Reference: fused_residual_gate_bf16, ltx_serve/triton_ltx_ops.py:590-611 (kernel :3552-3582; guard
+    ``_can_use_fused_residual_gate`` :1596-1609).  Runs the table residual kernel with a zero table and bias
+    and the gate as the timestep slot.
+    """
+    _require_cuda(x, y, gate)
+    if x.dtype != torch.bfloat16 or y.dtype != torch.bfloat16 or x.shape != y.shape or x.ndim < 2:
+        raise ValueError("x_shape")
+    if x.shape[-1] not in (2048, 4096) or not x.is_contiguous() or not y.is_contiguous():
+        raise ValueError("x_shape")
+    D = x.shape[-1]
+    if gate.dtype != torch.bfloat16 or gate.shape[-1] != D or gate.numel() % D:
+        raise ValueError("gate_shape")
+    x3 = x.reshape(-1, x.shape[-2], D) if x.ndim >= 3 else x.reshape(1, -1, D)
+    B, L = x3.shape[0], x3.shape[1]
+    ts = _row_broadcast(gate.reshape(-1, D), B, L, "gate_shape")  # [B, L, D]
+    key = (x.device, D)
+    zero = _ZERO_BIAS.get(key)
+    if zero is None:
+        zero = _ZERO_BIAS[key] = torch.zeros(D, device=x.device, dtype=torch.bfloat16)
+    out = fused_residual_gate_bias_from_ada(x3, y.reshape(x3.shape), zero, zero.view(1, D), ts, gate_index=0,
+                                            count_video_ada=False)
+    return out.reshape(x.shape)
 
 
 # ---------------------------------------------------------------- Q/K RMSNorm + split RoPE

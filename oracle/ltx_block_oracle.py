@@ -173,6 +173,27 @@ def adazero_from_ada(x, eps, table, ts_view, *, shift_index: int, scale_index: i
     return bf16_round(y.astype(np.float32))
 
 
+def adazero_explicit(x, eps, scale, shift) -> np.ndarray:
+    """``fused_adazero`` (ltx_serve/triton_ltx_ops.py:8-37, GPU kernel :3319-3357): rmsnorm(x) * (1 + scale)
+    + shift with explicit scale/shift rows (broadcast over the rows of x), exact math, one bf16 rounding."""
+    xf = _np(x).astype(np.float64)
+    inv = 1.0 / np.sqrt(np.mean(xf * xf, axis=-1, keepdims=True) + eps)
+    y = xf * inv * (1.0 + _np(scale).astype(np.float64)) + _np(shift).astype(np.float64)
+    return bf16_round(y.astype(np.float32))
+
+
+def mul_from_ada(x, table, ts_view, *, gate_index: int, table_is_bf16=False, ts_is_bf16=True) -> np.ndarray:
+    """``fused_mul_from_ada`` (ltx_serve/triton_ltx_ops.py:695-741, kernel :3723-3771): bf16(x * gate)."""
+    gate = ada_value(table, ts_view, gate_index, table_is_bf16=table_is_bf16, ts_is_bf16=ts_is_bf16)
+    return bf16_round(_np(x).astype(np.float32) * gate)
+
+
+def residual_gate_bf16(x, y, gate) -> np.ndarray:
+    """``fused_residual_gate_bf16`` (ltx_serve/triton_ltx_ops.py:590-611, kernel :3552-3582):
+    bf16(x + bf16(y * gate))."""
+    return bf16_round(_np(x).astype(np.float32) + bf16_round(_np(y).astype(np.float32) * _np(gate).astype(np.float32)))
+
+
 def head_gate_mul_bf16(out, gates, heads: int, dim_head: int) -> np.ndarray:
     """``fused_head_gate_mul_bf16``, ltx_serve/triton_ltx_ops.py:614-637: bf16(out * gate[head])."""
     o = _np(out).astype(np.float32)

@@ -23,7 +23,9 @@ seeded inputs:
   ``opengenie_b200.synthetic.make_ffn_weights(seed=9)``;
 - residual_nobias.npz: ``fused_residual_gate_from_ada`` (:640-694);
 - adaln_affine.npz: ``fused_adaln_affine_from_ada`` (:94-141);
-- head_gate.npz: ``fused_head_gate_mul_bf16`` (:614-637).
+- head_gate.npz: ``fused_head_gate_mul_bf16`` (:614-637);
+- ada_misc.npz: ``fused_mul_from_ada`` (:695-741), ``fused_residual_gate_bf16`` (:590-611) and
+  ``fused_adazero`` (:8-37).
 
 Inputs that are cheap to regenerate (seeded ``torch.Generator``) are stored too so
 the tests do not depend on regeneration.
@@ -194,6 +196,31 @@ def make_head_gate(ops) -> None:
     np.savez_compressed(os.path.join(HERE, "head_gate.npz"), out=bits(out), gates=bits(gates), y=bits(y))
 
 
+def make_ada_misc(ops) -> None:
+    """``fused_mul_from_ada`` (:695-741), ``fused_residual_gate_bf16`` (:590-611, per-token and per-sample gate)
+    and ``fused_adazero`` (:8-37, explicit per-sample scale/shift; its torch path rounds after each op)."""
+    g = torch.Generator().manual_seed(2028)
+    out = {}
+    x = torch.randn((1, 6, 4096), generator=g).to(torch.bfloat16)
+    table = torch.randn((9, 4096), generator=g) * 0.5
+    ts = torch.randn((1, 6, 9 * 4096), generator=g).to(torch.bfloat16)
+    out.update(mul_x=bits(x), mul_table=table.numpy(), mul_ts=bits(ts),
+               mul_y=bits(ops.fused_mul_from_ada(x, table, ts, gate_index=4)))
+    x = torch.randn((2, 5, 2048), generator=g).to(torch.bfloat16)
+    y = torch.randn((2, 5, 2048), generator=g).to(torch.bfloat16)
+    gate_tok = torch.randn((2, 5, 2048), generator=g).to(torch.bfloat16)
+    gate_sample = torch.randn((2, 1, 2048), generator=g).to(torch.bfloat16)
+    out.update(res_x=bits(x), res_y=bits(y), res_gate_tok=bits(gate_tok), res_gate_sample=bits(gate_sample),
+               res_out_tok=bits(ops.fused_residual_gate_bf16(x, y, gate_tok)),
+               res_out_sample=bits(ops.fused_residual_gate_bf16(x, y, gate_sample)))
+    x = torch.randn((2, 7, 4096), generator=g).to(torch.bfloat16)
+    scale = (torch.randn((2, 1, 4096), generator=g) * 0.3).to(torch.bfloat16)
+    shift = (torch.randn((2, 1, 4096), generator=g) * 0.3).to(torch.bfloat16)
+    out.update(ada_x=bits(x), ada_scale=bits(scale), ada_shift=bits(shift),
+               ada_y=bits(ops.fused_adazero(x, 1e-6, scale, shift)))
+    np.savez_compressed(os.path.join(HERE, "ada_misc.npz"), **out)
+
+
 GELU_SCALES_BF16 = [1.0, 0.0371, 1.0 / 448.0]
 GELU_SCALES_F16 = [1.0, 0.0371]
 
@@ -258,6 +285,7 @@ def main() -> None:
     make_residual_nobias(ops)
     make_adaln_affine(ops)
     make_head_gate(ops)
+    make_ada_misc(ops)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

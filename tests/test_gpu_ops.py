@@ -285,3 +285,34 @@ def test_head_gate_mul_bitwise_vs_golden(ops):
     y2 = ops.fused_head_gate_mul_bf16(out.cuda(), gates.cuda(), 16, 64)
     assert np.array_equal(to_np(y2), O.head_gate_mul_bf16(out, gates, 16, 64))
     assert status_clean()
+
+
+def test_mul_from_ada_and_residual_gate_bf16_bitwise_vs_golden(ops):
+    d = np.load(os.path.join(GOLD, "ada_misc.npz"))
+    y = ops.fused_mul_from_ada(from_bits(d["mul_x"]), torch.from_numpy(d["mul_table"]).cuda(), from_bits(d["mul_ts"]),
+                               gate_index=4)
+    assert np.array_equal(bf16_bits(y), d["mul_y"])
+    x, yy = from_bits(d["res_x"]), from_bits(d["res_y"])
+    for tag in ("tok", "sample"):
+        out = ops.fused_residual_gate_bf16(x, yy, from_bits(d[f"res_gate_{tag}"]))
+        assert np.array_equal(bf16_bits(out), d[f"res_out_{tag}"])
+    assert status_clean()
+
+
+@pytest.mark.parametrize("rows", ["one", "sample", "token"])
+def test_adazero_explicit_vs_oracle(ops, rows):
+    """``fused_adazero`` with explicit scale/shift of 1, batch or batch*tokens rows: within one bf16 ulp of the
+    one-rounding oracle, and within 0.0625 of the reference's torch path on its golden."""
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn((2, 9, 4096), generator=g).to(torch.bfloat16)
+    shape = {"one": (1, 1, 4096), "sample": (2, 1, 4096), "token": (2, 9, 4096)}[rows]
+    scale = (torch.randn(shape, generator=g) * 0.3).to(torch.bfloat16)
+    shift = torch.randn(shape, generator=g) * 0.3  # fp32 shift with a bf16 scale
+    out = ops.fused_adazero(x.cuda(), 1e-6, scale.cuda(), shift.cuda())
+    ref = O.adazero_explicit(x, 1e-6, scale.float(), shift)
+    ok, worst = within_ulps(to_np(out), ref, ulps=1.0, atol=1e-5)
+    assert ok, worst
+    d = np.load(os.path.join(GOLD, "ada_misc.npz"))
+    got = ops.fused_adazero(from_bits(d["ada_x"]), 1e-6, from_bits(d["ada_scale"]), from_bits(d["ada_shift"]))
+    assert np.abs(to_np(got) - O.bf16_from_bits(d["ada_y"])).max() <= 0.0625
+    assert status_clean()

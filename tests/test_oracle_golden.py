@@ -256,3 +256,20 @@ def test_head_gate_oracle_bitwise():
     d = g("head_gate.npz")
     out = O.head_gate_mul_bf16(bf(d["out"]), bf(d["gates"]), 32, 128)
     assert np.array_equal(out, bf(d["y"]))
+
+
+def test_mul_from_ada_and_residual_gate_bf16_oracle_bitwise():
+    d = g("ada_misc.npz")
+    out = O.mul_from_ada(bf(d["mul_x"]), d["mul_table"], bf(d["mul_ts"]).reshape(1, 6, 9, 4096), gate_index=4)
+    assert np.array_equal(out, bf(d["mul_y"]))
+    x, y = bf(d["res_x"]), bf(d["res_y"])
+    assert np.array_equal(O.residual_gate_bf16(x, y, bf(d["res_gate_tok"])), bf(d["res_out_tok"]))
+    assert np.array_equal(O.residual_gate_bf16(x, y, bf(d["res_gate_sample"])), bf(d["res_out_sample"]))
+
+
+def test_adazero_explicit_oracle_vs_reference_torch_path():
+    """``fused_adazero`` (:8-37): the oracle follows its GPU kernel (one rounding); the torch path rounds
+    after each op and agrees within the reference test's AdaZero tolerance (0.0625)."""
+    d = g("ada_misc.npz")
+    out = O.adazero_explicit(bf(d["ada_x"]), 1e-6, bf(d["ada_scale"]), bf(d["ada_shift"]))
+    assert np.abs(out - bf(d["ada_y"])).max() <= 0.0625
