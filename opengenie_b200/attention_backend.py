@@ -155,8 +155,6 @@ def video_msa_branch(block, video, vx: torch.Tensor, *, token_counts: set[int] |
     if pe is None:
         return _decline("missing_rope")
     attn = block.attn1
-    if getattr(attn, "to_gate_logits", None) is not None:
-        return _decline("gated_attention")
     fused = _MSA_BLOCKS.get(id(block))
     if fused is None:
         def lin(m):
@@ -165,7 +163,8 @@ def video_msa_branch(block, video, vx: torch.Tensor, *, token_counts: set[int] |
         w = BlockWeights(lin(attn.to_q), lin(attn.to_k), lin(attn.to_v), lin(attn.to_out[0]), attn.q_norm.weight,
                          attn.k_norm.weight, block.scale_shift_table, float(block.norm_eps),
                          float(getattr(attn.q_norm, "eps", 1e-6)))
-        fused = VideoSelfAttentionBlock(w, vx.device)
+        # gated checkpoints: the per-head gate 2*sigmoid(to_gate_logits(norm)) scales the attention output
+        fused = VideoSelfAttentionBlock(w, vx.device, to_gate_logits=getattr(attn, "to_gate_logits", None))
         _MSA_BLOCKS[id(block)] = fused
     _MSA_BRANCH_CALLS += 1
     return fused(vx, video.timesteps, (pe[0], pe[1]))

@@ -31,8 +31,13 @@ from .synthetic import FP8_MAX, BlockWeights
 class VideoSelfAttentionBlock:
     """One DiT layer's video self-attention branch with weights resident in HBM."""
 
-    def __init__(self, weights: BlockWeights, device: torch.device | str = "cuda"):
+    def __init__(self, weights: BlockWeights, device: torch.device | str = "cuda", *, to_gate_logits=None):
+        """``to_gate_logits``: for checkpoints with gated attention, the module (or callable) mapping the
+        AdaZero output [1, L, D] bf16 to per-head gate logits [1, L, H]; the attention output is then
+        multiplied per head by 2*sigmoid(logits) before the out-projection (the reference's
+        `_video_msa_gated_attention`, ltx_serve/triton_ltx_ops.py:2282-2302)."""
         self.device = torch.device(device)
+        self.to_gate_logits = to_gate_logits
         w = weights.to(self.device)
         self.w = w
         self.dim = w.to_q.in_features
@@ -63,15 +68,21 @@ class VideoSelfAttentionBlock:
         w = self.w
         D = self.dim
         if self.shared_quant:
-            ltx_ops_xq = ltx_ops.fused_adazero_from_ada_fp8(
-                vx, w.norm_eps, w.scale_shift_table, timestep, w.to_q.input_scale, shift_index=0, scale_index=1
-            )
+            if self.to_gate_logits is not None:  # the gate logits read the bf16 AdaZero output
+                ltx_ops_xq, ws["norm"] = ltx_ops.fused_adazero_from_ada_fp8(
+                    vx, w.norm_eps, w.scale_shift_table, timestep, w.to_q.input_scale, shift_index=0, scale_index=1,
+                    return_bf16=True)
+            else:
+                ltx_ops_xq = ltx_ops.fused_adazero_from_ada_fp8(
+                    vx, w.norm_eps, w.scale_shift_table, timestep, w.to_q.input_scale, shift_index=0, scale_index=1
+                )
             ws["xq"] = ltx_ops_xq
             ltx_ops.fp8_scaled_mm(
                 ltx_ops_xq, self.w_qkv, w.to_q.input_scale, self.s_qkv, bias=self.b_qkv, out=ws["qkv"], n_per_scale=D
             )
         else:
             norm = ltx_ops.fused_adazero_from_ada(vx, w.norm_eps, w.scale_shift_table, timestep, shift_index=0, scale_index=1)
+            ws["norm"] = norm
             for i, lin in enumerate((w.to_q, w.to_k, w.to_v)):
                 xq = ltx_ops.fused_fp8_quantize_e4m3(norm, lin.input_scale)
                 ltx_ops.fp8_scaled_mm(
@@ -100,13 +111,22 @@ class VideoSelfAttentionBlock:
         v = qkv[:, 2 * D:].unsqueeze(0)
         cos, sin = pe
         ltx_ops.fused_video_qk_rmsnorm_rope(q, k, w.q_norm_weight, w.k_norm_weight, w.qk_eps, cos, sin, out=(q, k))
-        ltx_ops.attention(q, k, v, self.heads, out=ws["oq"], out_e4m3_scale=w.to_out.input_scale)
+        if self.to_gate_logits is not None:
+            ws["oq"] = ltx_ops.fused_fp8_quantize_e4m3(self._gated_attention(q, k, v, ws["norm"]),
+                                                       w.to_out.input_scale)
+        else:
+            ltx_ops.attention(q, k, v, self.heads, out=ws["oq"], out_e4m3_scale=w.to_out.input_scale)
         return ltx_ops.fp8_scaled_mm_residual_gate(
             ws["oq"], w.to_out.weight, w.to_out.input_scale, w.to_out.weight_scale, w.to_out.bias,
             vx, w.scale_shift_table, timestep, gate_index=2, out=out,
         )
 
     __call__ = forward
+
+    def _gated_attention(self, q, k, v, norm: torch.Tensor) -> torch.Tensor:
+        """bf16 attention output times 2*sigmoid(gate logits) per head (the gated checkpoints)."""
+        gates = (2.0 * torch.sigmoid(self.to_gate_logits(norm))).to(torch.bfloat16).contiguous()
+        return ltx_ops.fused_head_gate_mul_bf16(ltx_ops.attention(q, k, v, self.heads), gates, self.heads, 128)
 
     def time_attention(self, steps: int, warmup: int = 3, tokens: int | None = None) -> float:
         """Average device time (ms) of the attention kernel alone on the current stream,
@@ -151,5 +171,8 @@ class VideoSelfAttentionBlock:
         k = qkv[:, D:2 * D].unsqueeze(0)
         v = qkv[:, 2 * D:].unsqueeze(0)
         ltx_ops.fused_video_qk_rmsnorm_rope(q, k, w.q_norm_weight, w.k_norm_weight, w.qk_eps, pe[0], pe[1], out=(q, k))
-        attn = ltx_ops.attention(q, k, v, self.heads)
+        if self.to_gate_logits is not None:
+            attn = self._gated_attention(q, k, v, ws["norm"])
+        else:
+            attn = ltx_ops.attention(q, k, v, self.heads)
         w.to_out.input_scale = (attn.float().abs().amax().clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)

@@ -214,3 +214,48 @@ def test_step_graph_replay_matches_eager(ogx_lib):
         g.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, blk(x, inp.timestep, (inp.cos, inp.sin)))
+
+
+def test_gated_attention_block(ogx_lib):
+    """Gated checkpoints: with zero gate logits (2*sigmoid(0) = 1) the gated block equals the plain block bit
+    for bit; with random logits it equals the composition of the public ops (AdaZero, Q/K/V GEMM, RoPE,
+    attention, per-head gate, quantiser, out-projection + gated residual)."""
+    from opengenie_b200 import ltx_ops, synthetic
+    from opengenie_b200.video_block import VideoSelfAttentionBlock
+
+    cfg = synthetic.small_config(2, 6, 25)
+    inp = synthetic.make_inputs(cfg, seed=81).to("cuda")
+    pe = (inp.cos, inp.sin)
+    w = synthetic.make_weights(seed=82)
+    plain = VideoSelfAttentionBlock(w, "cuda")
+    plain.calibrate_input_scales(inp.x, inp.timestep, pe)
+    zero = torch.nn.Linear(4096, 32, dtype=torch.bfloat16, device="cuda")
+    torch.nn.init.zeros_(zero.weight)
+    torch.nn.init.zeros_(zero.bias)
+    gated = VideoSelfAttentionBlock(w, "cuda", to_gate_logits=zero)
+    gated.calibrate_input_scales(inp.x, inp.timestep, pe)
+    assert torch.equal(gated.w.to_out.input_scale, plain.w.to_out.input_scale)
+    assert torch.equal(gated(inp.x, inp.timestep, pe), plain(inp.x, inp.timestep, pe))
+
+    g = torch.Generator(device="cuda").manual_seed(83)
+    lin = torch.nn.Linear(4096, 32, dtype=torch.bfloat16, device="cuda")
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn((32, 4096), device="cuda", generator=g) * 0.02)
+        lin.bias.copy_(torch.randn((32,), device="cuda", generator=g))
+    blk = VideoSelfAttentionBlock(w, "cuda", to_gate_logits=lin)
+    blk.calibrate_input_scales(inp.x, inp.timestep, pe)
+    out = blk(inp.x, inp.timestep, pe)
+    bw = blk.w
+    xq, norm = ltx_ops.fused_adazero_from_ada_fp8(inp.x, bw.norm_eps, bw.scale_shift_table, inp.timestep,
+                                                  bw.to_q.input_scale, shift_index=0, scale_index=1, return_bf16=True)
+    qkv = ltx_ops.fp8_scaled_mm(xq, blk.w_qkv, bw.to_q.input_scale, blk.s_qkv, bias=blk.b_qkv, n_per_scale=4096)
+    qkv = qkv.reshape(cfg.tokens, -1)
+    q, k, v = (qkv[:, i * 4096:(i + 1) * 4096].unsqueeze(0) for i in range(3))
+    qr, kr = ltx_ops.fused_video_qk_rmsnorm_rope(q, k, bw.q_norm_weight, bw.k_norm_weight, bw.qk_eps, *pe)
+    gates = (2.0 * torch.sigmoid(lin(norm))).to(torch.bfloat16)
+    attn = ltx_ops.fused_head_gate_mul_bf16(ltx_ops.attention(qr, kr, v.contiguous(), 32), gates, 32, 128)
+    oq = ltx_ops.fused_fp8_quantize_e4m3(attn, bw.to_out.input_scale)
+    ref = ltx_ops.fp8_scaled_mm_residual_gate(oq, bw.to_out.weight, bw.to_out.input_scale, bw.to_out.weight_scale,
+                                              bw.to_out.bias, inp.x, bw.scale_shift_table, inp.timestep, gate_index=2)
+    assert torch.equal(out, ref)
+    assert status_clean()
