@@ -182,6 +182,7 @@ struct AdaArgs {
   int64_t table_stride_row;                       // elements; innermost stride is 1
   int64_t rows, tokens;
   int shift_index, scale_index;
+  int rows_per_cta;  // AdaZero: rows each CTA normalises (at most kAdaRowsPerCta)
   float eps;
   const float* input_scale;  // device scalar (QUANT only)
   __nv_bfloat16* y;          // may be null when only q is wanted
@@ -201,7 +202,8 @@ __device__ __forceinline__ float row_sum(float v, float* red) {
 
 constexpr int kAdaRowsPerCta = 8;
 
-// One 128-thread CTA per kAdaRowsPerCta rows.  With a token-uniform timestep
+// One 128-thread CTA per a.rows_per_cta (<= kAdaRowsPerCta) rows: the host spreads short inputs (a GPU's
+// slice of the sequence) over more CTAs.  With a token-uniform timestep
 // (stride 0 over tokens, the uniform-timestep layout) shift/scale are the same
 // for every row, so each thread computes them for its columns once and keeps
 // them in registers; otherwise they are read per row.  The next row's x is
@@ -213,8 +215,8 @@ __global__ void __launch_bounds__(kRowThreads) adazero_from_ada_kernel(AdaArgs a
   constexpr int VPT = COLS / 8 / kRowThreads;  // 16-byte vectors per thread
   __shared__ float red[2][4];
   const int tid = threadIdx.x;
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kAdaRowsPerCta;
-  const int64_t row_end = (row0 + kAdaRowsPerCta < a.rows) ? row0 + kAdaRowsPerCta : a.rows;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta;
+  const int64_t row_end = (row0 + a.rows_per_cta < a.rows) ? row0 + a.rows_per_cta : a.rows;
 
   const TableT* table = static_cast<const TableT*>(a.table);
   const TableT* tshift = table + a.shift_index * a.table_stride_row;

@@ -156,8 +156,14 @@ bool dtype_ok(int dt) { return dt == OGX_DTYPE_BF16 || dt == OGX_DTYPE_F32; }
 
 // ------------------------------------------------------------- AdaZero
 template <int COLS, typename TableT, typename TsT, bool UNIFORM>
-void launch_ada_u(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) {
-  const dim3 grid(static_cast<unsigned>((a.rows + ogx::kAdaRowsPerCta - 1) / ogx::kAdaRowsPerCta));
+void launch_ada_u(ogx::AdaArgs a, bool quant, int qmode, cudaStream_t s) {
+  // at least 4 CTAs per SM: up to kAdaRowsPerCta rows each (the Ada values a CTA loads serve all its
+  // rows), fewer for short inputs so that they still fill the GPU (1152 rows: 7.7 us against 10.1 us
+  // with 8 rows per CTA; 4608 rows and more keep 8 rows per CTA)
+  const int64_t target = 4 * static_cast<int64_t>(sm_count());
+  const int64_t per = (a.rows + target - 1) / target;
+  a.rows_per_cta = static_cast<int>(per < 1 ? 1 : (per > ogx::kAdaRowsPerCta ? ogx::kAdaRowsPerCta : per));
+  const dim3 grid(static_cast<unsigned>((a.rows + a.rows_per_cta - 1) / a.rows_per_cta));
   const int threads = ogx::kRowThreads;
   if (!quant)
     launch(ogx::adazero_from_ada_kernel<COLS, TableT, TsT, false, 0, UNIFORM>, grid, threads, 0, s, a);

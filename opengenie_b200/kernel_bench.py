@@ -22,14 +22,22 @@ from . import ltx_ops, synthetic
 
 
 def _time(fn, steps: int, warmup: int) -> float:
+    """Device time per launch: the `steps` launches are captured in one CUDA graph and replayed, so host
+    overhead (a few tens of microseconds per eager call) does not hide short kernels.  Consecutive launches
+    overlap their set-up as in the block (programmatic dependent launch)."""
     for _ in range(warmup):
         fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        for _ in range(steps):
+            fn()
+    graph.replay()  # warm
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(steps):
-        fn()
+    graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps

@@ -131,6 +131,21 @@ def test_adazero_fused_quant_equals_separate_quant(ops):
     assert np.array_equal(codes(q_only), codes(q))
 
 
+@pytest.mark.parametrize("rows", [1157, 2307, 4609])
+def test_adazero_rows_per_cta_widths_vs_oracle(ops, rows):
+    """Row counts whose grids give each CTA 2, 4 and 8 rows (the host spreads short inputs over at least
+    4 CTAs per SM), each with a ragged last CTA, with the fused quantiser on."""
+    x, table, ts = _ada_case(rows, 4096, torch.float32, torch.bfloat16, True, seed=rows)
+    s = torch.tensor(0.0123, device="cuda")
+    q, y = ops.fused_adazero_from_ada_fp8(x.cuda(), 1e-6, table.cuda(), ts[:, :1].cuda().expand(ts.shape), s,
+                                          shift_index=0, scale_index=1, return_bf16=True)
+    ref = O.adazero_from_ada(x, 1e-6, table, ts.reshape(1, rows, 6, 4096), shift_index=0, scale_index=1,
+                             table_is_bf16=False, ts_is_bf16=True)
+    ok, worst = within_ulps(to_np(y), ref, ulps=1.0, atol=1e-5)
+    assert ok, worst
+    assert np.array_equal(codes(q), O.quantize_e4m3(to_np(y), 0.0123))
+
+
 def test_bias_add_bitwise(ops):
     d = np.load(os.path.join(GOLD, "ops.npz"))
     out = ops.fused_bias_add_bf16(from_bits(d["bias_x"]), torch.from_numpy(d["bias_b"]).cuda())
