@@ -143,6 +143,17 @@ int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void*
                                        void* v_out, int64_t out_stride_t, int64_t out_stride_g,
                                        int heads_per_group, void* stream);
 
+/* Q/K RMSNorm over 4096 columns (with weight) and no rotary embedding, fp32 math, one bf16 rounding
+ * (the arithmetic of ogx_video_qk_rmsnorm_rope with cos = 1, sin = 0): q_out = rmsnorm(q) * q_weight
+ * over q_rows rows and k_out = rmsnorm(k) * k_weight over k_rows rows in one launch.  q and k may have
+ * different row counts (queries from the video tokens, keys from the text context); each has its own
+ * row stride (a multiple of 8) and the outputs may alias the inputs.  weight_dtype: bf16 or f32.
+ * Replaces attn.q_norm(q), attn.k_norm(k) of the pre-attention when no positional embedding is given
+ * (ltx_serve/triton_ltx_ops.py:1864-1865; the text cross-attention, :2880). */
+int ogx_qk_rmsnorm(const void* q, int64_t q_rows, int64_t q_stride, const void* k, int64_t k_rows, int64_t k_stride,
+                   const void* q_weight, const void* k_weight, int weight_dtype, float eps, void* q_out,
+                   int64_t q_out_stride, void* k_out, int64_t k_out_stride, void* stream);
+
 /* FP8 scaled matmul with bias epilogue (tcgen05, e4m3 x e4m3 -> f32 -> bf16):
  *   out[m, n] = bf16(bf16(acc * scale_a * scale_b[n / n_per_scale]) + bf16(bias[n]))
  * a: e4m3 [M, K] (row stride lda), w: e4m3 [N, K] (row stride ldw), both
@@ -212,6 +223,23 @@ int ogx_attention_fwd_e4m3(const void* q, const void* k, const void* v, int64_t 
                            int64_t heads, int64_t head_dim, int64_t stride_b, int64_t stride_t, float softmax_scale,
                            const float* out_scale, void* out_q, int64_t out_stride_b, int64_t out_stride_t,
                            void* stream);
+
+/* Attention whose keys and values come from a sequence of another length: q has q_tokens rows with
+ * strides (q_stride_b, q_stride_t), k and v have kv_tokens rows sharing (kv_stride_b, kv_stride_t); no
+ * mask.  Replaces the attention backend call of the text cross-attention (attn2: queries from the
+ * video tokens, keys/values from the prompt context), which the backend serves by viewing k and v as
+ * [b, -1, heads, d] (benchmarks/official_ltx23_benchmark.py:3294-3305; call ltx_serve/triton_ltx_ops.py:2880). */
+int ogx_attention_fwd_kv(const void* q, const void* k, const void* v, int64_t batch, int64_t q_tokens,
+                         int64_t kv_tokens, int64_t heads, int64_t head_dim, int64_t q_stride_b, int64_t q_stride_t,
+                         int64_t kv_stride_b, int64_t kv_stride_t, float softmax_scale, void* out,
+                         int64_t out_stride_b, int64_t out_stride_t, void* stream);
+
+/* ogx_attention_fwd_kv with the output quantised to e4m3 as in ogx_attention_fwd_e4m3. */
+int ogx_attention_fwd_kv_e4m3(const void* q, const void* k, const void* v, int64_t batch, int64_t q_tokens,
+                              int64_t kv_tokens, int64_t heads, int64_t head_dim, int64_t q_stride_b,
+                              int64_t q_stride_t, int64_t kv_stride_b, int64_t kv_stride_t, float softmax_scale,
+                              const float* out_scale, void* out_q, int64_t out_stride_b, int64_t out_stride_t,
+                              void* stream);
 
 /* ---- Sequence-parallel exchange over NVLink (no reference counterpart: the reference is single-GPU).
  * Buffers are shared between the ranks' processes with CUDA IPC; the producing kernels store straight

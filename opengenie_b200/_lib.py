@@ -78,6 +78,18 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_float,
         c_void_p, c_void_p, c_int64, c_int64, c_void_p,
     ],
+    "ogx_attention_fwd_kv": [
+        c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
+        c_int64, c_int64, c_float, c_void_p, c_int64, c_int64, c_void_p,
+    ],
+    "ogx_attention_fwd_kv_e4m3": [
+        c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
+        c_int64, c_int64, c_float, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+    ],
+    "ogx_qk_rmsnorm": [
+        c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float,
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p,
+    ],
     "ogx_ipc_get_handle": [c_void_p, c_void_p, ctypes.POINTER(c_int64)],
     "ogx_ipc_open_handle": [c_void_p, ctypes.POINTER(c_void_p)],
     "ogx_ipc_close_handle": [c_void_p],

@@ -47,8 +47,10 @@ def resolve_attention(attention: str) -> str:
 
 
 class B200NativeAttention:
-    """Attention backend callable with the reference's contract: ``(q, k, v, heads) -> out``, q/k/v
-    [B, L, H*d] bf16, d = 128, no mask, scale d^-0.5 (official_ltx23_benchmark.py:3289-3373)."""
+    """Attention backend callable with the reference's contract: ``(q, k, v, heads) -> out``, q [B, L, H*d]
+    and k/v [B, L_kv, H*d] bf16, d = 128, no mask, scale d^-0.5 (official_ltx23_benchmark.py:3289-3373).
+    L_kv may differ from L: the same backend serves the self-attention (attn1) and the text cross-attention
+    (attn2, keys/values from the prompt context; the reference views k and v as [b, -1, heads, d], :3305)."""
 
     name = "b200-native"
 

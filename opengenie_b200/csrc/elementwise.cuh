@@ -650,4 +650,57 @@ __global__ void __launch_bounds__(kRowThreads, 8) qk_rmsnorm_rope_kernel(RopeArg
   }
 }
 
+// Q/K RMSNorm without rotary embedding (attention whose keys come from another sequence): rows
+// [0, rows_q) are Q rows, [rows_q, rows_q + rows_k) K rows, each normalised over its 4096 columns and
+// multiplied by its tensor's weight with the arithmetic of rmsnorm_rope_row (fp32, one bf16 rounding).
+struct RmsRowsArgs {
+  const __nv_bfloat16* in[2];
+  int64_t in_stride[2];  // elements between rows
+  __nv_bfloat16* out[2];
+  int64_t out_stride[2];
+  const void* weight[2];
+  int64_t rows_q;
+  float eps;
+};
+
+// One 128-thread CTA per row; a row is read whole into registers before its first store, so the output
+// may alias the input.
+template <typename WT>
+__global__ void __launch_bounds__(kRowThreads) qk_rmsnorm_rows_kernel(RmsRowsArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int VPT = 4096 / 8 / kRowThreads;  // 4
+  __shared__ float red[4];
+  const int tid = threadIdx.x;
+  const int64_t r = blockIdx.x;
+  // selects, not a.in[j]: a runtime index into the parameter arrays would copy them to local memory
+  const bool is_k = r >= a.rows_q;
+  const int64_t t = is_k ? r - a.rows_q : r;
+  const __nv_bfloat16* in = (is_k ? a.in[1] : a.in[0]) + t * (is_k ? a.in_stride[1] : a.in_stride[0]);
+  const WT* w = static_cast<const WT*>(is_k ? a.weight[1] : a.weight[0]);
+  uint4 xv[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    xv[i] = __ldg(reinterpret_cast<const uint4*>(in) + i * kRowThreads + tid);
+    float f[8];
+    unpack8(xv[i], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+  }
+  ss = row_sum(ss, red);
+  const float inv_rms = rsqrtf(ss / 4096.f + a.eps);
+  __nv_bfloat16* out = (is_k ? a.out[1] : a.out[0]) + t * (is_k ? a.out_stride[1] : a.out_stride[0]);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vec = i * kRowThreads + tid;
+    float f[8], wv[8], n[8];
+    unpack8(xv[i], f);
+    load8<WT>(w + vec * 8, wv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) n[e] = f[e] * inv_rms * wv[e];
+    reinterpret_cast<uint4*>(out)[vec] = pack8(n);
+  }
+}
+
 }  // namespace ogx

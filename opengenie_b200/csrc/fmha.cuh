@@ -3,7 +3,10 @@
 //   O[b, t, h, :] = softmax(Q[b, t, h, :] . K[b, :, h, :]^T * scale) V[b, :, h, :]
 // This is the contract of the reference's attention backends
 // (benchmarks/official_ltx23_benchmark.py:3289-3373: q/k/v [B, L, H*d] viewed
-// [B, L, H, d], scale d^-0.5, no mask).
+// [B, L, H, d], scale d^-0.5, no mask).  Keys and values may come from a
+// sequence of another length (the text cross-attention: queries from the video
+// tokens, keys/values from the prompt context; the backend views k and v as
+// [b, -1, heads, d], :3305).
 //
 // One CTA per (256-query block, head, batch), 12 warps:
 //   warp 0        TMA producer: Q (2 tiles x 128 rows, once), then K and V
@@ -59,7 +62,8 @@ constexpr uint32_t kRegsSoftmax = 200;
 static_assert(128 * kRegsProducer + 256 * kRegsSoftmax <= kThreads * kLaunchRegs, "register split exceeds the launch");
 
 struct Params {
-  int L;             // tokens (keys == queries)
+  int L;             // query tokens
+  int L_kv;          // key/value tokens (== L for self-attention)
   float scale_log2;  // softmax scale * log2(e)
   __nv_bfloat16* out;  // bf16 output (when out_q is null)
   uint8_t* out_q;      // e4m3 output (quantised with *out_scale, torch-path semantics)
@@ -176,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int head = blockIdx.y;
   const int batch = blockIdx.z;
   const int q_block0 = blockIdx.x * (NQ * BQ);
-  const int nkv = (p.L + BKV - 1) / BKV;
+  const int nkv = (p.L_kv + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
     mbar_init(&st.q_full, 1);
@@ -332,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
       tmem_ld_wait();
       float* sf = reinterpret_cast<float*>(sr);
-      const int kv_valid = p.L - j * BKV;
+      const int kv_valid = p.L_kv - j * BKV;
       if (kv_valid < BKV) {
 #pragma unroll
         for (int i = 0; i < BKV; ++i)

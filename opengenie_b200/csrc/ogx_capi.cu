@@ -554,6 +554,43 @@ int ogx_video_qk_rmsnorm_rope(const void* q, const void* k, int64_t tokens, int6
                                             out_stride_t, 0, 32, stream);
 }
 
+int ogx_qk_rmsnorm(const void* q, int64_t q_rows, int64_t q_stride, const void* k, int64_t k_rows, int64_t k_stride,
+                   const void* q_weight, const void* k_weight, int weight_dtype, float eps, void* q_out,
+                   int64_t q_out_stride, void* k_out, int64_t k_out_stride, void* stream) {
+  if (q == nullptr || k == nullptr || q_out == nullptr || k_out == nullptr || q_weight == nullptr ||
+      k_weight == nullptr)
+    return fail(OGX_EINVAL, "null_pointer");
+  if (q_rows < 0 || k_rows < 0 || q_rows + k_rows > INT32_MAX) return fail(OGX_EINVAL, "qk_shape");
+  if (!dtype_ok(weight_dtype)) return fail(OGX_EINVAL, "weight_dtype");
+  if (q_stride < 4096 || k_stride < 4096 || q_out_stride < 4096 || k_out_stride < 4096 || q_stride % 8 ||
+      k_stride % 8 || q_out_stride % 8 || k_out_stride % 8)
+    return fail(OGX_EINVAL, "qk_stride");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(q_weight) ||
+      !aligned16(k_weight))
+    return fail(OGX_EINVAL, "alignment");
+  if (q_rows + k_rows == 0) return OGX_OK;
+  ogx::RmsRowsArgs a{};
+  a.in[0] = static_cast<const __nv_bfloat16*>(q);
+  a.in[1] = static_cast<const __nv_bfloat16*>(k);
+  a.in_stride[0] = q_stride;
+  a.in_stride[1] = k_stride;
+  a.out[0] = static_cast<__nv_bfloat16*>(q_out);
+  a.out[1] = static_cast<__nv_bfloat16*>(k_out);
+  a.out_stride[0] = q_out_stride;
+  a.out_stride[1] = k_out_stride;
+  a.weight[0] = q_weight;
+  a.weight[1] = k_weight;
+  a.rows_q = q_rows;
+  a.eps = eps;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(q_rows + k_rows));
+  if (weight_dtype == OGX_DTYPE_F32)
+    launch(ogx::qk_rmsnorm_rows_kernel<float>, grid, ogx::kRowThreads, 0, s, a);
+  else
+    launch(ogx::qk_rmsnorm_rows_kernel<__nv_bfloat16>, grid, ogx::kRowThreads, 0, s, a);
+  return check_launch("qk_rmsnorm_rows_kernel");
+}
+
 }  // extern "C"
 
 namespace {
@@ -663,25 +700,29 @@ int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::P
   return check_launch("fp8_gemm_kernel");
 }
 
-int attention_common(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens, int64_t heads,
-                     int64_t head_dim, int64_t stride_b, int64_t stride_t, CUtensorMap* mq, CUtensorMap* mk,
-                     CUtensorMap* mv) {
+int attention_common(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens, int64_t kv_tokens,
+                     int64_t heads, int64_t head_dim, int64_t stride_b, int64_t stride_t, int64_t kv_stride_b,
+                     int64_t kv_stride_t, CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv) {
   if (q == nullptr || k == nullptr || v == nullptr) return fail(OGX_EINVAL, "null_pointer");
   if (head_dim != 128) return fail(OGX_EINVAL, "head_dim: only 128 is supported");
-  if (batch < 1 || tokens < 1 || heads < 1) return fail(OGX_EINVAL, "shape");
-  if (tokens > INT32_MAX || heads > 65535 || batch > 65535) return fail(OGX_EINVAL, "shape");
+  if (batch < 1 || tokens < 1 || kv_tokens < 1 || heads < 1) return fail(OGX_EINVAL, "shape");
+  if (tokens > INT32_MAX || kv_tokens > INT32_MAX || heads > 65535 || batch > 65535) return fail(OGX_EINVAL, "shape");
   if (stride_t % 8 || stride_b % 8 || stride_t < heads * 128) return fail(OGX_EINVAL, "stride");
+  if (kv_stride_t % 8 || kv_stride_b % 8 || kv_stride_t < heads * 128) return fail(OGX_EINVAL, "stride");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(OGX_EINVAL, "alignment");
-  const uint64_t dims[4] = {128, static_cast<uint64_t>(heads), static_cast<uint64_t>(tokens),
-                            static_cast<uint64_t>(batch)};
-  const uint64_t strides[3] = {256, static_cast<uint64_t>(stride_t) * 2, static_cast<uint64_t>(stride_b) * 2};
+  const uint64_t qdims[4] = {128, static_cast<uint64_t>(heads), static_cast<uint64_t>(tokens),
+                             static_cast<uint64_t>(batch)};
+  const uint64_t qstrides[3] = {256, static_cast<uint64_t>(stride_t) * 2, static_cast<uint64_t>(stride_b) * 2};
+  const uint64_t kvdims[4] = {128, static_cast<uint64_t>(heads), static_cast<uint64_t>(kv_tokens),
+                              static_cast<uint64_t>(batch)};
+  const uint64_t kvstrides[3] = {256, static_cast<uint64_t>(kv_stride_t) * 2, static_cast<uint64_t>(kv_stride_b) * 2};
   const uint32_t qbox[4] = {64, 1, static_cast<uint32_t>(ogx::fmha::BQ), 1};
   const uint32_t kvbox[4] = {64, 1, static_cast<uint32_t>(ogx::fmha::BKV), 1};
-  int rc = make_map(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, q, dims, strides, qbox);
+  int rc = make_map(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, q, qdims, qstrides, qbox);
   if (rc) return rc;
-  rc = make_map(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k, dims, strides, kvbox);
+  rc = make_map(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k, kvdims, kvstrides, kvbox);
   if (rc) return rc;
-  return make_map(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v, dims, strides, kvbox);
+  return make_map(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v, kvdims, kvstrides, kvbox);
 }
 
 template <bool E4M3>
@@ -828,11 +869,13 @@ int ogx_attention_fwd(const void* q, const void* k, const void* v, int64_t batch
                       int64_t head_dim, int64_t stride_b, int64_t stride_t, float softmax_scale, void* out,
                       int64_t out_stride_b, int64_t out_stride_t, void* stream) {
   CUtensorMap mq, mk, mv;
-  int rc = attention_common(q, k, v, batch, tokens, heads, head_dim, stride_b, stride_t, &mq, &mk, &mv);
+  int rc = attention_common(q, k, v, batch, tokens, tokens, heads, head_dim, stride_b, stride_t, stride_b, stride_t,
+                            &mq, &mk, &mv);
   if (rc) return rc;
   if (out == nullptr || !aligned16(out) || out_stride_t % 8 || out_stride_b % 8) return fail(OGX_EINVAL, "output");
   ogx::fmha::Params p{};
   p.L = static_cast<int>(tokens);
+  p.L_kv = p.L;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride_b = out_stride_b;
@@ -845,18 +888,61 @@ int ogx_attention_fwd_e4m3(const void* q, const void* k, const void* v, int64_t 
                            const float* out_scale, void* out_q, int64_t out_stride_b, int64_t out_stride_t,
                            void* stream) {
   CUtensorMap mq, mk, mv;
-  int rc = attention_common(q, k, v, batch, tokens, heads, head_dim, stride_b, stride_t, &mq, &mk, &mv);
+  int rc = attention_common(q, k, v, batch, tokens, tokens, heads, head_dim, stride_b, stride_t, stride_b, stride_t,
+                            &mq, &mk, &mv);
   if (rc) return rc;
   if (out_q == nullptr || out_scale == nullptr || !aligned16(out_q) || out_stride_t % 16 || out_stride_b % 16)
     return fail(OGX_EINVAL, "output");
   ogx::fmha::Params p{};
   p.L = static_cast<int>(tokens);
+  p.L_kv = p.L;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.out_q = static_cast<uint8_t*>(out_q);
   p.out_scale = out_scale;
   p.out_stride_b = out_stride_b;
   p.out_stride_t = out_stride_t;
   return attention_launch<true>(mq, mk, mv, batch, tokens, heads, p, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_attention_fwd_kv(const void* q, const void* k, const void* v, int64_t batch, int64_t q_tokens,
+                         int64_t kv_tokens, int64_t heads, int64_t head_dim, int64_t q_stride_b, int64_t q_stride_t,
+                         int64_t kv_stride_b, int64_t kv_stride_t, float softmax_scale, void* out,
+                         int64_t out_stride_b, int64_t out_stride_t, void* stream) {
+  CUtensorMap mq, mk, mv;
+  int rc = attention_common(q, k, v, batch, q_tokens, kv_tokens, heads, head_dim, q_stride_b, q_stride_t, kv_stride_b,
+                            kv_stride_t, &mq, &mk, &mv);
+  if (rc) return rc;
+  if (out == nullptr || !aligned16(out) || out_stride_t % 8 || out_stride_b % 8) return fail(OGX_EINVAL, "output");
+  ogx::fmha::Params p{};
+  p.L = static_cast<int>(q_tokens);
+  p.L_kv = static_cast<int>(kv_tokens);
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_b = out_stride_b;
+  p.out_stride_t = out_stride_t;
+  return attention_launch<false>(mq, mk, mv, batch, q_tokens, heads, p, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_attention_fwd_kv_e4m3(const void* q, const void* k, const void* v, int64_t batch, int64_t q_tokens,
+                              int64_t kv_tokens, int64_t heads, int64_t head_dim, int64_t q_stride_b,
+                              int64_t q_stride_t, int64_t kv_stride_b, int64_t kv_stride_t, float softmax_scale,
+                              const float* out_scale, void* out_q, int64_t out_stride_b, int64_t out_stride_t,
+                              void* stream) {
+  CUtensorMap mq, mk, mv;
+  int rc = attention_common(q, k, v, batch, q_tokens, kv_tokens, heads, head_dim, q_stride_b, q_stride_t, kv_stride_b,
+                            kv_stride_t, &mq, &mk, &mv);
+  if (rc) return rc;
+  if (out_q == nullptr || out_scale == nullptr || !aligned16(out_q) || out_stride_t % 16 || out_stride_b % 16)
+    return fail(OGX_EINVAL, "output");
+  ogx::fmha::Params p{};
+  p.L = static_cast<int>(q_tokens);
+  p.L_kv = static_cast<int>(kv_tokens);
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.out_q = static_cast<uint8_t*>(out_q);
+  p.out_scale = out_scale;
+  p.out_stride_b = out_stride_b;
+  p.out_stride_t = out_stride_t;
+  return attention_launch<true>(mq, mk, mv, batch, q_tokens, heads, p, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
@@ -963,13 +1049,15 @@ int ogx_attention_fwd_e4m3_to_peers(const void* q, const void* k, const void* v,
                                     void* const* peer_bases, int peers, int64_t tokens_per_peer,
                                     int64_t out_stride_t, void* stream) {
   CUtensorMap mq, mk, mv;
-  int rc = attention_common(q, k, v, 1, tokens, heads, 128, tokens * stride_t, stride_t, &mq, &mk, &mv);
+  int rc = attention_common(q, k, v, 1, tokens, tokens, heads, 128, tokens * stride_t, stride_t, tokens * stride_t,
+                            stride_t, &mq, &mk, &mv);
   if (rc) return rc;
   if (peer_bases == nullptr || out_scale == nullptr || peers < 1 || peers > 8) return fail(OGX_EINVAL, "peers");
   if (tokens_per_peer < 1 || tokens_per_peer * peers != tokens) return fail(OGX_EINVAL, "tokens_per_peer");
   if (out_stride_t % 16 || out_stride_t < heads * 128) return fail(OGX_EINVAL, "output");
   ogx::fmha::Params p{};
   p.L = static_cast<int>(tokens);
+  p.L_kv = p.L;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.out_scale = out_scale;
   p.out_stride_t = out_stride_t;

@@ -1,7 +1,7 @@
 """Times one kernel of the block alone, at any size: a CLI for sweeps and for profiler captures of a
 single launch on a small case.
 
-    python -m opengenie_b200.kernel_bench attention --tokens 9216 --heads 4 [--e4m3]
+    python -m opengenie_b200.kernel_bench attention --tokens 9216 --heads 4 [--e4m3] [--kv-tokens 1024]
     python -m opengenie_b200.kernel_bench gemm --m 9216 --n 12288 --k 4096 [--residual]
     python -m opengenie_b200.kernel_bench adazero --tokens 9216
     python -m opengenie_b200.kernel_bench rope --tokens 9216
@@ -46,9 +46,16 @@ def _time(fn, steps: int, warmup: int) -> float:
 def bench_attention(a) -> dict:
     g = torch.Generator(device="cuda").manual_seed(a.seed)
     L, H = a.tokens, a.heads
-    # packed [L][3][H*128] rows, as the QKV projection leaves them
-    qkv = torch.randn((L, 3 * H * 128), device="cuda", generator=g).to(torch.bfloat16)
-    q, k, v = (qkv[:, i * H * 128:(i + 1) * H * 128].unsqueeze(0) for i in range(3))
+    L_kv = a.kv_tokens or L
+    if a.kv_tokens:
+        # text cross-attention: q [L][H*128] from to_q, k/v the halves of the packed [L_kv][2][H*128] rows
+        q = torch.randn((1, L, H * 128), device="cuda", generator=g).to(torch.bfloat16)
+        kv = torch.randn((L_kv, 2 * H * 128), device="cuda", generator=g).to(torch.bfloat16)
+        k, v = kv[:, :H * 128].unsqueeze(0), kv[:, H * 128:].unsqueeze(0)
+    else:
+        # packed [L][3][H*128] rows, as the QKV projection leaves them
+        qkv = torch.randn((L, 3 * H * 128), device="cuda", generator=g).to(torch.bfloat16)
+        q, k, v = (qkv[:, i * H * 128:(i + 1) * H * 128].unsqueeze(0) for i in range(3))
     if a.e4m3:
         out = torch.empty((1, L, H * 128), device="cuda", dtype=torch.float8_e4m3fn)
         scale = torch.tensor(0.01, device="cuda")
@@ -57,8 +64,8 @@ def bench_attention(a) -> dict:
         out = torch.empty((1, L, H * 128), device="cuda", dtype=torch.bfloat16)
         fn = lambda: ltx_ops.attention(q, k, v, H, out=out)  # noqa: E731
     ms = _time(fn, a.steps, a.warmup)
-    flops = 4.0 * L * L * 128 * H
-    return {"kernel": "fmha_fwd_kernel", "tokens": L, "heads": H, "e4m3_out": a.e4m3, "ms": ms,
+    flops = 4.0 * L * L_kv * 128 * H
+    return {"kernel": "fmha_fwd_kernel", "tokens": L, "kv_tokens": L_kv, "heads": H, "e4m3_out": a.e4m3, "ms": ms,
             "tflops": flops / (ms * 1e-3) / 1e12}
 
 
@@ -118,6 +125,7 @@ def main(argv=None) -> None:
     ap.add_argument("--tokens", type=int, default=9216)
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--e4m3", action="store_true")
+    ap.add_argument("--kv-tokens", type=int, default=0, help="attention: keys from a sequence of this length")
     ap.add_argument("--m", type=int, default=9216)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=4096)

@@ -526,6 +526,54 @@ def fused_video_qkv_rmsnorm_rope_pack(
     return qkv
 
 
+def _norm_rows(t: torch.Tensor) -> tuple[int, int]:
+    """(rows, row stride) of a [B, L, 4096] bf16 tensor whose rows are evenly strided."""
+    if t.ndim != 3 or t.shape[-1] != 4096 or t.dtype != torch.bfloat16 or not t.is_cuda:
+        raise ValueError("qk_shape")
+    B, L, _ = t.shape
+    if t.stride(-1) != 1 or t.stride(1) % 8 or (B > 1 and t.stride(0) != L * t.stride(1)):
+        raise ValueError("qk_noncontiguous")
+    return B * L, t.stride(1)
+
+
+def fused_qk_rmsnorm(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    q_weight: torch.Tensor,
+    k_weight: torch.Tensor,
+    eps: float,
+    *,
+    out: tuple[torch.Tensor, torch.Tensor] | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Q/K RMSNorm over 4096 columns with weight and no rotary embedding: q [B, L, 4096] and k [B, L_kv, 4096]
+    bf16 (the lengths may differ), one launch for both.
+
+    Reference: the pre-attention without positional embedding, ``q = attn.q_norm(q); k = attn.k_norm(k)``
+    (ltx_serve/triton_ltx_ops.py:1864-1865), which the text cross-attention takes (:2880).  The arithmetic is
+    that of ``fused_video_qk_rmsnorm_rope`` (fp32, one bf16 rounding) with the rotation left out.  ``out``
+    may alias (q, k) for an in-place update.
+    """
+    q_rows, q_stride = _norm_rows(q)
+    k_rows, k_stride = _norm_rows(k)
+    if q_weight.shape != (4096,) or k_weight.shape != (4096,) or q_weight.dtype != k_weight.dtype:
+        raise ValueError("qk_weight_shape")
+    if out is None:
+        q_out, k_out = torch.empty_like(q), torch.empty_like(k)
+    else:
+        q_out, k_out = out
+        if q_out.shape != q.shape or k_out.shape != k.shape:
+            raise ValueError("qk_out_shape")
+    _, q_out_stride = _norm_rows(q_out)
+    _, k_out_stride = _norm_rows(k_out)
+    _lib.call(
+        "ogx_qk_rmsnorm",
+        q.data_ptr(), q_rows, q_stride, k.data_ptr(), k_rows, k_stride,
+        q_weight.contiguous().data_ptr(), k_weight.contiguous().data_ptr(), _code(q_weight), float(eps),
+        q_out.data_ptr(), q_out_stride, k_out.data_ptr(), k_out_stride, _stream(q),
+    )
+    return q_out, k_out
+
+
 # ---------------------------------------------------------------- FP8 linears
 def _scale_ptr(t: torch.Tensor) -> int:
     if t.numel() != 1 or t.dtype != torch.float32 or not t.is_cuda:
@@ -726,39 +774,61 @@ def attention(
     out: torch.Tensor | None = None,
     out_e4m3_scale: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Dense bidirectional attention, q/k/v [B, L, H*128] bf16 (token rows may be strided).
+    """Dense bidirectional attention, q [B, L, H*128] and k/v [B, L_kv, H*128] bf16 (token rows may be
+    strided; k and v share their strides).
 
     The attention-backend contract of the reference (benchmarks/official_ltx23_benchmark.py:3289-3373;
-    call site ltx_serve/triton_ltx_ops.py:2636).  With ``out_e4m3_scale`` the bf16
-    result is quantised to e4m3 in the epilogue (torch-path semantics).
+    call sites ltx_serve/triton_ltx_ops.py:2636 for the self-attention and :2880 for the text
+    cross-attention, whose keys/values come from the prompt context: the backend views k and v as
+    [b, -1, heads, d], :3305).  With ``out_e4m3_scale`` the bf16 result is quantised to e4m3 in the
+    epilogue (torch-path semantics).
     """
     _require_cuda(q, k, v)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
         raise ValueError("qkv_dtype")
-    if q.ndim != 3 or q.shape != k.shape or q.shape != v.shape:
+    if q.ndim != 3 or k.ndim != 3 or k.shape != v.shape or k.shape[0] != q.shape[0] or k.shape[2] != q.shape[2]:
         raise ValueError("qkv_shape")
     B, L, HD = q.shape
+    L_kv = k.shape[1]
+    if L < 1 or L_kv < 1:
+        raise ValueError("qkv_shape")
     if HD % heads or HD // heads != 128:
         raise ValueError("head_dim")
-    if q.stride() != k.stride() or q.stride() != v.stride() or q.stride(-1) != 1:
+    if k.stride() != v.stride() or q.stride(-1) != 1 or k.stride(-1) != 1:
         raise ValueError("qkv_stride")
     scale = float(softmax_scale) if softmax_scale is not None else 128 ** -0.5
+    self_attention = L_kv == L and q.stride() == k.stride()
     if out_e4m3_scale is None:
         if out is None:
             out = torch.empty((B, L, HD), device=q.device, dtype=torch.bfloat16)
-        _lib.call(
-            "ogx_attention_fwd",
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, heads, 128, q.stride(0), q.stride(1), scale,
-            out.data_ptr(), out.stride(0), out.stride(1), _stream(q),
-        )
+        if self_attention:
+            _lib.call(
+                "ogx_attention_fwd",
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, heads, 128, q.stride(0), q.stride(1), scale,
+                out.data_ptr(), out.stride(0), out.stride(1), _stream(q),
+            )
+        else:
+            _lib.call(
+                "ogx_attention_fwd_kv",
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, L_kv, heads, 128, q.stride(0), q.stride(1),
+                k.stride(0), k.stride(1), scale, out.data_ptr(), out.stride(0), out.stride(1), _stream(q),
+            )
     else:
         if out is None:
             out = torch.empty((B, L, HD), device=q.device, dtype=torch.float8_e4m3fn)
-        _lib.call(
-            "ogx_attention_fwd_e4m3",
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, heads, 128, q.stride(0), q.stride(1), scale,
-            _scale_ptr(out_e4m3_scale), out.data_ptr(), out.stride(0), out.stride(1), _stream(q),
-        )
+        if self_attention:
+            _lib.call(
+                "ogx_attention_fwd_e4m3",
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, heads, 128, q.stride(0), q.stride(1), scale,
+                _scale_ptr(out_e4m3_scale), out.data_ptr(), out.stride(0), out.stride(1), _stream(q),
+            )
+        else:
+            _lib.call(
+                "ogx_attention_fwd_kv_e4m3",
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, L_kv, heads, 128, q.stride(0), q.stride(1),
+                k.stride(0), k.stride(1), scale, _scale_ptr(out_e4m3_scale), out.data_ptr(), out.stride(0),
+                out.stride(1), _stream(q),
+            )
     return out
 
 
@@ -767,19 +837,30 @@ def collect_video_ada_values_calls() -> int:
 
 
 __all__ = [
-    "QUANT_SINGLE",
-    "QUANT_TORCH",
+    "ada_from_table_guard_reason",
     "attention",
+    "collect_video_ada_values_calls",
     "fp8_linear_forward",
     "fp8_linear_from_quantized_e4m3",
     "fp8_linear_without_bias",
     "fp8_qkv_from_shared_quantized_input",
     "fp8_scaled_mm",
+    "fp8_scaled_mm_gelu_e4m3",
     "fp8_scaled_mm_residual_gate",
+    "fused_adaln_affine_from_ada",
+    "fused_adazero",
     "fused_adazero_from_ada",
     "fused_adazero_from_ada_fp8",
     "fused_bias_add_bf16",
     "fused_fp8_quantize_e4m3",
+    "fused_gelu_tanh_fp8_quantize_e4m3",
+    "fused_head_gate_mul_bf16",
+    "fused_mul_from_ada",
+    "fused_qk_rmsnorm",
+    "fused_residual_gate_bf16",
     "fused_residual_gate_bias_from_ada",
+    "fused_residual_gate_from_ada",
     "fused_video_qk_rmsnorm_rope",
+    "fused_video_qk_rmsnorm_rope_guard_reason",
+    "fused_video_qkv_rmsnorm_rope_pack",
 ]

@@ -17,6 +17,13 @@ the benchmark configurations stand in for them:
   theta 10000 (construction in ``rope_tables``; the exact LTX frequency mapping lives in
   the un-vendored ltx_core preprocessor, so kernel and oracle both consume these tensors).
 
+For the text cross-attention branch (attn2): the layer's Ada table has 9 slots (6/7 the query-side
+AdaLN shift/scale, 8 the gate; ~N(0, 0.02) fp32 [9, 4096]) with a 9-slot uniform timestep embedding;
+the prompt context is ``TEXT_CONTEXT_TOKENS`` = 1024 tokens of x ~ N(0, 1) bf16 [1, 1024, 4096] (the
+caption length after the un-vendored ltx_core text connector is not fixed by the reference; 1024 is
+this library's stand-in) with a 2-slot prompt table ~N(0, 0.02) and a uniform N(0, 1) prompt timestep
+embedding.
+
 Everything is drawn on the CPU from ``torch.Generator().manual_seed(seed)`` so the
 same seed gives the same tensors on any machine with this torch version.
 """
@@ -32,6 +39,9 @@ DIM = 4096
 HEADS = 32
 HEAD_DIM = 128
 ADA_SLOTS = 6
+TEXT_ADA_SLOTS = 9  # + query-side shift/scale (6/7) and gate (8) of the text cross-attention
+PROMPT_ADA_SLOTS = 2
+TEXT_CONTEXT_TOKENS = 1024
 FP8_MAX = 448.0
 
 
@@ -183,6 +193,76 @@ def make_ffn_weights(seed: int = 0, *, dim: int = DIM, hidden: int = FFN_HIDDEN)
     out = linear(dim, hidden)
     table = torch.randn((ADA_SLOTS, dim), generator=g) * 0.02
     return FfnWeights(proj, out, table.to(torch.float32))
+
+
+@dataclass
+class TextAttentionWeights:
+    """The video text cross-attention (attn2) of the same layer with cross-attention AdaLN: to_q on the video
+    tokens, to_k/to_v on the prompt context, to_out with its bias, Q/K RMSNorm weights, the layer's 9-slot
+    Ada table (6/7 query-side shift/scale, 8 gate) and the 2-slot prompt table (context shift/scale)."""
+
+    to_q: Fp8Linear
+    to_k: Fp8Linear
+    to_v: Fp8Linear
+    to_out: Fp8Linear
+    q_norm_weight: torch.Tensor
+    k_norm_weight: torch.Tensor
+    scale_shift_table: torch.Tensor
+    prompt_scale_shift_table: torch.Tensor
+    norm_eps: float = 1e-6
+    qk_eps: float = 1e-6
+
+    def to(self, device) -> "TextAttentionWeights":
+        return TextAttentionWeights(
+            self.to_q.to(device), self.to_k.to(device), self.to_v.to(device), self.to_out.to(device),
+            self.q_norm_weight.to(device), self.k_norm_weight.to(device), self.scale_shift_table.to(device),
+            self.prompt_scale_shift_table.to(device), self.norm_eps, self.qk_eps,
+        )
+
+
+def make_text_attention_weights(seed: int = 0, *, dim: int = DIM) -> TextAttentionWeights:
+    """Random-init text cross-attention weights (CPU), distributed as ``make_weights``'s; input scales are
+    placeholders until calibrated."""
+    g = torch.Generator().manual_seed(seed)
+
+    def linear() -> Fp8Linear:
+        w = torch.randn((dim, dim), generator=g) * 0.02
+        q, s = quantize_weight_e4m3(w)
+        b = (torch.randn((dim,), generator=g) * 0.01).to(torch.bfloat16)
+        return Fp8Linear(q, s, torch.tensor(1.0, dtype=torch.float32), b)
+
+    to_q, to_k, to_v, to_out = linear(), linear(), linear(), linear()
+    q_norm = (1.0 + 0.1 * torch.randn((dim,), generator=g)).to(torch.bfloat16)
+    k_norm = (1.0 + 0.1 * torch.randn((dim,), generator=g)).to(torch.bfloat16)
+    table = (torch.randn((TEXT_ADA_SLOTS, dim), generator=g) * 0.02).to(torch.float32)
+    prompt_table = (torch.randn((PROMPT_ADA_SLOTS, dim), generator=g) * 0.02).to(torch.float32)
+    return TextAttentionWeights(to_q, to_k, to_v, to_out, q_norm, k_norm, table, prompt_table)
+
+
+@dataclass
+class TextInputs:
+    x: torch.Tensor  # bf16 [1, L, D]
+    timestep: torch.Tensor  # bf16 [1, L, 9*D], stride-0 over tokens
+    context: torch.Tensor  # bf16 [1, L_ctx, D]
+    prompt_timestep: torch.Tensor  # bf16 [1, L_ctx, 2*D], stride-0 over tokens
+
+    def to(self, device) -> "TextInputs":
+        return TextInputs(
+            self.x.to(device), self.timestep[:, :1].to(device).expand(self.timestep.shape), self.context.to(device),
+            self.prompt_timestep[:, :1].to(device).expand(self.prompt_timestep.shape),
+        )
+
+
+def make_text_inputs(tokens: int, context_tokens: int = TEXT_CONTEXT_TOKENS, seed: int = 1, *,
+                     dim: int = DIM) -> TextInputs:
+    """Seeded inputs (CPU) of the text cross-attention branch: video tokens, their 9-slot uniform timestep
+    embedding, the prompt context and its 2-slot uniform prompt timestep embedding."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((1, tokens, dim), generator=g).to(torch.bfloat16)
+    ts = torch.randn((TEXT_ADA_SLOTS * dim,), generator=g).to(torch.bfloat16).view(1, 1, -1)
+    context = torch.randn((1, context_tokens, dim), generator=g).to(torch.bfloat16)
+    pts = torch.randn((PROMPT_ADA_SLOTS * dim,), generator=g).to(torch.bfloat16).view(1, 1, -1)
+    return TextInputs(x, ts.expand(1, tokens, -1), context, pts.expand(1, context_tokens, -1))
 
 
 @dataclass

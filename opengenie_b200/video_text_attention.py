@@ -1,0 +1,156 @@
+"""The video text cross-attention branch (attn2, with cross-attention AdaLN) of the same LTX-2.3 DiT layer on
+one B200.
+
+The reference runs it (`_apply_video_text_cross_attention_adaln_from_ada`, ltx_serve/triton_ltx_ops.py:2810-2888,
+with the production flags) as
+
+    context: fused_adaln_affine_from_ada (prompt table, slots 0/1)
+    x:       rms_norm -> fused_adaln_affine_from_ada (slots 6/7)
+    attn(attn_input, context=...):  to_q (quant -> scaled_mm -> bias) on x, to_k / to_v on the context,
+             q_norm / k_norm (no RoPE), attention over the context, to_out (quant -> scaled_mm -> bias)
+    fused_residual_gate_from_ada (slot 8)
+
+(``_attention_without_out_bias`` declines the call: it needs a positional embedding, :2574).  Here it is
+eight kernels with the same arithmetic and rounding points:
+
+ 1. context Ada affine (prompt slots 0/1)                                -> bf16 [L_ctx, 4096]
+ 2. the E4M3 quantiser of the K/V linears                                -> e4m3 [L_ctx, 4096]
+ 3. packed K/V FP8 GEMM (one scale per weight) + bias                    -> bf16 [L_ctx, 2*4096]
+ 4. AdaZero (slots 6/7) fused with the quantiser of to_q                 -> e4m3 [L, 4096]
+    (RMSNorm and the affine in one pass, as the reference's other cross-attention path does with
+    ``fused_adazero``, :1780; the reference's rms_norm rounds to bf16 in between)
+ 5. to_q FP8 GEMM + bias                                                 -> bf16 [L, 4096]
+ 6. Q/K RMSNorm without RoPE, Q and K rows in one launch, in place
+ 7. attention of the L queries over the L_ctx keys, output quantised for to_out -> e4m3 [L, 4096]
+ 8. to_out FP8 GEMM fused with bias + Ada gate (slot 8) + residual       -> bf16 [L, 4096]
+
+(stages 1-3 depend only on the prompt and its timestep).  The branch is sequence-local
+for the video tokens: on several GPUs each rank runs it on its own tokens against the whole context.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ltx_ops
+from .synthetic import FP8_MAX, TextAttentionWeights
+
+
+class VideoTextCrossAttention:
+    """One DiT layer's video text cross-attention branch with weights resident in HBM."""
+
+    kernel_launches_per_step = 8
+
+    def __init__(self, weights: TextAttentionWeights, device: torch.device | str = "cuda"):
+        self.device = torch.device(device)
+        w = weights.to(self.device)
+        self.w = w
+        self.dim = w.to_q.in_features
+        self.heads = self.dim // 128
+        self.w_kv = torch.cat([w.to_k.weight, w.to_v.weight], dim=0).contiguous()
+        self.s_kv = torch.stack([w.to_k.weight_scale, w.to_v.weight_scale]).reshape(2).contiguous()
+        self.b_kv = torch.cat([w.to_k.bias, w.to_v.bias]).contiguous()
+        # to_k and to_v quantise the context with one scale: one quantiser and one packed GEMM serve both;
+        # otherwise the context is quantised once per linear, as the reference's FP8Linear.forward does.
+        # Decided here (comparing device scalars synchronises, which a graph capture forbids) and again by
+        # calibrate_input_scales; a caller that replaces the input scales by hand sets it anew.
+        self.shared_kv_quant = bool(torch.equal(w.to_k.input_scale, w.to_v.input_scale))
+        self._ws: dict[tuple[int, int], dict[str, torch.Tensor]] = {}
+
+    def workspace(self, tokens: int, context_tokens: int) -> dict[str, torch.Tensor]:
+        key = (tokens, context_tokens)
+        ws = self._ws.get(key)
+        if ws is None:
+            D = self.dim
+            ws = {
+                "q": torch.empty((tokens, D), device=self.device, dtype=torch.bfloat16),
+                "kv": torch.empty((context_tokens, 2 * D), device=self.device, dtype=torch.bfloat16),
+                "oq": torch.empty((1, tokens, D), device=self.device, dtype=torch.float8_e4m3fn),
+            }
+            self._ws[key] = ws
+        return ws
+
+    # ------------------------------------------------------------------ stages
+    def context_kv(self, context: torch.Tensor, prompt_timestep: torch.Tensor, ws: dict[str, torch.Tensor]) -> torch.Tensor:
+        """Stages 1-3: the prompt context through its Ada affine and the K/V projections -> [L_ctx, 2*D] bf16."""
+        w = self.w
+        D = self.dim
+        ctx = ltx_ops.fused_adaln_affine_from_ada(context, w.prompt_scale_shift_table, prompt_timestep,
+                                                  shift_index=0, scale_index=1)
+        if self.shared_kv_quant:
+            cq = ltx_ops.fused_fp8_quantize_e4m3(ctx, w.to_k.input_scale)
+            ltx_ops.fp8_scaled_mm(cq, self.w_kv, w.to_k.input_scale, self.s_kv, bias=self.b_kv, out=ws["kv"],
+                                  n_per_scale=D)
+        else:
+            for i, lin in enumerate((w.to_k, w.to_v)):
+                cq = ltx_ops.fused_fp8_quantize_e4m3(ctx, lin.input_scale)
+                ltx_ops.fp8_scaled_mm(cq, lin.weight, lin.input_scale, lin.weight_scale, bias=lin.bias,
+                                      out=ws["kv"][:, i * D:(i + 1) * D])
+        return ws["kv"]
+
+    def forward(
+        self,
+        vx: torch.Tensor,
+        timestep: torch.Tensor,
+        context: torch.Tensor,
+        prompt_timestep: torch.Tensor,
+        *,
+        out: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        """vx [1, L, 4096] bf16, timestep [1, L, 9*4096], context [1, L_ctx, 4096] bf16, prompt_timestep
+        [1, L_ctx, 2*4096] -> vx + gate * (to_out(attention(...)) + bias), bf16."""
+        if vx.ndim != 3 or vx.shape[0] != 1 or vx.shape[-1] != self.dim:
+            raise ValueError("shape")
+        if context.ndim != 3 or context.shape[0] != 1 or context.shape[-1] != self.dim or context.shape[1] < 1:
+            raise ValueError("context_shape")
+        w = self.w
+        L, L_ctx = vx.shape[1], context.shape[1]
+        D = self.dim
+        ws = self.workspace(L, L_ctx)
+        kv = self.context_kv(context, prompt_timestep, ws)
+        xq = ltx_ops.fused_adazero_from_ada_fp8(vx, w.norm_eps, w.scale_shift_table, timestep, w.to_q.input_scale,
+                                                shift_index=6, scale_index=7)
+        ltx_ops.fp8_scaled_mm(xq, w.to_q.weight, w.to_q.input_scale, w.to_q.weight_scale, bias=w.to_q.bias,
+                              out=ws["q"])
+        q = ws["q"].unsqueeze(0)
+        k = kv[:, :D].unsqueeze(0)
+        v = kv[:, D:].unsqueeze(0)
+        ltx_ops.fused_qk_rmsnorm(q, k, w.q_norm_weight, w.k_norm_weight, w.qk_eps, out=(q, k))
+        ltx_ops.attention(q, k, v, self.heads, out=ws["oq"], out_e4m3_scale=w.to_out.input_scale)
+        return ltx_ops.fp8_scaled_mm_residual_gate(
+            ws["oq"], w.to_out.weight, w.to_out.input_scale, w.to_out.weight_scale, w.to_out.bias,
+            vx, w.scale_shift_table, timestep, gate_index=8, out=out,
+        )
+
+    __call__ = forward
+
+    # ------------------------------------------------------------------ calibration
+    @torch.no_grad()
+    def calibrate_input_scales(self, vx: torch.Tensor, timestep: torch.Tensor, context: torch.Tensor,
+                               prompt_timestep: torch.Tensor) -> None:
+        """Static per-tensor input scales = amax/448 of the activations feeding each FP8 linear (the query-side
+        AdaZero output, the context after its Ada affine, the attention output); stand-ins for a checkpoint's
+        calibrated input_scale (ltx_serve/triton_ltx_ops.py:1692-1698)."""
+        w = self.w
+        D = self.dim
+
+        def amax_scale(t: torch.Tensor) -> torch.Tensor:
+            return (t.float().abs().amax().clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
+
+        norm = ltx_ops.fused_adazero_from_ada(vx, w.norm_eps, w.scale_shift_table, timestep, shift_index=6,
+                                              scale_index=7)
+        w.to_q.input_scale = amax_scale(norm)
+        ctx = ltx_ops.fused_adaln_affine_from_ada(context, w.prompt_scale_shift_table, prompt_timestep,
+                                                  shift_index=0, scale_index=1)
+        s_ctx = amax_scale(ctx)
+        w.to_k.input_scale = s_ctx.clone()
+        w.to_v.input_scale = s_ctx.clone()
+        self.shared_kv_quant = True
+        ws = self.workspace(vx.shape[1], context.shape[1])
+        kv = self.context_kv(context, prompt_timestep, ws)
+        xq = ltx_ops.fused_fp8_quantize_e4m3(norm, w.to_q.input_scale)
+        q = ltx_ops.fp8_scaled_mm(xq, w.to_q.weight, w.to_q.input_scale, w.to_q.weight_scale, bias=w.to_q.bias)
+        k, v = kv[:, :D].unsqueeze(0), kv[:, D:].unsqueeze(0)
+        ltx_ops.fused_qk_rmsnorm(q, k, w.q_norm_weight, w.k_norm_weight, w.qk_eps, out=(q, k))
+        attn = ltx_ops.attention(q, k, v, self.heads)
+        w.to_out.input_scale = amax_scale(attn)

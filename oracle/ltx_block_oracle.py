@@ -251,6 +251,19 @@ def qk_rmsnorm_rope(x, weight, eps, cos, sin) -> np.ndarray:
     return bf16_round(out.reshape(B, L, D).astype(np.float32))
 
 
+def qk_rmsnorm(x, weight, eps) -> np.ndarray:
+    """RMSNorm over the full row with weight and no rotation, exact math, one bf16 rounding.
+
+    The pre-attention when no positional embedding is given, ``attn.q_norm(q)`` / ``attn.k_norm(k)``
+    (ltx_serve/triton_ltx_ops.py:1864-1865: the text cross-attention), restated with the arithmetic of
+    ``qk_rmsnorm_rope`` (the reference's fused Q/K kernel, :3901-3978) without the rotation.
+    """
+    xf = _np(x).astype(np.float64)
+    w = _np(weight).astype(np.float64)
+    inv = 1.0 / np.sqrt(np.mean(xf * xf, axis=-1, keepdims=True) + eps)
+    return bf16_round((xf * inv * w).astype(np.float32))
+
+
 # ----------------------------------------------------------------------------- contractions
 
 
@@ -278,7 +291,8 @@ def attention(q, k, v, heads: int, scale: float | None = None) -> np.ndarray:
     """softmax(q k^T * scale) v per head in float64 (returned as float32, not rounded).
 
     The attention backend contract, benchmarks/official_ltx23_benchmark.py:3289-3373.
-    q/k/v [B, L, H*d].
+    q [B, L, H*d]; k/v [B, L_kv, H*d] (L_kv != L for the text cross-attention, whose keys come
+    from the prompt context; the backend views k and v as [b, -1, heads, d], :3305).
     """
     qt = torch.from_numpy(_np(q).astype(np.float64))
     kt = torch.from_numpy(_np(k).astype(np.float64))
@@ -287,10 +301,10 @@ def attention(q, k, v, heads: int, scale: float | None = None) -> np.ndarray:
     d = D // heads
     sc = d ** -0.5 if scale is None else scale
     qh = qt.view(B, L, heads, d).transpose(1, 2)
-    kh = kt.view(B, L, heads, d).transpose(1, 2)
-    vh = vt.view(B, L, heads, d).transpose(1, 2)
+    kh = kt.view(B, -1, heads, d).transpose(1, 2)
+    vh = vt.view(B, -1, heads, d).transpose(1, 2)
     out = torch.empty_like(qh)
-    for h in range(heads):  # one head at a time keeps the L x L scores small
+    for h in range(heads):  # one head at a time keeps the L x L_kv scores small
         s = (qh[:, h] @ kh[:, h].transpose(-1, -2)) * sc
         p = torch.softmax(s, dim=-1)
         out[:, h] = p @ vh[:, h]
@@ -298,10 +312,11 @@ def attention(q, k, v, heads: int, scale: float | None = None) -> np.ndarray:
 
 
 def attention_fp32_torch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int) -> torch.Tensor:
-    """Fast fp32 CPU attention (torch SDPA math) for the timed CPU baseline."""
+    """Fast fp32 CPU attention (torch SDPA math) for the timed CPU baseline; k/v may be shorter than q."""
     B, L, D = q.shape
     d = D // heads
-    qh, kh, vh = (t.float().view(B, L, heads, d).transpose(1, 2) for t in (q, k, v))
+    qh = q.float().view(B, L, heads, d).transpose(1, 2)
+    kh, vh = (t.float().view(B, -1, heads, d).transpose(1, 2) for t in (k, v))
     o = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh)
     return o.transpose(1, 2).reshape(B, L, D)
 
@@ -491,3 +506,96 @@ def video_ffn_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, fw, *, eps:
     y = lin(quant(g, fw.out.input_scale), fw.out.input_scale, fw.out, bias=False)
     yb = r16(y + r16(fw.out.bias.to(dev).float()))
     return r16(xf + r16(yb * ada(5))).to(torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------- the video text cross-attention
+
+
+def video_text_cross_attention(x, timestep_view, context, prompt_timestep_view, tw, *, heads: int = 32,
+                               return_intermediates: bool = False):
+    """The video branch's text cross-attention (attn2) with cross-attention AdaLN, in the reference's order and
+    rounding points.
+
+    `_apply_video_text_cross_attention_adaln_from_ada` (ltx_serve/triton_ltx_ops.py:2810-2888) with the
+    production flags: the context through ``fused_adaln_affine_from_ada`` with the prompt table (slots 0/1,
+    :2842-2851); x through RMSNorm and the Ada affine of slots 6/7 (:2856-2862), here as the fused
+    ``adazero_from_ada`` of the reference's other cross-attention path (``fused_adazero``, :1780); then
+    ``attn(attn_input, context=...)`` (:2880; ``_attention_without_out_bias`` declines without a positional
+    embedding, :2574): FP8Linear.forward for to_q on x and to_k/to_v on the context (:1676-1716), Q/K RMSNorm
+    without RoPE (:1864-1865), attention over the context, to_out with its bias; and
+    ``fused_residual_gate_from_ada`` with slot 8 (:2882-2888): bf16(x + bf16(out * gate)).
+    ``timestep_view`` is [1, L, 9, D], ``prompt_timestep_view`` [1, L_ctx, 2, D]; ``tw`` carries the
+    synthetic TextAttentionWeights.
+    """
+    table = tw.scale_shift_table
+    tab_bf16 = table.dtype == torch.bfloat16
+    ts_bf16 = timestep_view.dtype == torch.bfloat16
+    ptab = tw.prompt_scale_shift_table
+    ctx = adaln_affine_from_ada(context, ptab, prompt_timestep_view, shift_index=0, scale_index=1,
+                                table_is_bf16=ptab.dtype == torch.bfloat16,
+                                ts_is_bf16=prompt_timestep_view.dtype == torch.bfloat16)
+    norm = adazero_from_ada(x, tw.norm_eps, table, timestep_view, shift_index=6, scale_index=7,
+                            table_is_bf16=tab_bf16, ts_is_bf16=ts_bf16)
+
+    def linear(inp, lin, bias=True):
+        s_in = float(lin.input_scale)
+        return fp8_linear(quantize_e4m3(inp, s_in), s_in, lin.weight.view(torch.uint8).numpy(), float(lin.weight_scale),
+                          _np(lin.bias) if bias else None)
+
+    q = qk_rmsnorm(linear(norm, tw.to_q), tw.q_norm_weight, tw.qk_eps)
+    k = qk_rmsnorm(linear(ctx, tw.to_k), tw.k_norm_weight, tw.qk_eps)
+    v = linear(ctx, tw.to_v)
+    attn = attention(q, k, v, heads)
+    attn_bf16 = bf16_round(attn)
+    y = linear(attn_bf16, tw.to_out)  # to_out with its bias: bf16(bf16(acc) + bf16(bias))
+    gate = ada_value(table, timestep_view, 8, table_is_bf16=tab_bf16, ts_is_bf16=ts_bf16)
+    out = residual_gate_bf16(x, y, gate)
+    if return_intermediates:
+        return out, {"ctx": ctx, "norm": norm, "q": q, "k": k, "v": v, "attn": attn, "attn_bf16": attn_bf16, "y": y}
+    return out
+
+
+def video_text_cross_attention_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, context: torch.Tensor,
+                                        prompt_timestep_view: torch.Tensor, tw, *, heads: int = 32) -> torch.Tensor:
+    """The same branch on CPU torch in float32 (multi-threaded): same stages and rounding points as
+    ``video_text_cross_attention``, fp32 contractions, so full-size configurations finish in seconds."""
+    def r16(t):
+        return t.to(torch.bfloat16).float()
+
+    def ada_fn(table, ts_view):
+        tab = table.float()
+        if (table.dtype == torch.bfloat16) != (ts_view.dtype == torch.bfloat16):
+            tab = r16(tab)
+        ts = ts_view.float()
+
+        def ada(idx):
+            v = tab[idx].view(1, 1, -1) + ts[:, :, idx, :]
+            return r16(v) if ts_view.dtype == torch.bfloat16 else v
+        return ada
+
+    ada = ada_fn(tw.scale_shift_table, timestep_view)
+    pada = ada_fn(tw.prompt_scale_shift_table, prompt_timestep_view)
+    xf = x.float()
+    ctx = r16(r16(context.float() * r16(1 + pada(1))) + pada(0))
+    norm = r16(xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + tw.norm_eps) * (1 + ada(7)) + ada(6))
+
+    def quant(t, s):
+        r = torch.tensor(1.0, dtype=torch.float32) / s.float()
+        return torch.clamp(r16(t * r), -FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+
+    def lin(t, l):
+        tq = quant(t, l.input_scale)
+        acc = tq.reshape(-1, tq.shape[-1]).float() @ l.weight.float().T
+        y = r16(acc * (l.input_scale.float() * l.weight_scale.float()))
+        y = r16(y + r16(l.bias.float()))
+        return y.view(*t.shape[:-1], -1)
+
+    def rms(t, weight):
+        return r16(t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + tw.qk_eps) * weight.float())
+
+    q = rms(lin(norm, tw.to_q), tw.q_norm_weight)
+    k = rms(lin(ctx, tw.to_k), tw.k_norm_weight)
+    v = lin(ctx, tw.to_v)
+    attn = r16(attention_fp32_torch(q, k, v, heads))
+    y = lin(attn, tw.to_out)
+    return r16(xf + r16(y * ada(8)))

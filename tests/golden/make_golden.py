@@ -25,7 +25,15 @@ seeded inputs:
 - adaln_affine.npz: ``fused_adaln_affine_from_ada`` (:94-141);
 - head_gate.npz: ``fused_head_gate_mul_bf16`` (:614-637);
 - ada_misc.npz: ``fused_mul_from_ada`` (:695-741), ``fused_residual_gate_bf16`` (:590-611) and
-  ``fused_adazero`` (:8-37).
+  ``fused_adazero`` (:8-37);
+- text_xattn.npz: the video text cross-attention branch with cross-attention AdaLN (:2810-2888)
+  composed the same way, 16 video tokens over a 24-token context,
+  ``opengenie_b200.synthetic.make_text_attention_weights(seed=17)``.  Its ``rms_norm`` and the
+  attention module's ``q_norm`` / ``k_norm`` live in the un-vendored ltx_core; they are taken as
+  ``torch.nn.functional.rms_norm`` (without / with the norm weight), the function the reference's
+  own ``fused_adazero`` fallback calls (:9-10).
+
+``--only NAME`` (NAME without .npz) regenerates one fixture.
 
 Inputs that are cheap to regenerate (seeded ``torch.Generator``) are stored too so
 the tests do not depend on regeneration.
@@ -271,21 +279,80 @@ def make_ffn(ops) -> None:
     )
 
 
+def make_text_xattn(ops) -> None:
+    """The video text cross-attention branch (triton_ltx_ops.py:2810-2888, production flags) composed from
+    the reference's CPU functions with CPU ``torch._scaled_mm`` and fp32 SDPA, 16 video tokens over a
+    24-token prompt context, ``opengenie_b200.synthetic.make_text_attention_weights(seed=17)``."""
+    from opengenie_b200 import synthetic
+
+    inp = synthetic.make_text_inputs(16, 24, seed=15)
+    tw = synthetic.make_text_attention_weights(seed=17)
+    x, ts, context, pts = inp.x, inp.timestep, inp.context, inp.prompt_timestep
+    table = tw.scale_shift_table
+    D = x.shape[-1]
+    # context: Ada affine with the prompt table (:2842-2851)
+    ctx = ops.fused_adaln_affine_from_ada(context, tw.prompt_scale_shift_table, pts, shift_index=0, scale_index=1)
+    # x: rms_norm, then the Ada affine of slots 6/7 (:2856-2862)
+    x_norm = torch.nn.functional.rms_norm(x, (D,), eps=tw.norm_eps)
+    attn_input = ops.fused_adaln_affine_from_ada(x_norm, table, ts, shift_index=6, scale_index=7)
+    s_q = (attn_input.float().abs().amax() / 448.0).to(torch.float32)
+    s_kv = (ctx.float().abs().amax() / 448.0).to(torch.float32)
+
+    def linear(inp_q, s_a, lin):
+        o = torch._scaled_mm(inp_q.reshape(-1, inp_q.shape[-1]), lin.weight.t(), scale_a=s_a, scale_b=lin.weight_scale,
+                             out_dtype=torch.bfloat16, use_fast_accum=True)
+        return ops.fused_bias_add_bf16(o, lin.bias).reshape(1, -1, o.shape[-1])
+
+    # attn(attn_input, context=ctx): FP8Linear.forward per projection (:1676-1716), q_norm / k_norm without
+    # RoPE (:1864-1865), attention over the context, to_out with its bias
+    xq = ops.fused_fp8_quantize_e4m3(attn_input, s_q)
+    cq = ops.fused_fp8_quantize_e4m3(ctx, s_kv)
+    q_proj = linear(xq, s_q, tw.to_q)
+    k_proj = linear(cq, s_kv, tw.to_k)
+    v = linear(cq, s_kv, tw.to_v)
+    q = torch.nn.functional.rms_norm(q_proj, (D,), weight=tw.q_norm_weight, eps=tw.qk_eps)
+    k = torch.nn.functional.rms_norm(k_proj, (D,), weight=tw.k_norm_weight, eps=tw.qk_eps)
+    qh, kh, vh = (t.float().view(1, -1, 32, 128).transpose(1, 2) for t in (q, k, v))
+    attn = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh).transpose(1, 2).reshape(1, -1, D)
+    attn = attn.to(torch.bfloat16)
+    s_out = (attn.float().abs().amax() / 448.0).to(torch.float32)
+    oq = ops.fused_fp8_quantize_e4m3(attn, s_out)
+    y = linear(oq, s_out, tw.to_out)
+    # gated residual with slot 8 (:2882-2888)
+    out = ops.fused_residual_gate_from_ada(x, y, table, ts, gate_index=8, count_video_ada=False)
+    np.savez_compressed(
+        os.path.join(HERE, "text_xattn.npz"),
+        s_q=s_q.numpy(), s_kv=s_kv.numpy(), s_out=s_out.numpy(), ctx=bits(ctx), attn_input=bits(attn_input),
+        xq=xq.view(torch.uint8).numpy(), cq=cq.view(torch.uint8).numpy(), q_proj=bits(q_proj), k_proj=bits(k_proj),
+        q=bits(q), k=bits(k), v=bits(v), attn=bits(attn), oq=oq.view(torch.uint8).numpy(), y=bits(y), out=bits(out),
+        seed_inputs=np.array(15), seed_weights=np.array(17), tokens=np.array(16), context_tokens=np.array(24),
+    )
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the plugyawn/opengenie checkout")
+    ap.add_argument("--only", default=None, help="regenerate one fixture (its name without .npz)")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ops, rope_ref = load_reference(args.reference)
-    make_quant(ops)
-    make_ops(ops, rope_ref)
-    make_block(ops, rope_ref)
-    make_gelu(ops)
-    make_ffn(ops)
-    make_residual_nobias(ops)
-    make_adaln_affine(ops)
-    make_head_gate(ops)
-    make_ada_misc(ops)
+    makers = {
+        "quant": lambda: make_quant(ops),
+        "ops": lambda: make_ops(ops, rope_ref),
+        "block": lambda: make_block(ops, rope_ref),
+        "gelu_quant": lambda: make_gelu(ops),
+        "ffn": lambda: make_ffn(ops),
+        "residual_nobias": lambda: make_residual_nobias(ops),
+        "adaln_affine": lambda: make_adaln_affine(ops),
+        "head_gate": lambda: make_head_gate(ops),
+        "ada_misc": lambda: make_ada_misc(ops),
+        "text_xattn": lambda: make_text_xattn(ops),
+    }
+    if args.only is not None:
+        makers[args.only]()
+    else:
+        for make in makers.values():
+            make()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -21,6 +21,38 @@ def test_header_and_binding_agree():
     assert declared_functions() == sorted(_lib.EXPORTED)
 
 
+def _declared_parameters():
+    """name -> list of C parameter types, from the prototypes in include/ogx.h."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for ret, name, params in re.findall(r"\b(int|const char\*)\s+(ogx_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = " ".join(params.split())
+        out[name] = [] if params in ("", "void") else [p.strip().rsplit(" ", 1)[0] for p in params.split(",")]
+    return out
+
+
+def _ctype_of(c_type: str):
+    if "*" in c_type:
+        return "pointer"
+    return {"int64_t": ctypes.c_int64, "int": ctypes.c_int, "float": ctypes.c_float}[c_type]
+
+
+def test_binding_argument_types_match_the_header():
+    """Every ctypes signature has the header's parameter count and kinds (an int64 where the prototype has
+    int64_t, a pointer where it has a pointer), so no call passes a misread argument."""
+    declared = _declared_parameters()
+    assert sorted(declared) == sorted(_lib.EXPORTED)
+    for name, argtypes in _lib._SIGNATURES.items():
+        c_params = declared[name]
+        assert len(c_params) == len(argtypes), name
+        for i, (c_type, py_type) in enumerate(zip(c_params, argtypes)):
+            want = _ctype_of(c_type)
+            if want == "pointer":
+                assert py_type is ctypes.c_void_p or issubclass(py_type, ctypes._Pointer), (name, i, c_type)
+            else:
+                assert py_type is want, (name, i, c_type, py_type)
+
+
 def test_library_exports_every_declared_symbol(ogx_lib):
     for name in declared_functions():
         assert hasattr(ogx_lib, name), name
@@ -51,6 +83,15 @@ def test_guards_reject_before_touching_the_device(ogx_lib):
     # quantiser dtype must be bf16 or f16 (triton_ltx_ops.py:1021-1022)
     rc = ogx_lib.ogx_fp8_quantize_e4m3(16, 1, 64, 16, 0, 16, None)
     assert rc == -1 and _err(ogx_lib) == "x_dtype"
+    # attention over keys of another length: no keys, and a key row stride narrower than the heads
+    rc = ogx_lib.ogx_attention_fwd_kv(16, 16, 16, 1, 128, 0, 32, 128, 0, 4096, 0, 4096, 0.1, 16, 0, 4096, None)
+    assert rc == -1 and _err(ogx_lib) == "shape"
+    rc = ogx_lib.ogx_attention_fwd_kv_e4m3(16, 16, 16, 1, 128, 77, 32, 128, 0, 4096, 0, 2048, 0.1, 16, 16, 0, 4096,
+                                           None)
+    assert rc == -1 and _err(ogx_lib) == "stride"
+    # Q/K RMSNorm without RoPE: rows of 4096 need a row stride of at least 4096
+    rc = ogx_lib.ogx_qk_rmsnorm(16, 4, 2048, 16, 4, 4096, 16, 16, 0, 1e-6, 16, 4096, 16, 4096, None)
+    assert rc == -1 and _err(ogx_lib) == "qk_stride"
 
 
 def test_ops_refuse_cpu_tensors():

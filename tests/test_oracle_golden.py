@@ -273,3 +273,94 @@ def test_adazero_explicit_oracle_vs_reference_torch_path():
     d = g("ada_misc.npz")
     out = O.adazero_explicit(bf(d["ada_x"]), 1e-6, bf(d["ada_scale"]), bf(d["ada_shift"]))
     assert np.abs(out - bf(d["ada_y"])).max() <= 0.0625
+
+
+def _text_case():
+    from opengenie_b200 import synthetic
+
+    d = g("text_xattn.npz")
+    L, Lc = int(d["tokens"]), int(d["context_tokens"])
+    inp = synthetic.make_text_inputs(L, Lc, seed=int(d["seed_inputs"]))
+    tw = synthetic.make_text_attention_weights(seed=int(d["seed_weights"]))
+    tw.to_q.input_scale = torch.tensor(float(d["s_q"]), dtype=torch.float32)
+    for lin in (tw.to_k, tw.to_v):
+        lin.input_scale = torch.tensor(float(d["s_kv"]), dtype=torch.float32)
+    tw.to_out.input_scale = torch.tensor(float(d["s_out"]), dtype=torch.float32)
+    ts_view = inp.timestep.reshape(1, L, 9, 4096)
+    pts_view = inp.prompt_timestep.reshape(1, Lc, 2, 4096)
+    return d, inp, tw, ts_view, pts_view
+
+
+def test_text_xattn_inputs_regenerate_identically():
+    d, inp, _, _, _ = _text_case()
+    assert inp.x.shape == (1, int(d["tokens"]), 4096) and inp.context.shape == (1, int(d["context_tokens"]), 4096)
+    assert inp.timestep.stride(1) == 0 and inp.prompt_timestep.stride(1) == 0
+
+
+def test_text_xattn_oracle_stages_vs_reference_composition():
+    """Each stage of the oracle's text cross-attention branch, fed the reference's own input to that stage."""
+    d, inp, tw, ts_view, pts_view = _text_case()
+    L, Lc = int(d["tokens"]), int(d["context_tokens"])
+    s_q, s_kv, s_out = float(d["s_q"]), float(d["s_kv"]), float(d["s_out"])
+    _, mid = O.video_text_cross_attention(inp.x, ts_view, inp.context, pts_view, tw, return_intermediates=True)
+    # the context's Ada affine with the prompt table, and its K/V codes: bit-exact
+    assert np.array_equal(mid["ctx"], bf(d["ctx"]))
+    assert np.array_equal(O.quantize_e4m3(bf(d["ctx"]), s_kv), d["cq"])
+    # the query side: the oracle's AdaZero rounds once, the reference's rms_norm + affine after each op;
+    # within the reference's AdaZero test tolerance (tests/test_triton_ltx_ops.py:92), codes mostly equal
+    assert np.abs(mid["norm"] - bf(d["attn_input"])).max() <= 0.0625
+    assert (O.quantize_e4m3(mid["norm"], s_q) == d["xq"]).mean() >= 0.95
+
+    def lin(codes, s, layer, rows):
+        return O.fp8_linear(codes.reshape(rows, 4096), s, layer.weight.view(torch.uint8).numpy(),
+                            float(layer.weight_scale), layer.bias.float().numpy())
+
+    # projections from the reference's codes (CPU _scaled_mm vs float64 accumulation)
+    _close(lin(d["xq"], s_q, tw.to_q, L), bf(d["q_proj"]).reshape(L, 4096), atol=2e-2, rel_ulps=1.0)
+    _close(lin(d["cq"], s_kv, tw.to_k, Lc), bf(d["k_proj"]).reshape(Lc, 4096), atol=2e-2, rel_ulps=1.0)
+    _close(lin(d["cq"], s_kv, tw.to_v, Lc), bf(d["v"]).reshape(Lc, 4096), atol=2e-2, rel_ulps=1.0)
+    # Q/K RMSNorm without RoPE from the reference's projections: one rounding against torch's rms_norm
+    _close(O.qk_rmsnorm(bf(d["q_proj"]), tw.q_norm_weight, 1e-6), bf(d["q"]), atol=0.0, rel_ulps=1.0)
+    _close(O.qk_rmsnorm(bf(d["k_proj"]), tw.k_norm_weight, 1e-6), bf(d["k"]), atol=0.0, rel_ulps=1.0)
+    # attention of 16 queries over the 24 context keys (fp32 SDPA there, float64 here)
+    attn = O.attention(bf(d["q"]), bf(d["k"]), bf(d["v"]), 32)
+    _close(O.bf16_round(attn), bf(d["attn"]), atol=2e-2, rel_ulps=1.0)
+    # to_out's quantiser: bit-exact; to_out from its codes
+    assert np.array_equal(O.quantize_e4m3(bf(d["attn"]), s_out), d["oq"])
+    _close(lin(d["oq"], s_out, tw.to_out, L), bf(d["y"]).reshape(L, 4096), atol=2e-2, rel_ulps=1.0)
+    # the gated residual (slot 8) from the reference's y: bit-exact
+    gate = O.ada_value(tw.scale_shift_table, ts_view, 8, table_is_bf16=False, ts_is_bf16=True)
+    assert np.array_equal(O.residual_gate_bf16(inp.x, bf(d["y"]), gate), bf(d["out"]))
+
+
+def test_text_xattn_cpu_fp32_baseline_agrees_with_oracle():
+    d, inp, tw, ts_view, pts_view = _text_case()
+    a = O.video_text_cross_attention(inp.x, ts_view, inp.context, pts_view, tw)
+    b = O.video_text_cross_attention_cpu_fp32(inp.x, ts_view, inp.context, pts_view, tw).numpy()
+    diff = np.abs(a - b)
+    assert diff.sum() / np.abs(a).sum() <= 1e-3
+    assert diff.max() <= 0.125
+
+
+def test_qk_rmsnorm_is_rope_with_unit_rotation():
+    """The RMSNorm-only restatement equals the RMSNorm + RoPE one with cos = 1, sin = 0, bit for bit."""
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn((1, 5, 4096), generator=gen).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn((4096,), generator=gen)).to(torch.bfloat16)
+    cos, sin = torch.ones((1, 32, 5, 64)), torch.zeros((1, 32, 5, 64))
+    assert np.array_equal(O.qk_rmsnorm(x, w, 1e-6), O.qk_rmsnorm_rope(x, w, 1e-6, cos, sin))
+
+
+def test_attention_oracle_keys_of_another_length():
+    """softmax(q k^T / sqrt(d)) v per head with 7 queries over 3 keys, against a direct evaluation."""
+    gen = torch.Generator().manual_seed(4)
+    q = torch.randn((2, 7, 2 * 128), generator=gen, dtype=torch.float64)
+    k = torch.randn((2, 3, 2 * 128), generator=gen, dtype=torch.float64)
+    v = torch.randn((2, 3, 2 * 128), generator=gen, dtype=torch.float64)
+    got = O.attention(q.numpy(), k.numpy(), v.numpy(), 2)
+    for b in range(2):
+        for h in range(2):
+            sl = slice(h * 128, (h + 1) * 128)
+            s = q[b, :, sl] @ k[b, :, sl].T / np.sqrt(128.0)
+            ref = torch.softmax(s, dim=-1) @ v[b, :, sl]
+            assert np.allclose(got[b, :, sl], ref.numpy(), rtol=1e-6, atol=1e-6)
