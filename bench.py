@@ -358,6 +358,175 @@ def run_ffn(args) -> None:
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------- the text cross-attention branch
+TEXT_METRIC = ("video text cross-attention branch µs & TFLOP/s (attn2 with cross-attention AdaLN: FP8 projections, "
+               "bf16 attention over the prompt context) at L=9216, 1/2/4/8 B200")
+
+
+def text_flops(L: int, L_ctx: int, dim: int = 4096) -> float:
+    """to_q and to_out (2·L·D² each), the context's K/V projections (2·L_ctx·D·2D) and the attention
+    (4·L·L_ctx·D)."""
+    return 4.0 * L * dim * dim + 4.0 * L_ctx * dim * dim + 4.0 * L * L_ctx * dim
+
+
+def run_text(args) -> None:
+    """``--branch text``: the same layer's video text cross-attention (sequence-local for the video tokens: at
+    N GPUs each rank runs its L/N tokens against the whole context, no exchange).  Same timing rules as the
+    attention block; the prompt context and its timestep embedding stay resident (they are fixed for all
+    steps of a request), the video tokens come from the host in the e2e leg."""
+    from opengenie_b200 import _lib, ltx_ops, synthetic
+    from opengenie_b200.graphs import StepGraph
+    from opengenie_b200.streaming import HostPipeline
+    from opengenie_b200.video_text_attention import VideoTextCrossAttention
+    from oracle import ltx_block_oracle as O
+
+    rank, world, local, pg = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    cfg = synthetic.CONFIGS[args.config]
+    L, L_ctx = cfg.tokens, args.context_tokens
+    if L % world:
+        raise SystemExit(f"{L} tokens do not split over {world} ranks")
+    Ll = L // world
+    inp_cpu = synthetic.make_text_inputs(L, L_ctx, seed=1)
+    x_loc_cpu = inp_cpu.x[:, rank * Ll:(rank + 1) * Ll].contiguous()
+    x_loc = x_loc_cpu.to(dev)
+    ts_loc = inp_cpu.timestep[:, :1].to(dev).expand(1, Ll, inp_cpu.timestep.shape[-1])
+    context = inp_cpu.context.to(dev)
+    pts = inp_cpu.prompt_timestep[:, :1].to(dev).expand(inp_cpu.prompt_timestep.shape)
+    br = VideoTextCrossAttention(synthetic.make_text_attention_weights(seed=0), dev)
+    inp_dev = inp_cpu.to(dev)
+    br.calibrate_input_scales(inp_dev.x, inp_dev.timestep, inp_dev.context, inp_dev.prompt_timestep)  # all L tokens
+    del inp_dev
+    out_dev = torch.empty_like(x_loc)
+
+    def step():
+        br(x_loc, ts_loc, context, pts, out=out_dev)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    run_step = step
+    if not args.no_graph:
+        graph = StepGraph(step, dev)
+        run_step = graph.replay
+        for _ in range(2):
+            run_step()
+        torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    barrier(pg)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            run_step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(pg)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, pg)
+
+    # e2e: pinned host x in, output back, through the host pipeline
+    x_host = x_loc_cpu.pin_memory()
+    out_hosts = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(lambda xd, yd: br(xd, ts_loc, context, pts, out=yd), tuple(x_host.shape), x_host.dtype, dev,
+                        graphs=not args.no_graph)
+    pipe.run([x_host] * 2, out_hosts)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    pipe.start_after(e0)
+    pipe.run([x_host] * args.steps, [out_hosts[i % 2] for i in range(args.steps)])
+    pipe.wait_streams(stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, pg)
+
+    # the two largest kernels timed alone on the workspace the last step left: the attention over the context
+    # and the to_out GEMM with its gated-residual epilogue; the longer one is the roofline kernel
+    w = br.w
+    D = br.dim
+    ws = br.workspace(Ll, L_ctx)
+    q, k, v = ws["q"].unsqueeze(0), ws["kv"][:, :D].unsqueeze(0), ws["kv"][:, D:].unsqueeze(0)
+    oq = torch.empty_like(ws["oq"])
+    y = torch.empty_like(x_loc)
+
+    def attn():
+        ltx_ops.attention(q, k, v, br.heads, out=oq, out_e4m3_scale=w.to_out.input_scale)
+
+    def out_gemm():
+        ltx_ops.fp8_scaled_mm_residual_gate(ws["oq"], w.to_out.weight, w.to_out.input_scale, w.to_out.weight_scale,
+                                            w.to_out.bias, x_loc, w.scale_shift_table, ts_loc, gate_index=8, out=y)
+
+    def time_alone(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        k1.record(stream)
+        torch.cuda.synchronize(dev)
+        return max_over_ranks(k0.elapsed_time(k1) / args.steps, pg)
+
+    attn_ms, gemm_ms = time_alone(attn), time_alone(out_gemm)
+    status = _lib.device_status(clear=True)
+
+    if rank == 0:
+        peaks, peak_kind = measured_peaks()
+        a_flops = 4.0 * Ll * L_ctx * D
+        g_flops = 2.0 * Ll * D * D
+        if attn_ms >= gemm_ms:
+            achieved, peak = a_flops / (attn_ms * 1e-3) / 1e12, peaks["bf16_tflops"]
+            roof = {"kernel": f"fmha_fwd_kernel<e4m3 out> ({Ll} queries over {L_ctx} keys, dominant)",
+                    "peak_kind": f"{peak_kind} bf16 dense (burst)", "algorithmic_flops_per_launch": a_flops,
+                    "kernel_ms": attn_ms}
+        else:
+            achieved, peak = g_flops / (gemm_ms * 1e-3) / 1e12, 2.0 * peaks["bf16_tflops"]
+            roof = {"kernel": "fp8_gemm_kernel<EPI_RESIDUAL> (to_out, dominant)",
+                    "peak_kind": f"2 x {peak_kind} bf16 dense (burst): tcgen05 kind::f8f6f4 runs at twice the "
+                                 "kind::f16 rate", "algorithmic_flops_per_launch": g_flops, "kernel_ms": gemm_ms}
+        line = {
+            "metric": TEXT_METRIC, "value": text_flops(L, L_ctx) / (ms * 1e-3) / 1e12, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_block": ms * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e4m3 projections, bf16 attention, fp32 accumulate",
+            "data": "synthetic (seeded inputs, random-init weights)",
+            "config": {"workload": f"LTX-2.3 video text cross-attention branch, {args.config}", "tokens": L,
+                       "context_tokens": L_ctx, "hidden": D, "heads": br.heads, "batch": 1,
+                       "parallelism": ("single GPU" if world == 1 else
+                                       f"video tokens split over {world} GPUs, whole context on each"),
+                       "l2": "inputs larger than L2 (x 75 MB + weights 67 MB + context 8 MB per branch)",
+                       "launch": "eager launches" if args.no_graph else "one CUDA graph replay per step"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, **roof,
+                         "other_kernel_ms": gemm_ms if attn_ms >= gemm_ms else attn_ms},
+            "e2e": {"value": text_flops(L, L_ctx) / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": x_host.numel() * 2 * world, "d2h_bytes_per_step": x_host.numel() * 2 * world},
+            "gpu_launches": VideoTextCrossAttention.kernel_launches_per_step * args.steps,
+            "clocks": clk.summary(), "device_status": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = len(os.sched_getaffinity(0))
+            torch.set_num_threads(threads)
+            tw_cpu = br.w.to("cpu")
+            t0 = time.perf_counter()
+            with torch.no_grad():
+                O.video_text_cross_attention_cpu_fp32(inp_cpu.x, inp_cpu.timestep.reshape(1, L, 9, D), inp_cpu.context,
+                                                      inp_cpu.prompt_timestep.reshape(1, L_ctx, 2, D), tw_cpu)
+            per = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": text_flops(L, L_ctx) / per / 1e12, "unit": UNIT, "cores": threads,
+                                    "kind": "port", "sample": f"1 full branch (L={L}, {L_ctx} context tokens) in torch "
+                                                              f"fp32 on the host; {per * 1e3:.0f} ms"}
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- a stack of layers
 def layer_flops(L: int) -> float:
     """Attention (bf16) + Q/K/V, out-projection and FFN projections (FP8) of one layer's video branches."""
@@ -436,15 +605,19 @@ def main() -> None:
     ap.add_argument("--exchange", choices=["nvlink", "nccl"], default="nvlink",
                     help="N>1: peer stores over NVLink from the producing kernels, or NCCL all-to-alls")
     ap.add_argument("--phases", action="store_true", help="add a per-stage time breakdown (separate, untimed run)")
-    ap.add_argument("--branch", choices=["attention", "ffn", "layers"], default="attention",
-                    help="the video self-attention block (the headline), the same layer's video FFN branch, or "
-                         "a stack of layers' video branches")
+    ap.add_argument("--branch", choices=["attention", "ffn", "text", "layers"], default="attention",
+                    help="the video self-attention block (the headline), the same layer's video FFN branch or "
+                         "text cross-attention branch, or a stack of layers' video branches")
+    ap.add_argument("--context-tokens", type=int, default=1024, help="--branch text: prompt context tokens")
     ap.add_argument("--layers", type=int, default=48, help="--branch layers: layers in the stack")
     ap.add_argument("--distinct-weights", type=int, default=2, help="--branch layers: random weight sets")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.branch == "ffn" and args.impl == "ours":
         run_ffn(args)
+        return
+    if args.branch == "text" and args.impl == "ours":
+        run_text(args)
         return
     if args.branch == "layers" and args.impl == "ours":
         run_layers(args)
