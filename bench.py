@@ -178,9 +178,88 @@ def cpu_reference(cfg_name: str, steps: int, warmup: int, budget_s: float = 25.0
     }
 
 
+def cpu_reference_branch(args, budget_s: float = 25.0) -> dict:
+    """The oracle port of the FFN branch, the text cross-attention branch or one layer's video branches on the
+    host cores (torch fp32, all threads), timed on full-size inputs, best of the runs within ``budget_s``.
+    Returns the same metric, unit and FLOP accounting as the GPU arm of that branch."""
+    from oracle import ltx_block_oracle as O
+    from opengenie_b200 import synthetic
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    cfg = synthetic.CONFIGS[args.config]
+    L = cfg.tokens
+    if args.branch == "ffn":
+        inp = synthetic.make_inputs(cfg, seed=1)
+        fw = synthetic.make_ffn_weights(seed=0)
+        fw.proj.input_scale = torch.tensor(0.02, dtype=torch.float32)  # static scales of the order the GPU
+        fw.out.input_scale = torch.tensor(0.002, dtype=torch.float32)  # arm calibrates (amax / 448)
+        ts_view = inp.timestep.reshape(1, L, 6, 4096)
+
+        def run():
+            O.video_ffn_cpu_fp32(inp.x, ts_view, fw)
+        flops, metric, what = ffn_flops(L), FFN_METRIC, "FFN branch"
+        workload = f"LTX-2.3 video FFN branch, {args.config}"
+    elif args.branch == "text":
+        L_ctx = args.context_tokens
+        inp = synthetic.make_text_inputs(L, L_ctx, seed=1)
+        tw = synthetic.make_text_attention_weights(seed=0)
+        for lin, s in ((tw.to_q, 0.02), (tw.to_k, 0.02), (tw.to_v, 0.02), (tw.to_out, 0.002)):
+            lin.input_scale = torch.tensor(s, dtype=torch.float32)
+        ts_view = inp.timestep.reshape(1, L, 9, 4096)
+        pts_view = inp.prompt_timestep.reshape(1, L_ctx, 2, 4096)
+
+        def run():
+            O.video_text_cross_attention_cpu_fp32(inp.x, ts_view, inp.context, pts_view, tw)
+        flops, metric, what = text_flops(L, L_ctx), TEXT_METRIC, f"text cross-attention branch ({L_ctx} context tokens)"
+        workload = f"LTX-2.3 video text cross-attention branch, {args.config}"
+    else:  # layers: one layer's video branches, scaled by the layer count
+        inp = synthetic.make_inputs(cfg, seed=1)
+        w, fw = synthetic.make_weights(seed=100), synthetic.make_ffn_weights(seed=200)
+        for lin in (w.to_q, w.to_k, w.to_v, fw.proj):
+            lin.input_scale = torch.tensor(0.02, dtype=torch.float32)
+        w.to_out.input_scale = torch.tensor(0.002, dtype=torch.float32)
+        fw.out.input_scale = torch.tensor(0.002, dtype=torch.float32)
+        ts_view = inp.timestep.reshape(1, L, 6, 4096)
+
+        def run():
+            y = O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w).to(torch.bfloat16)
+            O.video_ffn_cpu_fp32(y, ts_view, fw)
+        flops, metric, what = args.layers * layer_flops(L), layers_metric(args.layers, L), "layer (self-attention + FFN)"
+        workload = f"LTX-2.3 video DiT layers (self-attention + FFN), {args.config}"
+    times = []
+    t_start = time.perf_counter()
+    with torch.no_grad():
+        for _ in range(max(1, args.steps)):
+            t0 = time.perf_counter()
+            run()
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s:
+                break
+    per = min(times)
+    ms = per * 1e3 * (args.layers if args.branch == "layers" else 1)
+    sample = f"{len(times)} full {what} run(s) (L={L}) in torch fp32 on the host, best of {len(times)}; {per * 1e3:.0f} ms"
+    if args.branch == "layers":
+        sample += f" per layer, x {args.layers} layers"
+    return {"metric": metric, "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": sample, "ms": ms, "workload": workload}
+
+
 def run_reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.branch != "attention":
+        cb = cpu_reference_branch(args)
+        line = {
+            "metric": cb["metric"], "impl": "reference", "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16/e4m3 (fp32 on CPU)", "data": "synthetic",
+            "config": {"workload": cb["workload"], "branch": args.branch},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
         return
     cb = cpu_reference(args.config, args.steps, args.warmup)
     line = {
@@ -528,6 +607,10 @@ def run_text(args) -> None:
 
 
 # --------------------------------------------------------------------------- a stack of layers
+def layers_metric(layers: int, L: int) -> str:
+    return f"video branches of {layers} DiT layers (self-attention + FFN) ms per denoising step at L={L}, 1 B200"
+
+
 def layer_flops(L: int) -> float:
     """Attention (bf16) + Q/K/V, out-projection and FFN projections (FP8) of one layer's video branches."""
     return attn_flops(L) + 2.0 * L * 4096 * (3 * 4096 + 4096) + ffn_flops(L)
@@ -577,7 +660,7 @@ def run_layers(args) -> None:
     finite = bool(torch.isfinite(out.float()).all())
     per_layer = layer_flops(L)
     line = {
-        "metric": f"video branches of {args.layers} DiT layers (self-attention + FFN) ms per denoising step at L={L}, 1 B200",
+        "metric": layers_metric(args.layers, L),
         "value": args.layers * per_layer / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3 / args.layers, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16 attention / e4m3 projections",

@@ -28,3 +28,23 @@ def test_reference_arm_prints_one_json_line():
     assert d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["tokens"] == 2304
+
+
+def test_branch_reference_arms_keep_the_contract():
+    """``--impl reference --branch ffn|text``: the oracle port of that branch, under the branch's own metric."""
+    sys.path.insert(0, REPO)
+    import bench
+
+    for branch, metric in (("ffn", bench.FFN_METRIC), ("text", bench.TEXT_METRIC)):
+        r = subprocess.run(
+            [sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--branch", branch, "--config",
+             "c0_l2304", "--context-tokens", "256", "--steps", "1", "--warmup", "0"],
+            capture_output=True, text=True, timeout=600, cwd=REPO,
+        )
+        assert r.returncode == 0, r.stderr[-2000:]
+        lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+        assert len(lines) == 1, lines
+        d = json.loads(lines[0])
+        assert d["impl"] == "reference" and d["metric"] == metric and d["config"]["branch"] == branch
+        assert d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["kind"] == "port"
+        assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["value"] == d["value"]
