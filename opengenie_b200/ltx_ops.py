@@ -742,15 +742,24 @@ def fp8_scaled_mm_residual_gate(
     if x.shape[0] != 1:
         raise ValueError("x_shape")
     _check_index(scale_shift_table, gate_index)
+    _require_cuda(qinput, weight, scale_a, scale_b, bias)
+    if qinput.dtype != torch.float8_e4m3fn or weight.dtype != torch.float8_e4m3fn:
+        raise ValueError("fp8_dtype")
     a2 = qinput.reshape(-1, qinput.shape[-1])
     M, K = a2.shape
+    if weight.ndim != 2 or weight.shape[1] != K or weight.stride(-1) != 1 or a2.stride(-1) != 1:
+        raise ValueError("fp8_shape")
     N = weight.shape[0]
     if x.shape[1] != M or x.shape[2] != N:
         raise ValueError("x_shape")
+    if bias.ndim != 1 or bias.shape[0] != N:
+        raise ValueError("bias_shape")
     _VIDEO_ADA_VALUES_CALLS += 1
     ts_view = _ts_view(x, scale_shift_table, timestep)
     if out is None:
         out = torch.empty_like(x)
+    elif out.shape != x.shape or out.dtype != torch.bfloat16 or out.device != x.device or out.stride(-1) != 1:
+        raise ValueError("out_shape: out must be a bf16 tensor shaped like x with unit column stride")
     _lib.call(
         "ogx_fp8_scaled_mm_residual_gate",
         a2.data_ptr(), M, K, a2.stride(0), weight.data_ptr(), N, weight.stride(0),
@@ -798,6 +807,11 @@ def attention(
         raise ValueError("qkv_stride")
     scale = float(softmax_scale) if softmax_scale is not None else 128 ** -0.5
     self_attention = L_kv == L and q.stride() == k.stride()
+    if out is not None:
+        want = torch.bfloat16 if out_e4m3_scale is None else torch.float8_e4m3fn
+        if (out.shape != (B, L, HD) or out.dtype != want or out.device != q.device or out.stride(-1) != 1
+                or (L > 1 and out.stride(1) < HD)):
+            raise ValueError("out_shape: out must be [B, L, H*128] of the output dtype with unit column stride")
     if out_e4m3_scale is None:
         if out is None:
             out = torch.empty((B, L, HD), device=q.device, dtype=torch.bfloat16)
