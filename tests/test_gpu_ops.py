@@ -314,6 +314,28 @@ def test_mul_from_ada_and_residual_gate_bf16_bitwise_vs_golden(ops):
     assert status_clean()
 
 
+def test_explicit_value_ops_take_noncontiguous_rows(ops):
+    """The reference's strided-input cases (tests/test_triton_ltx_ops.py:8-47): scale/shift and gate as slices
+    of a [1, rows, 3, cols] tensor (token stride 3*cols).  AdaZero within one ulp of the one-rounding oracle;
+    the gated residual bit-equal to torch's ``x + y * gate``, as the reference asserts."""
+    g = torch.Generator().manual_seed(0)
+    rows, cols = 7, 2048
+    x = torch.randn((1, rows, cols), generator=g).to(torch.bfloat16)
+    scale_shift = torch.randn((1, rows, 3, cols), generator=g).to(torch.bfloat16).cuda()
+    scale, shift = scale_shift[:, :, 1, :], scale_shift[:, :, 2, :]
+    assert not scale.is_contiguous() and scale.stride(1) == 3 * cols
+    out = ops.fused_adazero(x.cuda(), 1e-6, scale, shift)
+    ok, worst = within_ulps(to_np(out), O.adazero_explicit(x, 1e-6, scale.float().cpu(), shift.float().cpu()),
+                            ulps=1.0, atol=1e-5)
+    assert ok, worst
+    xr = torch.randn((1, rows, cols), generator=g).to(torch.bfloat16).cuda()
+    y = torch.randn((1, rows, cols), generator=g).to(torch.bfloat16).cuda()
+    gate = scale_shift[:, :, 1, :]
+    out = ops.fused_residual_gate_bf16(xr, y, gate)
+    assert torch.equal(out, xr + y * gate)
+    assert status_clean()
+
+
 @pytest.mark.parametrize("rows", ["one", "sample", "token"])
 def test_adazero_explicit_vs_oracle(ops, rows):
     """``fused_adazero`` with explicit scale/shift of 1, batch or batch*tokens rows: within one bf16 ulp of the
