@@ -8,7 +8,9 @@ here patch a class or a module tree handed to them, following the same pattern.
 
 Also provides `video_msa_branch`, the counterpart of `_video_msa_branch_from_ada`
 (ltx_serve/triton_ltx_ops.py:2891-2981): the whole video self-attention branch of a DiT block as one
-fail-closed call that either returns the new residual stream or declines with a recorded reason.
+fail-closed call that either returns the new residual stream or declines with a recorded reason; and
+`video_text_cross_attention_branch`, the same for the text cross-attention with cross-attention AdaLN
+(`_apply_video_text_cross_attention_adaln_from_ada`, :2810-2888).
 """
 
 from __future__ import annotations
@@ -176,3 +178,73 @@ def collect_video_msa_branch_stats() -> dict:
     """Call / decline counters, as `collect_video_msa_branch_stats` (triton_ltx_ops.py:2235-2266)."""
     return {"calls": _MSA_BRANCH_CALLS, "fallbacks": sum(_MSA_BRANCH_FALLBACK_REASONS.values()),
             "fallback_reasons": dict(_MSA_BRANCH_FALLBACK_REASONS)}
+
+
+_TEXT_BRANCH_CALLS = 0
+_TEXT_BRANCH_FALLBACK_REASONS: Counter = Counter()
+_TEXT_BRANCHES: dict[int, object] = {}
+
+
+def _decline_text(reason: str):
+    _TEXT_BRANCH_FALLBACK_REASONS[reason] += 1
+    return None
+
+
+def text_attention_weights_from_modules(block, attn):
+    """The text cross-attention's weights read from the reference's module objects: ``attn`` (attn2) with FP8
+    linears ``to_q/to_k/to_v/to_out[0]`` (``weight``, ``weight_scale``, ``input_scale``, ``bias``) and
+    ``q_norm``/``k_norm`` (``weight``, ``eps``); ``block`` with the layer's ``scale_shift_table`` (9 slots),
+    ``prompt_scale_shift_table`` and ``norm_eps``.  Tensors are taken as they are, not copied."""
+    from .synthetic import Fp8Linear, TextAttentionWeights
+
+    def lin(m):
+        return Fp8Linear(m.weight, m.weight_scale, m.input_scale, m.bias)
+
+    return TextAttentionWeights(lin(attn.to_q), lin(attn.to_k), lin(attn.to_v), lin(attn.to_out[0]),
+                                attn.q_norm.weight, attn.k_norm.weight, block.scale_shift_table,
+                                block.prompt_scale_shift_table, float(block.norm_eps),
+                                float(getattr(attn.q_norm, "eps", 1e-6)))
+
+
+def video_text_cross_attention_branch(block, x: torch.Tensor, context: torch.Tensor, attn, timestep: torch.Tensor,
+                                      prompt_timestep: torch.Tensor, context_mask=None):
+    """Video text cross-attention with cross-attention AdaLN on the B200 kernels, returning the new residual
+    stream, or None with a recorded reason.
+
+    Counterpart of `_apply_video_text_cross_attention_adaln_from_ada` (ltx_serve/triton_ltx_ops.py:2810-2888),
+    same arguments.  Declines (the caller keeps the reference's path) when the block has no cross-attention
+    AdaLN or no prompt table (`no_cross_attention_adaln`, `no_prompt_table`; the reference's own branches
+    :2821-2835), on shapes other than batch 1 x 4096 (`shape`, `context_shape`), a table of fewer than 9
+    slots (`table_shape`), a context mask (`mask`: pass the prompt's valid tokens as the context instead) and
+    gated attention (`gated_attention`).  Otherwise the eight launches of ``VideoTextCrossAttention``, built
+    once per block from its modules.
+    """
+    global _TEXT_BRANCH_CALLS
+    from .video_text_attention import VideoTextCrossAttention
+
+    if not getattr(block, "cross_attention_adaln", False):
+        return _decline_text("no_cross_attention_adaln")
+    if getattr(block, "prompt_scale_shift_table", None) is None:
+        return _decline_text("no_prompt_table")
+    if x.ndim != 3 or x.shape[0] != 1 or x.shape[-1] != 4096:
+        return _decline_text("shape")
+    if context.ndim != 3 or context.shape[0] != 1 or context.shape[-1] != 4096 or context.shape[1] < 1:
+        return _decline_text("context_shape")
+    if block.scale_shift_table.ndim != 2 or block.scale_shift_table.shape[0] < 9:
+        return _decline_text("table_shape")
+    if context_mask is not None:
+        return _decline_text("mask")
+    if getattr(attn, "to_gate_logits", None) is not None:
+        return _decline_text("gated_attention")
+    branch = _TEXT_BRANCHES.get(id(block))
+    if branch is None:
+        branch = _TEXT_BRANCHES[id(block)] = VideoTextCrossAttention(text_attention_weights_from_modules(block, attn),
+                                                                     x.device)
+    _TEXT_BRANCH_CALLS += 1
+    return branch(x, timestep, context, prompt_timestep)
+
+
+def collect_video_text_branch_stats() -> dict:
+    """Call / decline counters of ``video_text_cross_attention_branch``."""
+    return {"calls": _TEXT_BRANCH_CALLS, "fallbacks": sum(_TEXT_BRANCH_FALLBACK_REASONS.values()),
+            "fallback_reasons": dict(_TEXT_BRANCH_FALLBACK_REASONS)}

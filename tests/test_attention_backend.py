@@ -1,4 +1,5 @@
-"""Host logic of the attention-backend switch and the fail-closed video MSA branch (CPU), plus its GPU run."""
+"""Host logic of the attention-backend switch, the fail-closed video MSA branch (CPU, plus its GPU run) and the
+fail-closed text cross-attention branch (CPU: declines and the weights it reads from the reference's modules)."""
 
 import types
 
@@ -81,3 +82,49 @@ def test_video_msa_branch_equals_fused_block(ogx_lib):
     out = ab.video_msa_branch(block, video, inp.x)
     assert out is not None
     assert torch.equal(out, ref_blk(inp.x, inp.timestep, (inp.cos, inp.sin)))
+
+
+def _text_modules():
+    def lin(i):
+        return types.SimpleNamespace(weight=torch.full((2, 2), float(i)), weight_scale=torch.tensor(0.1 * i),
+                                     input_scale=torch.tensor(0.01 * i), bias=torch.full((2,), float(i)))
+
+    attn2 = types.SimpleNamespace(to_q=lin(1), to_k=lin(2), to_v=lin(3), to_out=[lin(4)],
+                                  q_norm=types.SimpleNamespace(weight=torch.ones(4), eps=1e-5),
+                                  k_norm=types.SimpleNamespace(weight=torch.ones(4) * 2, eps=1e-5), to_gate_logits=None)
+    block = types.SimpleNamespace(cross_attention_adaln=True, scale_shift_table=torch.zeros(9, 4096),
+                                  prompt_scale_shift_table=torch.zeros(2, 4096), norm_eps=1e-6)
+    return block, attn2
+
+
+def test_text_cross_attention_branch_declines_with_reasons():
+    block, attn2 = _text_modules()
+    x, ctx = torch.zeros(1, 8, 4096), torch.zeros(1, 5, 4096)
+    call = ab.video_text_cross_attention_branch
+    assert call(types.SimpleNamespace(**{**vars(block), "cross_attention_adaln": False}), x, ctx, attn2, None,
+                None) is None
+    assert call(types.SimpleNamespace(**{**vars(block), "prompt_scale_shift_table": None}), x, ctx, attn2, None,
+                None) is None
+    assert call(block, torch.zeros(2, 8, 4096), ctx, attn2, None, None) is None
+    assert call(block, x, torch.zeros(1, 0, 4096), attn2, None, None) is None
+    assert call(types.SimpleNamespace(**{**vars(block), "scale_shift_table": torch.zeros(6, 4096)}), x, ctx, attn2,
+                None, None) is None
+    assert call(block, x, ctx, attn2, None, None, context_mask=torch.ones(1, 5)) is None
+    assert call(block, x, ctx, types.SimpleNamespace(**{**vars(attn2), "to_gate_logits": object()}), None,
+                None) is None
+    reasons = ab.collect_video_text_branch_stats()["fallback_reasons"]
+    for r in ("no_cross_attention_adaln", "no_prompt_table", "shape", "context_shape", "table_shape", "mask",
+              "gated_attention"):
+        assert reasons.get(r, 0) >= 1, r
+
+
+def test_text_attention_weights_read_from_the_reference_modules():
+    block, attn2 = _text_modules()
+    w = ab.text_attention_weights_from_modules(block, attn2)
+    for got, mod in ((w.to_q, attn2.to_q), (w.to_k, attn2.to_k), (w.to_v, attn2.to_v), (w.to_out, attn2.to_out[0])):
+        assert got.weight is mod.weight and got.weight_scale is mod.weight_scale
+        assert got.input_scale is mod.input_scale and got.bias is mod.bias
+    assert w.q_norm_weight is attn2.q_norm.weight and w.k_norm_weight is attn2.k_norm.weight
+    assert w.scale_shift_table is block.scale_shift_table
+    assert w.prompt_scale_shift_table is block.prompt_scale_shift_table
+    assert w.norm_eps == 1e-6 and w.qk_eps == 1e-5
