@@ -5,6 +5,7 @@ single launch on a small case.
     python -m opengenie_b200.kernel_bench gemm --m 9216 --n 12288 --k 4096 [--residual]
     python -m opengenie_b200.kernel_bench adazero --tokens 9216
     python -m opengenie_b200.kernel_bench rope --tokens 9216
+    python -m opengenie_b200.kernel_bench qk_rmsnorm --tokens 9216 --kv-tokens 1024
 
 Prints one JSON line: the average device time of a launch (CUDA events on the launching stream,
 after warm-up) and the algorithmic rate (TFLOP/s for the contractions, GB/s of unique bytes for the
@@ -119,13 +120,31 @@ def bench_rope(a) -> dict:
     return {"kernel": "qk_rmsnorm_rope_kernel", "tokens": a.tokens, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9}
 
 
+def bench_qk_rmsnorm(a) -> dict:
+    """Q/K RMSNorm without RoPE (the text cross-attention), in place on q [L, 4096] and the K half of a packed
+    [L_kv, 2*4096] K/V buffer, as the branch runs it."""
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    L_kv = a.kv_tokens or a.tokens
+    q = torch.randn((1, a.tokens, 4096), device="cuda", generator=g).to(torch.bfloat16)
+    kv = torch.randn((L_kv, 8192), device="cuda", generator=g).to(torch.bfloat16)
+    k = kv[:, :4096].unsqueeze(0)
+    qw = (1 + 0.1 * torch.randn((4096,), device="cuda", generator=g)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn((4096,), device="cuda", generator=g)).to(torch.bfloat16)
+    fn = lambda: ltx_ops.fused_qk_rmsnorm(q, k, qw, kw, 1e-6, out=(q, k))  # noqa: E731
+    ms = _time(fn, a.steps, a.warmup)
+    nbytes = (a.tokens + L_kv) * 4096 * 2 * 2  # rows read + written
+    return {"kernel": "qk_rmsnorm_rows_kernel", "tokens": a.tokens, "kv_tokens": L_kv, "ms": ms,
+            "gbs": nbytes / (ms * 1e-3) / 1e9}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["attention", "gemm", "adazero", "rope"])
+    ap.add_argument("kernel", choices=["attention", "gemm", "adazero", "rope", "qk_rmsnorm"])
     ap.add_argument("--tokens", type=int, default=9216)
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--e4m3", action="store_true")
-    ap.add_argument("--kv-tokens", type=int, default=0, help="attention: keys from a sequence of this length")
+    ap.add_argument("--kv-tokens", type=int, default=0,
+                    help="attention / qk_rmsnorm: keys from a sequence of this length")
     ap.add_argument("--m", type=int, default=9216)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=4096)
@@ -134,7 +153,8 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
-    fn = {"attention": bench_attention, "gemm": bench_gemm, "adazero": bench_adazero, "rope": bench_rope}[a.kernel]
+    fn = {"attention": bench_attention, "gemm": bench_gemm, "adazero": bench_adazero, "rope": bench_rope,
+          "qk_rmsnorm": bench_qk_rmsnorm}[a.kernel]
     print(json.dumps(fn(a)))
 
 
