@@ -851,6 +851,8 @@ def collect_video_ada_values_calls() -> int:
 
 
 __all__ = [
+    "QUANT_SINGLE",
+    "QUANT_TORCH",
     "ada_from_table_guard_reason",
     "attention",
     "collect_video_ada_values_calls",
