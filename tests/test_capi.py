@@ -110,3 +110,15 @@ def test_ops_refuse_cpu_tensors():
     cos = torch.zeros((1, 32, 4, 64), dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="qk_device_or_dtype"):
         ltx_ops.fused_video_qk_rmsnorm_rope(x, x, x[0, 0], x[0, 0], 1e-6, cos, cos)
+
+
+def test_python_surface_exports_every_public_op():
+    """``ltx_ops.__all__`` names every public function (the reference's op names and this library's fused ones)
+    and the quantiser mode constants, and nothing that does not exist."""
+    import inspect
+
+    from opengenie_b200 import ltx_ops
+
+    public = {n for n, f in vars(ltx_ops).items()
+              if inspect.isfunction(f) and f.__module__ == ltx_ops.__name__ and not n.startswith("_")}
+    assert public | {"QUANT_SINGLE", "QUANT_TORCH"} == set(ltx_ops.__all__)
