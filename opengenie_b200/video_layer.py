@@ -4,10 +4,11 @@ stack of layers per denoising step, captured once as a CUDA graph.
 In the reference's layer (``BasicAVTransformerBlock._forward`` patched by
 ``_patch_ltx_block_residuals``, ltx_serve/triton_ltx_ops.py:2984-3300) the video stream runs the
 self-attention branch (Ada slots 0-2, :3006-3083), then the text cross-attention (slots 6-8) and the
-audio-video cross-attention, then the feed-forward branch (slots 3-5, :3224-3258).  This library builds the
-two video branches; the cross-attention branches are not part of it, so a ``VideoLayer`` here is the
-self-attention block followed directly by the FFN branch.  Each layer is 8 kernel launches; a stack of
-48 is 384, which one graph replay issues at once.
+audio-video cross-attention, then the feed-forward branch (slots 3-5, :3224-3258).  A ``VideoLayer`` here is
+the self-attention block followed directly by the FFN branch: the text cross-attention branch exists on its
+own (``video_text_attention.VideoTextCrossAttention``) and is not chained in yet, and the audio-video
+cross-attention is not part of this library.  Each layer is 8 kernel launches; a stack of 48 is 384, which
+one graph replay issues at once.
 """
 
 from __future__ import annotations
