@@ -142,8 +142,41 @@ def max_over_ranks(v: float, pg) -> float:
 
 
 # --------------------------------------------------------------------------- CPU reference arm
-def cpu_reference(cfg_name: str, steps: int, warmup: int, budget_s: float = 25.0) -> dict:
-    """The reference's algorithm for the block on the host cores (the oracle port), bounded sample."""
+REF_BUDGET_S = 150.0  # wall-clock cap of the reference arm's warm-up + timed blocks
+
+
+def time_cpu_steps(run, steps: int, warmup: int, budget_s: float) -> tuple[list[float], int]:
+    """Runs ``run()`` ``warmup`` untimed times then up to ``steps`` timed times, stopping early once the
+    elapsed wall time would pass ``budget_s`` (estimated from the runs so far).  Returns the timed
+    durations (s) and the number of warm-up runs done."""
+    t_start = time.perf_counter()
+    done_warm, times = 0, []
+    est = None
+    with torch.no_grad():
+        for _ in range(max(0, warmup)):
+            t0 = time.perf_counter()
+            run()
+            est = time.perf_counter() - t0
+            done_warm += 1
+            if time.perf_counter() - t_start + est > budget_s:
+                break
+        for _ in range(max(1, steps)):
+            if times and time.perf_counter() - t_start + (est or 0.0) > budget_s:
+                break
+            t0 = time.perf_counter()
+            run()
+            times.append(time.perf_counter() - t0)
+            est = times[-1]
+    return times, done_warm
+
+
+def cpu_reference(cfg_name: str, steps: int, warmup: int, budget_s: float = REF_BUDGET_S) -> dict:
+    """The reference's algorithm for the block on the host cores (the oracle port), timed on full blocks.
+
+    Input scales are calibrated on the same input the way the GPU arm calibrates them (amax/448 of the
+    AdaZero output and of the attention output; one untimed block), then ``warmup`` untimed and up to
+    ``steps`` timed blocks run within ``budget_s`` of wall time.  ``steps`` in the result is the number of
+    blocks actually timed and ``ms_per_block`` their mean."""
     from oracle import ltx_block_oracle as O
     from opengenie_b200 import synthetic
 
@@ -153,35 +186,33 @@ def cpu_reference(cfg_name: str, steps: int, warmup: int, budget_s: float = 25.0
     inp = synthetic.make_inputs(cfg, seed=1)
     w = synthetic.make_weights(seed=0)
     ts_view = inp.timestep.reshape(1, cfg.tokens, 6, 4096)
-    # static input scales as the GPU arm calibrates them (amax / 448)
-    for lin in (w.to_q, w.to_k, w.to_v):
-        lin.input_scale = torch.tensor(0.02, dtype=torch.float32)
-    w.to_out.input_scale = torch.tensor(0.002, dtype=torch.float32)
-    times = []
-    t_start = time.perf_counter()
     with torch.no_grad():
-        for i in range(max(1, steps)):
-            t0 = time.perf_counter()
-            O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w)
-            times.append(time.perf_counter() - t0)
-            if time.perf_counter() - t_start > budget_s:
-                break
-    per_block = min(times)
+        O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w, calibrate=True)
+
+    def run():
+        O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w)
+
+    times, done_warm = time_cpu_steps(run, steps, warmup, budget_s)
+    per_block = statistics.mean(times)
     return {
         "value": attn_flops(cfg.tokens) / per_block / 1e12,
         "unit": UNIT,
         "cores": threads,
         "kind": "port",
-        "sample": f"{len(times)} full {cfg_name} block(s) (L={cfg.tokens}) in torch fp32 on the host, best of "
-                  f"{len(times)}; {per_block * 1e3:.0f} ms/block",
+        "sample": f"{len(times)} full {cfg_name} block(s) (L={cfg.tokens}) in torch fp32 on the host after "
+                  f"{done_warm} untimed, input scales calibrated as on the GPU; mean {per_block * 1e3:.0f} ms/block",
         "ms_per_block": per_block * 1e3,
+        "steps": len(times),
+        "warmup": done_warm,
     }
 
 
-def cpu_reference_branch(args, budget_s: float = 25.0) -> dict:
+def cpu_reference_branch(args, budget_s: float = REF_BUDGET_S) -> dict:
     """The oracle port of the FFN branch, the text cross-attention branch or one layer's video branches on the
-    host cores (torch fp32, all threads), timed on full-size inputs, best of the runs within ``budget_s``.
-    Returns the same metric, unit and FLOP accounting as the GPU arm of that branch."""
+    host cores (torch fp32, all threads), timed on full-size inputs (input scales calibrated as the GPU arm
+    calibrates them, one untimed run; then ``--warmup`` untimed and up to ``--steps`` timed runs within
+    ``budget_s``).  Returns the same metric, unit and FLOP accounting as the GPU arm of that branch, the
+    number of runs timed and their mean."""
     from oracle import ltx_block_oracle as O
     from opengenie_b200 import synthetic
 
@@ -192,9 +223,9 @@ def cpu_reference_branch(args, budget_s: float = 25.0) -> dict:
     if args.branch == "ffn":
         inp = synthetic.make_inputs(cfg, seed=1)
         fw = synthetic.make_ffn_weights(seed=0)
-        fw.proj.input_scale = torch.tensor(0.02, dtype=torch.float32)  # static scales of the order the GPU
-        fw.out.input_scale = torch.tensor(0.002, dtype=torch.float32)  # arm calibrates (amax / 448)
         ts_view = inp.timestep.reshape(1, L, 6, 4096)
+        with torch.no_grad():
+            O.video_ffn_cpu_fp32(inp.x, ts_view, fw, calibrate=True)
 
         def run():
             O.video_ffn_cpu_fp32(inp.x, ts_view, fw)
@@ -204,10 +235,10 @@ def cpu_reference_branch(args, budget_s: float = 25.0) -> dict:
         L_ctx = args.context_tokens
         inp = synthetic.make_text_inputs(L, L_ctx, seed=1)
         tw = synthetic.make_text_attention_weights(seed=0)
-        for lin, s in ((tw.to_q, 0.02), (tw.to_k, 0.02), (tw.to_v, 0.02), (tw.to_out, 0.002)):
-            lin.input_scale = torch.tensor(s, dtype=torch.float32)
         ts_view = inp.timestep.reshape(1, L, 9, 4096)
         pts_view = inp.prompt_timestep.reshape(1, L_ctx, 2, 4096)
+        with torch.no_grad():
+            O.video_text_cross_attention_cpu_fp32(inp.x, ts_view, inp.context, pts_view, tw, calibrate=True)
 
         def run():
             O.video_text_cross_attention_cpu_fp32(inp.x, ts_view, inp.context, pts_view, tw)
@@ -216,33 +247,25 @@ def cpu_reference_branch(args, budget_s: float = 25.0) -> dict:
     else:  # layers: one layer's video branches, scaled by the layer count
         inp = synthetic.make_inputs(cfg, seed=1)
         w, fw = synthetic.make_weights(seed=100), synthetic.make_ffn_weights(seed=200)
-        for lin in (w.to_q, w.to_k, w.to_v, fw.proj):
-            lin.input_scale = torch.tensor(0.02, dtype=torch.float32)
-        w.to_out.input_scale = torch.tensor(0.002, dtype=torch.float32)
-        fw.out.input_scale = torch.tensor(0.002, dtype=torch.float32)
         ts_view = inp.timestep.reshape(1, L, 6, 4096)
+        with torch.no_grad():
+            y0 = O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w, calibrate=True).to(torch.bfloat16)
+            O.video_ffn_cpu_fp32(y0, ts_view, fw, calibrate=True)
 
         def run():
             y = O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w).to(torch.bfloat16)
             O.video_ffn_cpu_fp32(y, ts_view, fw)
         flops, metric, what = args.layers * layer_flops(L), layers_metric(args.layers, L), "layer (self-attention + FFN)"
         workload = f"LTX-2.3 video DiT layers (self-attention + FFN), {args.config}"
-    times = []
-    t_start = time.perf_counter()
-    with torch.no_grad():
-        for _ in range(max(1, args.steps)):
-            t0 = time.perf_counter()
-            run()
-            times.append(time.perf_counter() - t0)
-            if time.perf_counter() - t_start > budget_s:
-                break
-    per = min(times)
+    times, done_warm = time_cpu_steps(run, args.steps, args.warmup, budget_s)
+    per = statistics.mean(times)
     ms = per * 1e3 * (args.layers if args.branch == "layers" else 1)
-    sample = f"{len(times)} full {what} run(s) (L={L}) in torch fp32 on the host, best of {len(times)}; {per * 1e3:.0f} ms"
+    sample = (f"{len(times)} full {what} run(s) (L={L}) in torch fp32 on the host after {done_warm} untimed, input "
+              f"scales calibrated as on the GPU; mean {per * 1e3:.0f} ms")
     if args.branch == "layers":
         sample += f" per layer, x {args.layers} layers"
     return {"metric": metric, "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": sample, "ms": ms, "workload": workload}
+            "sample": sample, "ms": ms, "workload": workload, "steps": len(times), "warmup": done_warm}
 
 
 def run_reference_arm(args) -> None:
@@ -253,7 +276,7 @@ def run_reference_arm(args) -> None:
         cb = cpu_reference_branch(args)
         line = {
             "metric": cb["metric"], "impl": "reference", "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms"], "higher_is_better": True,
+            "steps": cb["steps"], "warmup": cb["warmup"], "ms_per_step": cb["ms"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16/e4m3 (fp32 on CPU)", "data": "synthetic",
             "config": {"workload": cb["workload"], "branch": args.branch},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -264,16 +287,16 @@ def run_reference_arm(args) -> None:
     cb = cpu_reference(args.config, args.steps, args.warmup)
     line = {
         "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_block"], "higher_is_better": True,
+        "steps": cb["steps"], "warmup": cb["warmup"], "ms_per_step": cb["ms_per_block"], "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16/e4m3 (fp32 on CPU)", "data": "synthetic",
-        "config": config_dict(args.config, args.gpus, args.exchange, graph=False),
+        "config": config_dict(args.config, args.gpus, args.exchange),
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def config_dict(name: str, n: int, exchange: str = "nvlink", graph: bool = True) -> dict:
+def config_dict(name: str, n: int, exchange: str = "nvlink") -> dict:
     from opengenie_b200 import synthetic
 
     cfg = synthetic.CONFIGS[name]
@@ -284,7 +307,6 @@ def config_dict(name: str, n: int, exchange: str = "nvlink", graph: bool = True)
         "attention": "bf16, fp32 softmax/accumulate", "per_token_timestep": cfg.per_token_timestep,
         "parallelism": "single GPU" if n == 1 else f"ulysses heads {32 // n}/GPU, {exchange} exchange",
         "l2": "inputs larger than L2 (x 75 MB + weights 67 MB + cos/sin 75 MB read per block)",
-        "launch": "one CUDA graph replay per step" if graph else "eager launches",
     }
 
 
@@ -559,7 +581,7 @@ def run_text(args) -> None:
         g_flops = 2.0 * Ll * D * D
         if attn_ms >= gemm_ms:
             achieved, peak = a_flops / (attn_ms * 1e-3) / 1e12, peaks["bf16_tflops"]
-            roof = {"kernel": f"fmha_fwd_kernel<e4m3 out> ({Ll} queries over {L_ctx} keys, dominant)",
+            roof = {"kernel": f"attn_fwd_kernel<e4m3 out> ({Ll} queries over {L_ctx} keys, dominant)",
                     "peak_kind": f"{peak_kind} bf16 dense (burst)", "algorithmic_flops_per_launch": a_flops,
                     "kernel_ms": attn_ms}
         else:
@@ -829,9 +851,10 @@ def main() -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "us_per_block": ms * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 attention / e4m3 projections",
-            "data": "synthetic (seeded inputs, random-init weights)", "config": config_dict(args.config, world, args.exchange, use_graph),
+            "data": "synthetic (seeded inputs, random-init weights)", "config": config_dict(args.config, world, args.exchange),
+            "launch": "one CUDA graph replay per step" if use_graph else "eager launches",
             "roofline": {
-                "bound": "tensor", "kernel": "fmha_fwd_kernel (attention, dominant)",
+                "bound": "tensor", "kernel": "attn_fwd_kernel (attention, dominant)",
                 "achieved": achieved, "peak": peaks.get("bf16_tflops"), "unit": "TFLOP/s",
                 "frac": (achieved / peaks["bf16_tflops"]) if achieved else None,
                 "peak_kind": f"{peak_kind} bf16 dense (burst)",
@@ -847,7 +870,7 @@ def main() -> None:
         if phases is not None:
             line["phases_ms"] = phases
         if world == 1 and not args.no_cpu_baseline:
-            cb = cpu_reference(args.config, 2, 0, budget_s=20.0)
+            cb = cpu_reference(args.config, 3, 1, budget_s=30.0)
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
     if pg is not None:

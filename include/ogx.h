@@ -264,13 +264,17 @@ int ogx_peer_barrier(unsigned int* local_signals, void* const* peer_signals, int
  * cannot allocate device memory, e.g. a runtime driving all of its GPUs from one process with their
  * memory reserved up front for its own pool.  The signal block is a 64-byte array inside the library,
  * one per GPU that loads it and held until the process exits; it is zero at load and never cleared
- * (barrier numbers only grow).  Ranks are GPUs of this process: devices[i] is rank i's device ordinal,
- * devices[rank] must be the current device, and the caller enables peer access between them
- * (cudaDeviceEnablePeerAccess) before a call with world > 1.  world is at most 8; larger values are
- * rejected.  The first call naming a device looks up that device's array address (so make it before
- * any stream capture).  count_out (device memory, may be NULL) receives the number of barriers this
+ * (barrier numbers only grow).  Ranks are GPUs of this process: devices[i] is rank i's device ordinal
+ * (no ordinal twice), devices[rank] must be the current device, and every pair must be able to reach
+ * each other (cudaDeviceCanAccessPeer); the call enables access from the current device to each peer
+ * if the caller has not (a per-process mapping).  world is at most 8; larger values are rejected.
+ * Set-up: the first call naming a device looks up that device's array address with the device made
+ * current, which creates the device's primary context if it has none (the context, not this call,
+ * takes device memory) and may load the library's module there.  So every device in devices[] should
+ * already have its context, and one warm-up call per rank should run before serving starts and before
+ * any stream capture.  count_out (device memory, may be NULL) receives the number of barriers this
  * rank has passed.  Every call on a device shares its array: one barrier group per process, and calls
- * that overlap on a GPU race.  Allocates nothing. */
+ * that overlap on a GPU race.  Allocates no device memory. */
 int ogx_peer_barrier_static(int rank, int world, const int* devices, unsigned int* count_out, void* stream);
 
 /* ogx_video_qkv_rmsnorm_rope_scatter with one destination base per head group (groups = world size):

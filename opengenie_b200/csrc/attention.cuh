@@ -33,7 +33,7 @@
 #include "elementwise.cuh"
 
 namespace ogx {
-namespace fmha {
+namespace attn {
 
 constexpr int HD = 128;
 constexpr int BQ = 128;
@@ -163,7 +163,7 @@ __device__ __forceinline__ void load_rows(uint8_t* dst, const CUtensorMap* map, 
 
 template <bool OUT_E4M3>
 __global__ void __launch_bounds__(kThreads, 1)
-    fmha_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, Params p) {
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
@@ -443,7 +443,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* dst;
             if (p.peer_tokens > 0) {
               const int d = tok / p.peer_tokens;
-              dst = p.out_peer[d] + static_cast<int64_t>(tok - d * p.peer_tokens) * p.out_stride_t;
+              // constant-index selects: a runtime index into the parameter array would copy it to local memory
+              uint8_t* peer = p.out_peer[0];
+#pragma unroll
+              for (int i = 1; i < 8; ++i) peer = (d == i) ? p.out_peer[i] : peer;
+              dst = peer + static_cast<int64_t>(tok - d * p.peer_tokens) * p.out_stride_t;
             } else {
               dst = p.out_q + static_cast<int64_t>(batch) * p.out_stride_b + static_cast<int64_t>(tok) * p.out_stride_t;
             }
@@ -482,5 +486,5 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-}  // namespace fmha
+}  // namespace attn
 }  // namespace ogx

@@ -571,6 +571,15 @@ struct RopeArgs {
   int system_fence;  // fence the stores system-wide at exit (peer destinations)
 };
 
+// Base pointer of head group g (< 8) by constant-index selects: a runtime index into the kernel's parameter
+// array would copy the array to local memory.
+__device__ __forceinline__ __nv_bfloat16* group_base(__nv_bfloat16* const (&bases)[8], int g) {
+  __nv_bfloat16* b = bases[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) b = (g == i) ? bases[i] : b;
+  return b;
+}
+
 template <typename WT, typename CsT>
 __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* in, const WT* w, const CsT* cosb,
                                                  const CsT* sinb, const RopeArgs& a, int64_t t, float* red, int j_out) {
@@ -611,7 +620,7 @@ __device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* in, const 
       o[i] = second ? fmaf(n[i], c[i], other[i] * s[i]) : fmaf(n[i], c[i], -(other[i] * s[i]));
     const int g = head / a.heads_per_group;
     const int hl = head - g * a.heads_per_group;
-    __nv_bfloat16* dst = a.dst[j_out][g] + t * a.out_stride_t + hl * 128 + (col & 127);
+    __nv_bfloat16* dst = group_base(a.dst[j_out], g) + t * a.out_stride_t + hl * 128 + (col & 127);
     *reinterpret_cast<uint4*>(dst) = pack8(o);
   }
 }
@@ -639,7 +648,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) qk_rmsnorm_rope_kernel(RopeArg
       const int g = head / a.heads_per_group;
       const int hl = head - g * a.heads_per_group;
       const uint4 val = __ldg(reinterpret_cast<const uint4*>(vin) + vec);
-      *reinterpret_cast<uint4*>(a.dst[2][g] + t * a.out_stride_t + hl * 128 + (col & 127)) = val;
+      *reinterpret_cast<uint4*>(group_base(a.dst[2], g) + t * a.out_stride_t + hl * 128 + (col & 127)) = val;
     }
   }
   if (a.system_fence) {

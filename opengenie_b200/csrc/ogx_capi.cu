@@ -19,7 +19,7 @@
 
 #include "../../include/ogx.h"
 #include "elementwise.cuh"
-#include "fmha.cuh"
+#include "attention.cuh"
 #include "fp8_gemm.cuh"
 #include "peer.cuh"
 
@@ -716,8 +716,8 @@ int attention_common(const void* q, const void* k, const void* v, int64_t batch,
   const uint64_t kvdims[4] = {128, static_cast<uint64_t>(heads), static_cast<uint64_t>(kv_tokens),
                               static_cast<uint64_t>(batch)};
   const uint64_t kvstrides[3] = {256, static_cast<uint64_t>(kv_stride_t) * 2, static_cast<uint64_t>(kv_stride_b) * 2};
-  const uint32_t qbox[4] = {64, 1, static_cast<uint32_t>(ogx::fmha::BQ), 1};
-  const uint32_t kvbox[4] = {64, 1, static_cast<uint32_t>(ogx::fmha::BKV), 1};
+  const uint32_t qbox[4] = {64, 1, static_cast<uint32_t>(ogx::attn::BQ), 1};
+  const uint32_t kvbox[4] = {64, 1, static_cast<uint32_t>(ogx::attn::BKV), 1};
   int rc = make_map(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, q, qdims, qstrides, qbox);
   if (rc) return rc;
   rc = make_map(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k, kvdims, kvstrides, kvbox);
@@ -727,22 +727,22 @@ int attention_common(const void* q, const void* k, const void* v, int64_t batch,
 
 template <bool E4M3>
 int attention_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int64_t batch,
-                     int64_t tokens, int64_t heads, const ogx::fmha::Params& p, cudaStream_t s) {
-  auto kern = ogx::fmha::fmha_fwd_kernel<E4M3>;
-  int rc = ensure_smem(kern, ogx::fmha::SMEM_BYTES);
+                     int64_t tokens, int64_t heads, const ogx::attn::Params& p, cudaStream_t s) {
+  auto kern = ogx::attn::attn_fwd_kernel<E4M3>;
+  int rc = ensure_smem(kern, ogx::attn::SMEM_BYTES);
   if (rc) return rc;
   // The softmax warpgroups raise their register limit with setmaxnreg, drawing on the registers the
   // launch reserved; only launch a build whose per-thread count is the one the split was sized for.
   cudaFuncAttributes attr;
   rc = check_cuda(cudaFuncGetAttributes(&attr, kern), "cudaFuncGetAttributes");
   if (rc) return rc;
-  if (attr.numRegs != ogx::fmha::kLaunchRegs)
-    return fail(OGX_ECUDA, "fmha kernel built with %d registers per thread, the register split needs %d", attr.numRegs,
-                ogx::fmha::kLaunchRegs);
+  if (attr.numRegs != ogx::attn::kLaunchRegs)
+    return fail(OGX_ECUDA, "attention kernel built with %d registers per thread, the register split needs %d", attr.numRegs,
+                ogx::attn::kLaunchRegs);
   const dim3 grid(static_cast<unsigned>((tokens + 255) / 256), static_cast<unsigned>(heads),
                   static_cast<unsigned>(batch));
-  launch(kern, grid, ogx::fmha::kThreads, ogx::fmha::SMEM_BYTES, s, mq, mk, mv, p);
-  return check_launch("fmha_fwd_kernel");
+  launch(kern, grid, ogx::attn::kThreads, ogx::attn::SMEM_BYTES, s, mq, mk, mv, p);
+  return check_launch("attn_fwd_kernel");
 }
 
 }  // namespace
@@ -873,7 +873,7 @@ int ogx_attention_fwd(const void* q, const void* k, const void* v, int64_t batch
                             &mq, &mk, &mv);
   if (rc) return rc;
   if (out == nullptr || !aligned16(out) || out_stride_t % 8 || out_stride_b % 8) return fail(OGX_EINVAL, "output");
-  ogx::fmha::Params p{};
+  ogx::attn::Params p{};
   p.L = static_cast<int>(tokens);
   p.L_kv = p.L;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
@@ -893,7 +893,7 @@ int ogx_attention_fwd_e4m3(const void* q, const void* k, const void* v, int64_t 
   if (rc) return rc;
   if (out_q == nullptr || out_scale == nullptr || !aligned16(out_q) || out_stride_t % 16 || out_stride_b % 16)
     return fail(OGX_EINVAL, "output");
-  ogx::fmha::Params p{};
+  ogx::attn::Params p{};
   p.L = static_cast<int>(tokens);
   p.L_kv = p.L;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
@@ -913,7 +913,7 @@ int ogx_attention_fwd_kv(const void* q, const void* k, const void* v, int64_t ba
                             kv_stride_t, &mq, &mk, &mv);
   if (rc) return rc;
   if (out == nullptr || !aligned16(out) || out_stride_t % 8 || out_stride_b % 8) return fail(OGX_EINVAL, "output");
-  ogx::fmha::Params p{};
+  ogx::attn::Params p{};
   p.L = static_cast<int>(q_tokens);
   p.L_kv = static_cast<int>(kv_tokens);
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
@@ -934,7 +934,7 @@ int ogx_attention_fwd_kv_e4m3(const void* q, const void* k, const void* v, int64
   if (rc) return rc;
   if (out_q == nullptr || out_scale == nullptr || !aligned16(out_q) || out_stride_t % 16 || out_stride_b % 16)
     return fail(OGX_EINVAL, "output");
-  ogx::fmha::Params p{};
+  ogx::attn::Params p{};
   p.L = static_cast<int>(q_tokens);
   p.L_kv = static_cast<int>(kv_tokens);
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
@@ -1055,7 +1055,7 @@ int ogx_attention_fwd_e4m3_to_peers(const void* q, const void* k, const void* v,
   if (peer_bases == nullptr || out_scale == nullptr || peers < 1 || peers > 8) return fail(OGX_EINVAL, "peers");
   if (tokens_per_peer < 1 || tokens_per_peer * peers != tokens) return fail(OGX_EINVAL, "tokens_per_peer");
   if (out_stride_t % 16 || out_stride_t < heads * 128) return fail(OGX_EINVAL, "output");
-  ogx::fmha::Params p{};
+  ogx::attn::Params p{};
   p.L = static_cast<int>(tokens);
   p.L_kv = p.L;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
@@ -1127,6 +1127,12 @@ int ogx_peer_barrier_static(int rank, int world, const int* devices, unsigned in
   if (rc) return rc;
   if (devices[rank] != cur)
     return fail(OGX_EINVAL, "devices[rank] is %d but the current device is %d", devices[rank], cur);
+  // Two ranks on one ordinal would share one slot/count block: their barrier numbers would drift apart and
+  // every later wait would run out.
+  for (int i = 0; i < world; ++i)
+    for (int j = i + 1; j < world; ++j)
+      if (devices[i] == devices[j])
+        return fail(OGX_EINVAL, "devices: ranks %d and %d both name device %d", i, j, devices[i]);
   unsigned int* local = nullptr;
   rc = static_peer_block(cur, &local);
   if (rc) return rc;
@@ -1137,6 +1143,17 @@ int ogx_peer_barrier_static(int rank, int world, const int* devices, unsigned in
       rc = check_cuda(cudaDeviceCanAccessPeer(&can, cur, devices[i]), "cudaDeviceCanAccessPeer");
       if (rc) return rc;
       if (!can) return fail(OGX_EINVAL, "device %d cannot access peer device %d", cur, devices[i]);
+      // The kernel stores into the peer's copy of the block: access must be enabled, not merely possible,
+      // or the store is an illegal address.  Enabling is a per-process mapping (no lasting GPU setting);
+      // an access the caller already enabled is reported as such and is fine.
+      const cudaError_t e = cudaDeviceEnablePeerAccess(devices[i], 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();  // clear the sticky-free status this call leaves
+      } else if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(OGX_EINVAL, "peer access from device %d to device %d could not be enabled: %s", cur, devices[i],
+                    cudaGetErrorString(e));
+      }
     }
     rc = static_peer_block(devices[i], &ps.slot[i]);
     if (rc) return rc;

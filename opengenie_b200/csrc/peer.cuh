@@ -34,7 +34,11 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(unsigned int* local, P
   const int i = threadIdx.x;
   const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(local + kPeerCountWord) + 1u;
   if (i < world && i != rank) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.slot[i] + rank), "r"(epoch) : "memory");
+    // constant-index selects: a runtime index into the parameter array would copy it to local memory
+    unsigned int* peer = peers.slot[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) peer = (i == j) ? peers.slot[j] : peer;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer + rank), "r"(epoch) : "memory");
     const unsigned long long t0 = global_ns();
     for (uint32_t n = 0;; ++n) {
       unsigned int v;

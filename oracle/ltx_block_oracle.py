@@ -377,11 +377,15 @@ def video_block(x, timestep_view, cos, sin, w, *, eps: float = 1e-6, qk_eps: flo
 
 
 def video_block_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, w, *,
-                         eps: float = 1e-6, qk_eps: float = 1e-6, heads: int = 32) -> torch.Tensor:
+                         eps: float = 1e-6, qk_eps: float = 1e-6, heads: int = 32,
+                         calibrate: bool = False) -> torch.Tensor:
     """The same block on CPU torch in float32 (multi-threaded), used as the timed CPU baseline.
 
     Same stages and rounding points as ``video_block`` (torch ops instead of float64
-    numpy), so it runs at full-size configurations in seconds, not hours.
+    numpy), so it runs at full-size configurations in seconds, not hours.  With
+    ``calibrate`` the static input scales are first set from this input the way the
+    GPU block calibrates them: amax/448 of the AdaZero output for to_q/to_k/to_v and
+    of the bf16 attention output for to_out (written into ``w``).
     """
     def r16(t):
         return t.to(torch.bfloat16).float()
@@ -397,6 +401,10 @@ def video_block_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, cos: torc
 
     xf = x.float()
     norm = r16(xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1 + ada(1)) + ada(0))
+    if calibrate:
+        s_in = (norm.abs().amax().clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
+        for lin_ in (w.to_q, w.to_k, w.to_v):
+            lin_.input_scale = s_in.clone()
 
     def quant(t, s):
         r = torch.tensor(1.0, dtype=torch.float32) / s.float()
@@ -429,6 +437,8 @@ def video_block_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, cos: torc
 
     qr, kr = rope(q, w.q_norm_weight), rope(k, w.k_norm_weight)
     attn = r16(attention_fp32_torch(qr, kr, v, heads))
+    if calibrate:
+        w.to_out.input_scale = (attn.abs().amax().clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
     oq = quant(attn, w.to_out.input_scale)
     y = lin(oq, w.to_out.input_scale, w.to_out, bias=False)
     gate = ada(2)
@@ -468,11 +478,14 @@ def video_ffn(x, timestep_view, fw, *, eps: float = 1e-6, return_intermediates: 
     return out
 
 
-def video_ffn_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, fw, *, eps: float = 1e-6) -> torch.Tensor:
+def video_ffn_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, fw, *, eps: float = 1e-6,
+                      calibrate: bool = False) -> torch.Tensor:
     """The same branch with every contraction in fp32 torch (on the tensors' device): the timed CPU
     baseline and the fp32 reference of the full-size GPU tolerance test.  Same stages and rounding
     points as ``video_ffn``; the quantisers keep the reference's torch-path semantics (activations are
-    FP8 in the model), with 1/s kept in fp32 as the reference's CPU path computes it."""
+    FP8 in the model), with 1/s kept in fp32 as the reference's CPU path computes it.  With
+    ``calibrate`` the two input scales are first set to amax/448 of the AdaZero output and of the GELU
+    output, as the GPU branch calibrates them (written into ``fw``)."""
     dev = x.device
 
     def r16(t):
@@ -501,8 +514,12 @@ def video_ffn_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, fw, *, eps:
             y = r16(y + r16(l.bias.to(dev).float()))
         return y.view(*tq.shape[:-1], -1)
 
+    if calibrate:
+        fw.proj.input_scale = (norm.abs().amax().clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
     hidden = lin(quant(norm, fw.proj.input_scale), fw.proj.input_scale, fw.proj)
     g = torch.nn.functional.gelu(hidden.to(torch.bfloat16), approximate="tanh").float()
+    if calibrate:
+        fw.out.input_scale = (g.abs().amax().clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
     y = lin(quant(g, fw.out.input_scale), fw.out.input_scale, fw.out, bias=False)
     yb = r16(y + r16(fw.out.bias.to(dev).float()))
     return r16(xf + r16(yb * ada(5))).to(torch.bfloat16)
@@ -556,9 +573,13 @@ def video_text_cross_attention(x, timestep_view, context, prompt_timestep_view, 
 
 
 def video_text_cross_attention_cpu_fp32(x: torch.Tensor, timestep_view: torch.Tensor, context: torch.Tensor,
-                                        prompt_timestep_view: torch.Tensor, tw, *, heads: int = 32) -> torch.Tensor:
+                                        prompt_timestep_view: torch.Tensor, tw, *, heads: int = 32,
+                                        calibrate: bool = False) -> torch.Tensor:
     """The same branch on CPU torch in float32 (multi-threaded): same stages and rounding points as
-    ``video_text_cross_attention``, fp32 contractions, so full-size configurations finish in seconds."""
+    ``video_text_cross_attention``, fp32 contractions, so full-size configurations finish in seconds.
+    With ``calibrate`` the input scales are first set to amax/448 of each linear's input (the AdaZero
+    output for to_q, the context after its affine for to_k/to_v, the attention output for to_out), as
+    the GPU branch calibrates them (written into ``tw``)."""
     def r16(t):
         return t.to(torch.bfloat16).float()
 
@@ -593,9 +614,18 @@ def video_text_cross_attention_cpu_fp32(x: torch.Tensor, timestep_view: torch.Te
     def rms(t, weight):
         return r16(t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + tw.qk_eps) * weight.float())
 
+    def amax_scale(t):
+        return (t.abs().amax().clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
+
+    if calibrate:
+        tw.to_q.input_scale = amax_scale(norm)
+        tw.to_k.input_scale = amax_scale(ctx)
+        tw.to_v.input_scale = tw.to_k.input_scale.clone()
     q = rms(lin(norm, tw.to_q), tw.q_norm_weight)
     k = rms(lin(ctx, tw.to_k), tw.k_norm_weight)
     v = lin(ctx, tw.to_v)
     attn = r16(attention_fp32_torch(q, k, v, heads))
+    if calibrate:
+        tw.to_out.input_scale = amax_scale(attn)
     y = lin(attn, tw.to_out)
     return r16(xf + r16(y * ada(8)))

@@ -28,6 +28,28 @@ def test_reference_arm_prints_one_json_line():
     assert d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["tokens"] == 2304
+    # the line reports the blocks it actually timed and warmed up with (bench.py raises --warmup to 3)
+    assert d["steps"] == 1 and d["warmup"] == 3
+
+
+def test_reference_arm_stops_within_its_budget():
+    """Asked for more blocks than fit in the wall-clock budget, the arm times fewer and says how many."""
+    sys.path.insert(0, REPO)
+    import time
+
+    import bench
+
+    calls = []
+
+    def run():
+        calls.append(time.perf_counter())
+        time.sleep(0.05)
+
+    times, warm = bench.time_cpu_steps(run, steps=100, warmup=2, budget_s=0.4)
+    assert warm == 2
+    assert 1 <= len(times) < 100
+    assert len(calls) == warm + len(times)
+    assert calls[-1] - calls[0] < 0.4
 
 
 def test_branch_reference_arms_keep_the_contract():

@@ -140,7 +140,7 @@ def test_block_zero_gate_is_identity(ogx_lib):
     assert torch.equal(out, dev.x)
 
 
-@pytest.mark.parametrize("name", ["c1_l9216", "c2_df_l9216"])
+@pytest.mark.parametrize("name", ["c1_l9216", "c2_df_l9216", "c4_l28800"])
 def test_block_full_size_vs_fp32_reference_on_gpu(ogx_lib, name):
     """L=9216 (uniform and diffusion-forcing timesteps): the fused block against the same stages in
     torch fp32 on the GPU (fp32 matmuls on the dequantised e4m3 operands, fp32 SDPA).

@@ -38,8 +38,11 @@ def _accum_atol(aq, s_a, wq, s_w):
     return accum_atol(codes(aq), s_a, codes(wq), s_w)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (17, 256, 4096), (300, 512, 4096), (256, 4096, 1024), (1, 32, 16)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (17, 256, 4096), (300, 512, 4096), (256, 4096, 1024), (1, 32, 16),
+                                   (3600, 512, 4096)])
 def test_fp8_gemm_bias_vs_oracle(ops, M, N, K):
+    """(3600, ...): the per-GPU row count of the 720p-class window (L = 28800) over 8 GPUs, whose last row
+    tile is ragged (3600 = 14 * 256 + 16)."""
     aq, s_a, wq, s_w, bias = _fp8_case(M, N, K, seed=M * 7 + N)
     out = ops.fp8_scaled_mm(aq.cuda(), wq.cuda(), torch.tensor(s_a, device="cuda"), torch.tensor([s_w], device="cuda"),
                             bias=bias.cuda())
@@ -115,7 +118,7 @@ def test_fp8_gemm_residual_epilogue_vs_oracle(ops):
     assert ok, worst
 
 
-@pytest.mark.parametrize("M,blocks", [(4608, 2), (1152, 8), (300, 4)])
+@pytest.mark.parametrize("M,blocks", [(4608, 2), (1152, 8), (300, 4), (3600, 8)])
 def test_fp8_gemm_residual_kblocked_equals_plain(ops, M, blocks):
     """The out-projection reading A as `blocks` column blocks [blocks][M][K/blocks] (the Ulysses receive
     buffer, through a 3-D tensor map) equals the same GEMM on the assembled [M, K] operand, bit for bit,
@@ -191,9 +194,11 @@ def test_attention_packed_rows_and_e4m3_epilogue(ops):
     assert np.array_equal(codes(oq), codes(ops.fused_fp8_quantize_e4m3(out, s)))
 
 
-@pytest.mark.parametrize("L", [2304, 9216])
+@pytest.mark.parametrize("L", [2304, 9216, 28800])
 def test_attention_full_size_vs_torch_sdpa(ops, L):
-    """Full configuration sizes against torch SDPA on the same GPU (fp32 math per head)."""
+    """Full configuration sizes against torch SDPA on the same GPU (fp32 math per head), within the north-star
+    bound as stated: max|d| <= 2e-2 and sum|d|/sum|ref| <= 1e-2.  L = 28800 (the 720p-class window) ends in
+    a ragged query block: 28800 = 112 * 256 + 128, so the last CTA's second 128-query tile is all padding."""
     H = 32
     g = torch.Generator(device="cuda").manual_seed(L)
     q, k, v = (torch.randn((1, L, H * 128), device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
@@ -205,7 +210,7 @@ def test_attention_full_size_vs_torch_sdpa(ops, L):
                                                                vh[:, h:h + 4].float())
         got = out.view(1, L, H, 128).transpose(1, 2)[:, h:h + 4].float()
         d = (got - ref).abs()
-        worst_max = max(worst_max, (d - 2.0 ** -7 * ref.abs()).max().item())
+        worst_max = max(worst_max, d.max().item())
         num += d.sum().item()
         den += ref.abs().sum().item()
     assert worst_max <= 2e-2

@@ -74,7 +74,7 @@ def _worker(rank, world, port, cfg_name, exchange, result):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
-@pytest.mark.parametrize("cfg_name", ["c0_l2304", "c2_df_l9216"])
+@pytest.mark.parametrize("cfg_name", ["c0_l2304", "c2_df_l9216", "c4_l28800"])
 @pytest.mark.parametrize("exchange", ["nvlink", "nccl"])
 def test_ulysses_block_equals_single_gpu(ogx_lib, cfg_name, exchange):
     import torch.multiprocessing as mp

@@ -52,3 +52,58 @@ def test_static_barrier_rejects_more_ranks_than_its_block_holds(ogx_lib):
     assert ogx_lib.ogx_peer_barrier_static(0, 9, devices, None, stream) != 0
     assert b"at most 8 ranks" in ogx_lib.ogx_last_error()
     assert ogx_lib.ogx_peer_barrier_static(1, 1, devices, None, stream) != 0
+
+
+def test_static_barrier_rejects_a_device_named_twice(ogx_lib):
+    dev = torch.cuda.current_device()
+    devices = (ctypes.c_int * 2)(dev, dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert ogx_lib.ogx_peer_barrier_static(0, 2, devices, None, stream) != 0
+    assert b"both name device" in ogx_lib.ogx_last_error()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in this process")
+def test_static_barrier_across_two_gpus_of_one_process(ogx_lib):
+    """The part the one-GPU case cannot reach: each device's copy of the array looked up on its own
+    device, and the stores into the other GPU's copy (plain peer stores, no multicast).  Two ranks on
+    GPUs 0 and 1 of this process, each on its own stream, pass two barriers together."""
+    from opengenie_b200 import _lib
+
+    counts = [torch.zeros(1, dtype=torch.int32, device=f"cuda:{d}") for d in (0, 1)]
+    streams = [torch.cuda.Stream(device=d) for d in (0, 1)]
+    solo = (ctypes.c_int * 1)()
+
+    def one_rank_barrier(d):
+        # a group of one on device d: advances d's count by one and returns it
+        solo[0] = d
+        with torch.cuda.device(d):
+            assert ogx_lib.ogx_peer_barrier_static(0, 1, solo, counts[d].data_ptr(), streams[d].cuda_stream) == 0, \
+                ogx_lib.ogx_last_error()
+            streams[d].synchronize()
+        return int(counts[d].item())
+
+    # the counts live for the whole process: bring both devices to the same barrier number first
+    c = [one_rank_barrier(0), one_rank_barrier(1)]
+    while c[0] != c[1]:
+        lo = 0 if c[0] < c[1] else 1
+        c[lo] = one_rank_barrier(lo)
+    start = c[0]
+    for d in (0, 1):
+        with torch.cuda.device(d):
+            _lib.device_status(clear=True)
+
+    devices = (ctypes.c_int * 2)(0, 1)
+    seen = {0: [], 1: []}
+    for _ in range(2):
+        for r in (0, 1):
+            with torch.cuda.device(r):
+                assert ogx_lib.ogx_peer_barrier_static(r, 2, devices, counts[r].data_ptr(),
+                                                       streams[r].cuda_stream) == 0, ogx_lib.ogx_last_error()
+        for r in (0, 1):
+            streams[r].synchronize()
+            seen[r].append(int(counts[r].item()))
+    assert seen[0] == [start + 1, start + 2]
+    assert seen[1] == seen[0]
+    for d in (0, 1):
+        with torch.cuda.device(d):
+            assert _lib.device_status(clear=True) == 0
