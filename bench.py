@@ -296,6 +296,17 @@ def run_reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def rope_input(args, cfg, inp, dev):
+    """The block's RoPE input: cos/sin generated in the RoPE kernel from the tokens' (t, h, w) positions (the
+    default: no cos/sin tables are read), or the [1, 32, L, 64] tables of the reference's interface
+    (--rope-tables).  Both hold the same angles (synthetic.rope_tables / synthetic.rope_positions)."""
+    from opengenie_b200 import synthetic
+
+    if args.rope_tables:
+        return (inp.cos, inp.sin)
+    return synthetic.rope_positions(cfg.frames, cfg.grid_h, cfg.grid_w, device=dev)
+
+
 def config_dict(name: str, n: int, exchange: str = "nvlink") -> dict:
     from opengenie_b200 import synthetic
 
@@ -306,7 +317,7 @@ def config_dict(name: str, n: int, exchange: str = "nvlink") -> dict:
         "head_dim": 128, "batch": 1, "qkv_out_proj": "e4m3 per-tensor scales, fp32 accumulate",
         "attention": "bf16, fp32 softmax/accumulate", "per_token_timestep": cfg.per_token_timestep,
         "parallelism": "single GPU" if n == 1 else f"ulysses heads {32 // n}/GPU, {exchange} exchange",
-        "l2": "inputs larger than L2 (x 75 MB + weights 67 MB + cos/sin 75 MB read per block)",
+        "l2": "inputs larger than L2 (x 75 MB + weights 67 MB read per block, qkv 226 MB written and re-read)",
     }
 
 
@@ -656,7 +667,7 @@ def run_layers(args) -> None:
     sets = [(synthetic.make_weights(seed=100 + i), synthetic.make_ffn_weights(seed=200 + i))
             for i in range(max(1, args.distinct_weights))]
     stack = VideoLayerStack([VideoLayer(*sets[i % len(sets)], dev) for i in range(args.layers)])
-    pe = (inp.cos, inp.sin)
+    pe = rope_input(args, cfg, inp, dev)
     stack.calibrate_input_scales(inp.x, inp.timestep, pe)
     out = torch.empty_like(inp.x)
 
@@ -713,6 +724,8 @@ def main() -> None:
     ap.add_argument("--branch", choices=["attention", "ffn", "text", "layers"], default="attention",
                     help="the video self-attention block (the headline), the same layer's video FFN branch or "
                          "text cross-attention branch, or a stack of layers' video branches")
+    ap.add_argument("--rope-tables", action="store_true",
+                    help="feed the RoPE kernel cos/sin tables (the reference's interface) instead of positions")
     ap.add_argument("--context-tokens", type=int, default=1024, help="--branch text: prompt context tokens")
     ap.add_argument("--layers", type=int, default=48, help="--branch layers: layers in the stack")
     ap.add_argument("--distinct-weights", type=int, default=2, help="--branch layers: random weight sets")
@@ -742,26 +755,27 @@ def main() -> None:
     inp_cpu = synthetic.make_inputs(cfg, seed=1)
     w = synthetic.make_weights(seed=0)
     inp = inp_cpu.to(dev)
+    pe = rope_input(args, cfg, inp, dev)
 
     if world == 1:
         blk = VideoSelfAttentionBlock(w, dev)
-        blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
+        blk.calibrate_input_scales(inp.x, inp.timestep, pe)
         launches_per_step = 5
         out_dev = torch.empty_like(inp.x)
 
         def step():
-            blk(inp.x, inp.timestep, (inp.cos, inp.sin), out=out_dev)
+            blk(inp.x, inp.timestep, pe, out=out_dev)
     else:
         from opengenie_b200.ulysses import UlyssesVideoSelfAttention
 
         blk = UlyssesVideoSelfAttention(w, dev, pg, exchange=args.exchange)
-        blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
+        blk.calibrate_input_scales(inp.x, inp.timestep, pe)
         launches_per_step = blk.kernel_launches_per_step
         x_loc = blk.local_slice(inp.x)
         out_dev = torch.empty_like(x_loc)
 
         def step():
-            blk.forward_local(x_loc, inp.timestep, (inp.cos, inp.sin), out=out_dev)
+            blk.forward_local(x_loc, inp.timestep, pe, out=out_dev)
 
     # the step as one CUDA graph replay (NCCL's all-to-alls stay eager)
     use_graph = not args.no_graph and (world == 1 or args.exchange == "nvlink")
@@ -803,10 +817,10 @@ def main() -> None:
     out_hosts = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
     if world == 1:
         def host_step(xd, yd):
-            blk(xd, inp.timestep, (inp.cos, inp.sin), out=yd)
+            blk(xd, inp.timestep, pe, out=yd)
     else:
         def host_step(xd, yd):
-            blk.forward_local(xd, inp.timestep, (inp.cos, inp.sin), out=yd)
+            blk.forward_local(xd, inp.timestep, pe, out=yd)
     pipe = HostPipeline(host_step, tuple(x_host.shape), x_host.dtype, dev, graphs=use_graph)
     pipe.run([x_host] * 2, out_hosts)  # warm-up
     torch.cuda.synchronize(dev)
@@ -853,6 +867,8 @@ def main() -> None:
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 attention / e4m3 projections",
             "data": "synthetic (seeded inputs, random-init weights)", "config": config_dict(args.config, world, args.exchange),
             "launch": "one CUDA graph replay per step" if use_graph else "eager launches",
+            "rope": ("cos/sin tables [1, 32, L, 64] read by the RoPE kernel" if args.rope_tables else
+                     "cos/sin generated in the RoPE kernel from the tokens' (t, h, w) positions"),
             "roofline": {
                 "bound": "tensor", "kernel": "attn_fwd_kernel (attention, dominant)",
                 "achieved": achieved, "peak": peaks.get("bf16_tflops"), "unit": "TFLOP/s",

@@ -130,6 +130,37 @@ int ogx_video_qk_rmsnorm_rope(const void* q, const void* k, int64_t tokens, int6
                               const void* cos, const void* sin, int cs_dtype, int64_t cs_stride_h,
                               int64_t cs_stride_t, void* q_out, void* k_out, int64_t out_stride_t, void* stream);
 
+/* ogx_video_qk_rmsnorm_rope with the cos/sin generated in the kernel instead of read from tables: token i
+ * (global index token0 + i) sits at (t, h, w) = (g / (grid_h*grid_w), (g / grid_w) % grid_h, g % grid_w)
+ * of the latent raster, and rotary slot s = 64*head + j turns by position[slot_axis[s]] * inv_freq[s]
+ * radians (axis 0 = t, 1 = h, 2 = w); cos and sin are rounded to bf16 before use, as the reference's bf16
+ * tables hold them.  inv_freq: float64 [2048] and slot_axis: uint8 [2048], device memory.  Saves the
+ * tables' 8 KB of HBM reads per token.  The reference builds these tables in the un-vendored ltx_core
+ * preprocessor and caches them (ltx_serve/triton_ltx_ops.py:2413-2497); the arithmetic on q/k is that of
+ * fused_video_qk_rmsnorm_rope, :320-378. */
+int ogx_video_qk_rmsnorm_rope_positions(const void* q, const void* k, int64_t tokens, int64_t in_stride_t,
+                                        const void* q_weight, const void* k_weight, int weight_dtype, float eps,
+                                        const double* inv_freq, const unsigned char* slot_axis, int64_t grid_h,
+                                        int64_t grid_w, int64_t token0, void* q_out, void* k_out,
+                                        int64_t out_stride_t, void* stream);
+
+/* ogx_video_qkv_rmsnorm_rope_scatter with the cos/sin generated from positions as in
+ * ogx_video_qk_rmsnorm_rope_positions. */
+int ogx_video_qkv_rmsnorm_rope_positions_scatter(const void* q, const void* k, const void* v, int64_t tokens,
+                                                 int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                                 int weight_dtype, float eps, const double* inv_freq,
+                                                 const unsigned char* slot_axis, int64_t grid_h, int64_t grid_w,
+                                                 int64_t token0, void* q_out, void* k_out, void* v_out,
+                                                 int64_t out_stride_t, int64_t out_stride_g, int heads_per_group,
+                                                 void* stream);
+
+/* The cos/sin ogx_video_qk_rmsnorm_rope_positions generates, written as [32, tokens, 64] tables (bf16 or
+ * f32) for tokens [token0, token0 + tokens): the tables the reference's interface takes
+ * (ltx_serve/triton_ltx_ops.py:2413-2497 caches them), bit-equal to the generated values. */
+int ogx_rope_tables_from_positions(const double* inv_freq, const unsigned char* slot_axis, int64_t grid_h,
+                                   int64_t grid_w, int64_t token0, int64_t tokens, int cs_dtype, void* cos_out,
+                                   void* sin_out, void* stream);
+
 /* The same normalisation + RoPE, writing Q/K and copying V into the
  * head-grouped send layout of the sequence-to-head exchange: head h of token t
  * goes to out + t*out_stride_t + (h / heads_per_group)*out_stride_g +
@@ -286,6 +317,15 @@ int ogx_video_qkv_rmsnorm_rope_to_peers(const void* q, const void* k, const void
                                         int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
                                         int64_t cs_stride_h, int64_t cs_stride_t, void* const* group_bases,
                                         int groups, int64_t out_stride_t, void* stream);
+
+/* ogx_video_qkv_rmsnorm_rope_to_peers with the cos/sin generated from positions as in
+ * ogx_video_qk_rmsnorm_rope_positions (token0 = the first token of this rank's slice). */
+int ogx_video_qkv_rmsnorm_rope_positions_to_peers(const void* q, const void* k, const void* v, int64_t tokens,
+                                                  int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                                  int weight_dtype, float eps, const double* inv_freq,
+                                                  const unsigned char* slot_axis, int64_t grid_h, int64_t grid_w,
+                                                  int64_t token0, void* const* group_bases, int groups,
+                                                  int64_t out_stride_t, void* stream);
 
 /* ogx_attention_fwd_e4m3 (batch 1) whose output row for token t goes to
  * peer_bases[t / tokens_per_peer] + (t % tokens_per_peer)*out_stride_t + head*128 (the receive buffers

@@ -52,6 +52,17 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p, c_void_p,
         c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
     ],
+    "ogx_video_qk_rmsnorm_rope_positions": [
+        c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p, c_void_p,
+        c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
+    ],
+    "ogx_video_qkv_rmsnorm_rope_positions_scatter": [
+        c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p,
+        c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p,
+    ],
+    "ogx_rope_tables_from_positions": [
+        c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+    ],
     "ogx_video_qkv_rmsnorm_rope_scatter": [
         c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p,
         c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p,
@@ -103,6 +114,10 @@ _SIGNATURES: dict[str, list] = {
     "ogx_video_qkv_rmsnorm_rope_to_peers": [
         c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p,
         c_void_p, c_int, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p,
+    ],
+    "ogx_video_qkv_rmsnorm_rope_positions_to_peers": [
+        c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_float, c_void_p,
+        c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p,
     ],
     "ogx_attention_fwd_e4m3_to_peers": [
         c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_int, c_int64,

@@ -1,8 +1,8 @@
-// HBM-bound stages of the video self-attention block: AdaZero-from-table
-// (optionally fused with the E4M3 activation quantiser), the standalone E4M3
-// quantiser, the bf16 bias add, the bias + Ada-gated residual, and the fused
-// Q/K RMSNorm + split RoPE (which also scatters Q/K/V into a head-grouped
-// layout for the sequence-to-head exchange).
+// HBM-bound stages of the video self-attention block and the numerics they share:
+// the E4M3 quantiser, the standalone quantiser and GELU + quantiser kernels, the
+// bf16 bias add, the bias + Ada-gated residual, the Ada affine / multiply, the
+// per-head gate and the Q/K RMSNorm without RoPE; the argument blocks of the
+// row-pipeline AdaZero and Q/K RMSNorm + RoPE kernels (rows.cuh).
 //
 // All of them move 16-byte vectors (8 x bf16) per lane so every warp access is
 // a fully used 512-byte span, keep fp32 arithmetic and round to bf16 exactly
@@ -166,14 +166,9 @@ __device__ __forceinline__ uint2 quant8<__nv_bfloat16, kQuantTorch>(const float 
   return make_uint2(w[0], w[1]);
 }
 
-// ----------------------------------------------------------------- AdaZero
-// y = rmsnorm(x) * (1 + scale) + shift in fp32 with one bf16 rounding
-// (the reference's GPU kernel, triton_ltx_ops.py:3359-3427), with
-// shift/scale read from scale_shift_table + timestep.  One 128-thread CTA per
-// row (COLS / 1024 16-byte vectors per thread, the row stays in registers
-// between the reduction and the normalisation).  With QUANT the bf16 result
-// is also (or only) quantised to e4m3, so the codes are bit-equal to
-// quantising the bf16 output separately.
+// ----------------------------------------------------------------- AdaZero arguments
+// y = rmsnorm(x) * (1 + scale) + shift with shift/scale read from scale_shift_table + timestep (the
+// row-pipeline kernel in rows.cuh; the Ada elementwise kernels below take the same arguments).
 struct AdaArgs {
   const __nv_bfloat16* x;
   const void* table;
@@ -182,7 +177,6 @@ struct AdaArgs {
   int64_t table_stride_row;                       // elements; innermost stride is 1
   int64_t rows, tokens;
   int shift_index, scale_index;
-  int rows_per_cta;  // AdaZero: rows each CTA normalises (at most kAdaRowsPerCta)
   float eps;
   const float* input_scale;  // device scalar (QUANT only)
   __nv_bfloat16* y;          // may be null when only q is wanted
@@ -198,104 +192,6 @@ __device__ __forceinline__ float row_sum(float v, float* red) {
   if ((threadIdx.x & 31) == 0) red[w] = v;
   __syncthreads();
   return red[0] + red[1] + red[2] + red[3];
-}
-
-constexpr int kAdaRowsPerCta = 8;
-
-// One 128-thread CTA per a.rows_per_cta (<= kAdaRowsPerCta) rows: the host spreads short inputs (a GPU's
-// slice of the sequence) over more CTAs.  With a token-uniform timestep
-// (stride 0 over tokens, the uniform-timestep layout) shift/scale are the same
-// for every row, so each thread computes them for its columns once and keeps
-// them in registers; otherwise they are read per row.  The next row's x is
-// loaded before the current row's reduction completes.
-template <int COLS, typename TableT, typename TsT, bool QUANT, int QMODE, bool UNIFORM>
-__global__ void __launch_bounds__(kRowThreads) adazero_from_ada_kernel(AdaArgs a) {
-  pdl_trigger();
-  pdl_wait();
-  constexpr int VPT = COLS / 8 / kRowThreads;  // 16-byte vectors per thread
-  __shared__ float red[2][4];
-  const int tid = threadIdx.x;
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta;
-  const int64_t row_end = (row0 + a.rows_per_cta < a.rows) ? row0 + a.rows_per_cta : a.rows;
-
-  const TableT* table = static_cast<const TableT*>(a.table);
-  const TableT* tshift = table + a.shift_index * a.table_stride_row;
-  const TableT* tscale = table + a.scale_index * a.table_stride_row;
-  float s = 0.f, r = 0.f;
-  if (QUANT) {
-    s = __ldg(a.input_scale);
-    r = __frcp_rn(s);
-  }
-
-  float ushift[UNIFORM ? VPT : 1][8], uscale[UNIFORM ? VPT : 1][8];
-  if (UNIFORM) {
-    const TsT* ts = static_cast<const TsT*>(a.ts);
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int col = (j * kRowThreads + tid) * 8;
-      ada_values8<TableT, TsT>(tshift + col, ts + a.shift_index * a.ts_stride_p + col, ushift[j % (UNIFORM ? VPT : 1)]);
-      ada_values8<TableT, TsT>(tscale + col, ts + a.scale_index * a.ts_stride_p + col, uscale[j % (UNIFORM ? VPT : 1)]);
-    }
-  }
-
-  uint4 xn[VPT];
-  if (row0 < row_end) {
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) xn[j] = __ldg(reinterpret_cast<const uint4*>(a.x + row0 * COLS) + j * kRowThreads + tid);
-  }
-  for (int64_t row = row0; row < row_end; ++row) {
-    uint4 xv[VPT];
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) xv[j] = xn[j];
-    if (row + 1 < row_end) {
-#pragma unroll
-      for (int j = 0; j < VPT; ++j)
-        xn[j] = __ldg(reinterpret_cast<const uint4*>(a.x + (row + 1) * COLS) + j * kRowThreads + tid);
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      float f[8];
-      unpack8(xv[j], f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
-    }
-    ss = warp_sum(ss);
-    float* rb = red[row & 1];
-    if ((tid & 31) == 0) rb[tid >> 5] = ss;
-    __syncthreads();
-    ss = rb[0] + rb[1] + rb[2] + rb[3];
-    const float inv_rms = rsqrtf(ss / static_cast<float>(COLS) + a.eps);
-
-    const int64_t b = row / a.tokens;
-    const int64_t t = row - b * a.tokens;
-    const TsT* ts = static_cast<const TsT*>(a.ts) + b * a.ts_stride_b + t * a.ts_stride_t;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int vec = j * kRowThreads + tid;
-      const int col = vec * 8;
-      float f[8], y[8];
-      unpack8(xv[j], f);
-      if (UNIFORM) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = fmaf(f[i] * inv_rms, 1.0f + uscale[j % (UNIFORM ? VPT : 1)][i],
-                                                ushift[j % (UNIFORM ? VPT : 1)][i]);
-      } else {
-        float shift[8], scale[8];
-        ada_values8<TableT, TsT>(tshift + col, ts + a.shift_index * a.ts_stride_p + col, shift);
-        ada_values8<TableT, TsT>(tscale + col, ts + a.scale_index * a.ts_stride_p + col, scale);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = fmaf(f[i] * inv_rms, 1.0f + scale[i], shift[i]);
-      }
-      const uint4 yv = pack8(y);
-      if (a.y != nullptr) reinterpret_cast<uint4*>(a.y + row * COLS)[vec] = yv;
-      if (QUANT) {
-        float yb[8];
-        unpack8(yv, yb);
-        reinterpret_cast<uint2*>(a.q + row * COLS)[vec] = quant8<__nv_bfloat16, QMODE>(yb, s, r);
-      }
-    }
-  }
 }
 
 // ----------------------------------------------------------------- per-head gate
@@ -535,14 +431,13 @@ __global__ void __launch_bounds__(256) residual_gate_bias_kernel(ResidualArgs a)
   }
 }
 
-// ----------------------------------------------------------------- Q/K RMSNorm + split RoPE
+// ----------------------------------------------------------------- Q/K RMSNorm + split RoPE arguments
 // Per token: q_hat = q * rsqrt(mean(q^2) + eps) * w_q over all 4096 columns,
 // then per head h and half index j < 64:
 //   o[j]    = q_hat[j] * cos[h,t,j] - q_hat[j+64] * sin[h,t,j]
 //   o[j+64] = q_hat[j+64] * cos[h,t,j] + q_hat[j] * sin[h,t,j]
-// in fp32 with one bf16 rounding (triton_ltx_ops.py:3901-3978).  Same for k.
-// One warp per token.  Lane l holds vectors v = 32*j + l (8 columns each); the
-// partner half of the same head sits in lane l ^ 8, reached with a shuffle.
+// in fp32 with one bf16 rounding (triton_ltx_ops.py:3901-3978).  Same for k.  The kernel is the
+// row-pipeline qk_rmsnorm_rope_ring_kernel (rows.cuh).
 //
 // Outputs are addressed per (token, head) through a table of group bases:
 // dst[j][h / heads_per_group] + t*out_stride_t + (h % heads_per_group)*128 + d,
@@ -578,85 +473,6 @@ __device__ __forceinline__ __nv_bfloat16* group_base(__nv_bfloat16* const (&base
 #pragma unroll
   for (int i = 1; i < 8; ++i) b = (g == i) ? bases[i] : b;
   return b;
-}
-
-template <typename WT, typename CsT>
-__device__ __forceinline__ void rmsnorm_rope_row(const __nv_bfloat16* in, const WT* w, const CsT* cosb,
-                                                 const CsT* sinb, const RopeArgs& a, int64_t t, float* red, int j_out) {
-  constexpr int VPT = 4096 / 8 / kRowThreads;  // 4
-  const int tid = threadIdx.x;
-  uint4 xv[VPT];
-  float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    xv[j] = __ldg(reinterpret_cast<const uint4*>(in) + j * kRowThreads + tid);
-    float f[8];
-    unpack8(xv[j], f);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
-  }
-  ss = row_sum(ss, red);
-  const float inv_rms = rsqrtf(ss / 4096.f + a.eps);
-  // vector v holds columns [8v, 8v+8): head v/16, its partner half is v ^ 8,
-  // which lives in lane (tid ^ 8) of the same warp.
-  const bool second = (tid & 8) != 0;
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int vec = j * kRowThreads + tid;
-    const int col = vec * 8;
-    const int head = col >> 7;
-    const int half_off = col & 63;  // index into the 64 cos/sin values
-    float f[8], wv[8], n[8], other[8], c[8], s[8], o[8];
-    unpack8(xv[j], f);
-    load8<WT>(w + col, wv);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) n[i] = f[i] * inv_rms * wv[i];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) other[i] = __shfl_xor_sync(0xffffffffu, n[i], 8);
-    load8<CsT>(cosb + head * a.cs_stride_h + t * a.cs_stride_t + half_off, c);
-    load8<CsT>(sinb + head * a.cs_stride_h + t * a.cs_stride_t + half_off, s);
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      o[i] = second ? fmaf(n[i], c[i], other[i] * s[i]) : fmaf(n[i], c[i], -(other[i] * s[i]));
-    const int g = head / a.heads_per_group;
-    const int hl = head - g * a.heads_per_group;
-    __nv_bfloat16* dst = group_base(a.dst[j_out], g) + t * a.out_stride_t + hl * 128 + (col & 127);
-    *reinterpret_cast<uint4*>(dst) = pack8(o);
-  }
-}
-
-// One 128-thread CTA per token.  Register budget for 8 CTAs (1024 threads) per SM: more tokens in
-// flight beat fewer, spill-free ones (79.6 vs 84.5 us at L=9216; batching both rows' loads ahead of one
-// barrier at 163 registers: 106 us).
-template <typename WT, typename CsT>
-__global__ void __launch_bounds__(kRowThreads, 8) qk_rmsnorm_rope_kernel(RopeArgs a) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ float red[2][4];
-  const int64_t t = blockIdx.x;
-  const CsT* cosb = static_cast<const CsT*>(a.cos);
-  const CsT* sinb = static_cast<const CsT*>(a.sin);
-  rmsnorm_rope_row<WT, CsT>(a.q + t * a.in_stride_t, static_cast<const WT*>(a.q_weight), cosb, sinb, a, t, red[0], 0);
-  rmsnorm_rope_row<WT, CsT>(a.k + t * a.in_stride_t, static_cast<const WT*>(a.k_weight), cosb, sinb, a, t, red[1], 1);
-  if (a.copy_v) {
-    const __nv_bfloat16* vin = a.v + t * a.in_stride_t;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int vec = j * kRowThreads + threadIdx.x;
-      const int col = vec * 8;
-      const int head = col >> 7;
-      const int g = head / a.heads_per_group;
-      const int hl = head - g * a.heads_per_group;
-      const uint4 val = __ldg(reinterpret_cast<const uint4*>(vin) + vec);
-      *reinterpret_cast<uint4*>(group_base(a.dst[2], g) + t * a.out_stride_t + hl * 128 + (col & 127)) = val;
-    }
-  }
-  if (a.system_fence) {
-    // one system-scope fence per CTA, after the barrier: fences are cumulative, so it orders every
-    // thread's peer stores before the signal the next kernel releases
-    __syncthreads();
-    if (threadIdx.x == 0) __threadfence_system();
-  }
 }
 
 // Q/K RMSNorm without rotary embedding (attention whose keys come from another sequence): rows

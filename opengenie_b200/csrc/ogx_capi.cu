@@ -20,6 +20,7 @@
 #include "../../include/ogx.h"
 #include "elementwise.cuh"
 #include "attention.cuh"
+#include "rows.cuh"
 #include "fp8_gemm.cuh"
 #include "peer.cuh"
 
@@ -155,40 +156,38 @@ int ensure_smem(K kernel, int bytes) {
 bool dtype_ok(int dt) { return dt == OGX_DTYPE_BF16 || dt == OGX_DTYPE_F32; }
 
 // ------------------------------------------------------------- AdaZero
+// One persistent row-pipeline CTA per SM (csrc/rows.cuh), at most one per row.
+template <int COLS, typename TableT, typename TsT, bool QUANT, int QMODE, bool UNIFORM>
+int launch_ada_ring(const ogx::AdaArgs& a, cudaStream_t s) {
+  auto kern = ogx::rows::adazero_ring_kernel<COLS, TableT, TsT, QUANT, QMODE, UNIFORM>;
+  const int smem = ogx::rows::AdaLayout<COLS, TsT>::smem_bytes(UNIFORM) + 128;
+  int rc = ensure_smem(kern, smem);
+  if (rc) return rc;
+  const int64_t sms = sm_count();
+  const dim3 grid(static_cast<unsigned>(a.rows < sms ? a.rows : sms));
+  launch(kern, grid, ogx::rows::kThreads, static_cast<size_t>(smem), s, a);
+  return OGX_OK;
+}
+
 template <int COLS, typename TableT, typename TsT, bool UNIFORM>
-void launch_ada_u(ogx::AdaArgs a, bool quant, int qmode, cudaStream_t s) {
-  // at least 4 CTAs per SM: up to kAdaRowsPerCta rows each (the Ada values a CTA loads serve all its
-  // rows), fewer for short inputs so that they still fill the GPU (1152 rows: 7.7 us against 10.1 us
-  // with 8 rows per CTA; 4608 rows and more keep 8 rows per CTA)
-  const int64_t target = 4 * static_cast<int64_t>(sm_count());
-  const int64_t per = (a.rows + target - 1) / target;
-  a.rows_per_cta = static_cast<int>(per < 1 ? 1 : (per > ogx::kAdaRowsPerCta ? ogx::kAdaRowsPerCta : per));
-  const dim3 grid(static_cast<unsigned>((a.rows + a.rows_per_cta - 1) / a.rows_per_cta));
-  const int threads = ogx::kRowThreads;
-  if (!quant)
-    launch(ogx::adazero_from_ada_kernel<COLS, TableT, TsT, false, 0, UNIFORM>, grid, threads, 0, s, a);
-  else if (qmode == OGX_QUANT_TORCH)
-    launch(ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantTorch, UNIFORM>, grid, threads, 0, s, a);
-  else
-    launch(ogx::adazero_from_ada_kernel<COLS, TableT, TsT, true, ogx::kQuantSingle, UNIFORM>, grid, threads, 0, s, a);
+int launch_ada_u(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) {
+  if (!quant) return launch_ada_ring<COLS, TableT, TsT, false, 0, UNIFORM>(a, s);
+  if (qmode == OGX_QUANT_TORCH) return launch_ada_ring<COLS, TableT, TsT, true, ogx::kQuantTorch, UNIFORM>(a, s);
+  return launch_ada_ring<COLS, TableT, TsT, true, ogx::kQuantSingle, UNIFORM>(a, s);
 }
 
 template <int COLS, typename TableT, typename TsT>
-void launch_ada_cols(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) {
+int launch_ada_cols(const ogx::AdaArgs& a, bool quant, int qmode, cudaStream_t s) {
   // token-uniform timestep: every row of every batch reads the same Ada slots
   const bool uniform = a.ts_stride_t == 0 && (a.ts_stride_b == 0 || a.rows <= a.tokens);
-  if (uniform)
-    launch_ada_u<COLS, TableT, TsT, true>(a, quant, qmode, s);
-  else
-    launch_ada_u<COLS, TableT, TsT, false>(a, quant, qmode, s);
+  if (uniform) return launch_ada_u<COLS, TableT, TsT, true>(a, quant, qmode, s);
+  return launch_ada_u<COLS, TableT, TsT, false>(a, quant, qmode, s);
 }
 
 template <typename TableT, typename TsT>
-void launch_ada_t(const ogx::AdaArgs& a, int64_t cols, bool quant, int qmode, cudaStream_t s) {
-  if (cols == 4096)
-    launch_ada_cols<4096, TableT, TsT>(a, quant, qmode, s);
-  else
-    launch_ada_cols<2048, TableT, TsT>(a, quant, qmode, s);
+int launch_ada_t(const ogx::AdaArgs& a, int64_t cols, bool quant, int qmode, cudaStream_t s) {
+  if (cols == 4096) return launch_ada_cols<4096, TableT, TsT>(a, quant, qmode, s);
+  return launch_ada_cols<2048, TableT, TsT>(a, quant, qmode, s);
 }
 
 int ada_guard(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table, int table_dtype,
@@ -210,15 +209,69 @@ int ada_guard(const void* x, int64_t batch, int64_t tokens, int64_t cols, const 
 int ada_dispatch(const ogx::AdaArgs& a, int64_t cols, int table_dtype, int ts_dtype, bool quant, int qmode,
                  cudaStream_t s) {
   if (a.rows == 0) return OGX_OK;
+  int rc;
   if (table_dtype == OGX_DTYPE_F32 && ts_dtype == OGX_DTYPE_BF16)
-    launch_ada_t<float, __nv_bfloat16>(a, cols, quant, qmode, s);
+    rc = launch_ada_t<float, __nv_bfloat16>(a, cols, quant, qmode, s);
   else if (table_dtype == OGX_DTYPE_BF16 && ts_dtype == OGX_DTYPE_BF16)
-    launch_ada_t<__nv_bfloat16, __nv_bfloat16>(a, cols, quant, qmode, s);
+    rc = launch_ada_t<__nv_bfloat16, __nv_bfloat16>(a, cols, quant, qmode, s);
   else if (table_dtype == OGX_DTYPE_F32 && ts_dtype == OGX_DTYPE_F32)
-    launch_ada_t<float, float>(a, cols, quant, qmode, s);
+    rc = launch_ada_t<float, float>(a, cols, quant, qmode, s);
   else
-    launch_ada_t<__nv_bfloat16, float>(a, cols, quant, qmode, s);
-  return check_launch("adazero_from_ada_kernel");
+    rc = launch_ada_t<__nv_bfloat16, float>(a, cols, quant, qmode, s);
+  if (rc) return rc;
+  return check_launch("adazero_ring_kernel");
+}
+
+// ------------------------------------------------------------- Q/K RMSNorm + RoPE
+// One persistent row-pipeline CTA per SM (csrc/rows.cuh), at most one per token; cos/sin from tables
+// (src == nullptr) or generated from the tokens' positions.
+template <typename WT, typename CsT, bool GEN, bool COPY_V>
+int launch_rope_ring(const ogx::RopeArgs& a, const ogx::rows::RopeSource& src, cudaStream_t s) {
+  auto kern = ogx::rows::qk_rmsnorm_rope_ring_kernel<WT, CsT, GEN, COPY_V>;
+  const int smem = ogx::rows::RopeLayout<WT>::smem_bytes(COPY_V) + 128;
+  int rc = ensure_smem(kern, smem);
+  if (rc) return rc;
+  const int64_t sms = sm_count();
+  const dim3 grid(static_cast<unsigned>(a.tokens < sms ? a.tokens : sms));
+  launch(kern, grid, ogx::rows::kThreads, static_cast<size_t>(smem), s, a, src);
+  return OGX_OK;
+}
+
+template <typename WT>
+int rope_dispatch_w(const ogx::RopeArgs& a, const ogx::rows::RopeSource* src, int cs_dtype, cudaStream_t s) {
+  const ogx::rows::RopeSource none{};
+  if (src != nullptr)
+    return a.copy_v ? launch_rope_ring<WT, __nv_bfloat16, true, true>(a, *src, s)
+                    : launch_rope_ring<WT, __nv_bfloat16, true, false>(a, *src, s);
+  if (cs_dtype == OGX_DTYPE_F32)
+    return a.copy_v ? launch_rope_ring<WT, float, false, true>(a, none, s)
+                    : launch_rope_ring<WT, float, false, false>(a, none, s);
+  return a.copy_v ? launch_rope_ring<WT, __nv_bfloat16, false, true>(a, none, s)
+                  : launch_rope_ring<WT, __nv_bfloat16, false, false>(a, none, s);
+}
+
+int rope_dispatch(const ogx::RopeArgs& a, const ogx::rows::RopeSource* src, int weight_dtype, int cs_dtype,
+                  cudaStream_t s) {
+  const int rc = weight_dtype == OGX_DTYPE_F32 ? rope_dispatch_w<float>(a, src, cs_dtype, s)
+                                               : rope_dispatch_w<__nv_bfloat16>(a, src, cs_dtype, s);
+  if (rc) return rc;
+  return check_launch("qk_rmsnorm_rope_ring_kernel");
+}
+
+// Checks of the generated-cos/sin arguments: the 2048-slot frequency and axis tables (device memory) and
+// the latent grid that maps a token index to its (t, h, w) position.
+int rope_source(const void* inv_freq, const void* slot_axis, int64_t grid_h, int64_t grid_w, int64_t token0,
+                ogx::rows::RopeSource* src) {
+  if (inv_freq == nullptr || slot_axis == nullptr) return fail(OGX_EINVAL, "rope_shape: null frequency table");
+  if (reinterpret_cast<uintptr_t>(inv_freq) & 7u) return fail(OGX_EINVAL, "alignment");
+  if (grid_h < 1 || grid_w < 1 || grid_h > INT32_MAX || grid_w > INT32_MAX || token0 < 0)
+    return fail(OGX_EINVAL, "rope_shape: grid");
+  src->inv_freq = static_cast<const double*>(inv_freq);
+  src->slot_axis = static_cast<const uint8_t*>(slot_axis);
+  src->grid_h = static_cast<int>(grid_h);
+  src->grid_w = static_cast<int>(grid_w);
+  src->token0 = token0;
+  return OGX_OK;
 }
 
 int grid_for(int64_t nvec) {
@@ -489,24 +542,30 @@ int ogx_residual_gate_bias_from_ada(const void* x, const void* y, int64_t batch,
   return check_launch("residual_gate_bias_kernel");
 }
 
-int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void* v, int64_t tokens,
-                                       int64_t in_stride_t, const void* q_weight, const void* k_weight,
-                                       int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
-                                       int64_t cs_stride_h, int64_t cs_stride_t, void* q_out, void* k_out,
-                                       void* v_out, int64_t out_stride_t, int64_t out_stride_g,
-                                       int heads_per_group, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Q/K RMSNorm + RoPE into [tokens][..] rows per head group; cos/sin from the tables, or generated (src).
+int rope_scatter_impl(const void* q, const void* k, const void* v, int64_t tokens, int64_t in_stride_t,
+                      const void* q_weight, const void* k_weight, int weight_dtype, float eps, const void* cos,
+                      const void* sin, int cs_dtype, int64_t cs_stride_h, int64_t cs_stride_t,
+                      const ogx::rows::RopeSource* src, void* q_out, void* k_out, void* v_out, int64_t out_stride_t,
+                      int64_t out_stride_g, int heads_per_group, void* stream) {
   if (q == nullptr || k == nullptr || q_out == nullptr || k_out == nullptr) return fail(OGX_EINVAL, "null_pointer");
   if (q_weight == nullptr || k_weight == nullptr) return fail(OGX_EINVAL, "qk_weight_shape");
-  if (cos == nullptr || sin == nullptr) return fail(OGX_EINVAL, "rope_shape");
+  if (src == nullptr && (cos == nullptr || sin == nullptr)) return fail(OGX_EINVAL, "rope_shape");
   if (tokens < 1) return fail(OGX_EINVAL, "empty_tokens");
-  if (!dtype_ok(weight_dtype) || !dtype_ok(cs_dtype)) return fail(OGX_EINVAL, "qk_device_or_dtype");
+  if (!dtype_ok(weight_dtype) || (src == nullptr && !dtype_ok(cs_dtype))) return fail(OGX_EINVAL, "qk_device_or_dtype");
   if (heads_per_group < 4 || 32 % heads_per_group) return fail(OGX_EINVAL, "heads_per_group");
   if (in_stride_t % 8 || out_stride_t % 8 || out_stride_g % 8) return fail(OGX_EINVAL, "qk_noncontiguous");
-  const int cesz = cs_dtype == OGX_DTYPE_F32 ? 4 : 2;
-  if ((cs_stride_h * cesz) % 16 || (cs_stride_t * cesz) % 16) return fail(OGX_EINVAL, "rope_shape");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(cos) ||
-      !aligned16(sin) || !aligned16(q_weight) || !aligned16(k_weight) || (v && !aligned16(v)) ||
-      (v_out && !aligned16(v_out)))
+  if (src == nullptr) {
+    const int cesz = cs_dtype == OGX_DTYPE_F32 ? 4 : 2;
+    if ((cs_stride_h * cesz) % 16 || (cs_stride_t * cesz) % 16) return fail(OGX_EINVAL, "rope_shape");
+    if (!aligned16(cos) || !aligned16(sin)) return fail(OGX_EINVAL, "alignment");
+  }
+  if (!aligned16(q) || !aligned16(k) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(q_weight) ||
+      !aligned16(k_weight) || (v && !aligned16(v)) || (v_out && !aligned16(v_out)))
     return fail(OGX_EINVAL, "alignment");
   ogx::RopeArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -530,19 +589,70 @@ int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void*
   a.heads_per_group = heads_per_group;
   a.copy_v = (v != nullptr && v_out != nullptr) ? 1 : 0;
   a.system_fence = 0;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 grid(static_cast<unsigned>(tokens));
-  const int threads = ogx::kRowThreads;
-  const bool wf = weight_dtype == OGX_DTYPE_F32;
-  const bool cf = cs_dtype == OGX_DTYPE_F32;
-  if (wf) {
-    if (cf) launch(ogx::qk_rmsnorm_rope_kernel<float, float>, grid, threads, 0, s, a);
-    else launch(ogx::qk_rmsnorm_rope_kernel<float, __nv_bfloat16>, grid, threads, 0, s, a);
-  } else {
-    if (cf) launch(ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, float>, grid, threads, 0, s, a);
-    else launch(ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, __nv_bfloat16>, grid, threads, 0, s, a);
-  }
-  return check_launch("qk_rmsnorm_rope_kernel");
+  return rope_dispatch(a, src, weight_dtype, cs_dtype, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+int ogx_video_qkv_rmsnorm_rope_scatter(const void* q, const void* k, const void* v, int64_t tokens,
+                                       int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                       int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
+                                       int64_t cs_stride_h, int64_t cs_stride_t, void* q_out, void* k_out,
+                                       void* v_out, int64_t out_stride_t, int64_t out_stride_g,
+                                       int heads_per_group, void* stream) {
+  return rope_scatter_impl(q, k, v, tokens, in_stride_t, q_weight, k_weight, weight_dtype, eps, cos, sin, cs_dtype,
+                           cs_stride_h, cs_stride_t, nullptr, q_out, k_out, v_out, out_stride_t, out_stride_g,
+                           heads_per_group, stream);
+}
+
+int ogx_video_qk_rmsnorm_rope_positions(const void* q, const void* k, int64_t tokens, int64_t in_stride_t,
+                                        const void* q_weight, const void* k_weight, int weight_dtype, float eps,
+                                        const double* inv_freq, const unsigned char* slot_axis, int64_t grid_h,
+                                        int64_t grid_w, int64_t token0, void* q_out, void* k_out,
+                                        int64_t out_stride_t, void* stream) {
+  ogx::rows::RopeSource src{};
+  const int rc = rope_source(inv_freq, slot_axis, grid_h, grid_w, token0, &src);
+  if (rc) return rc;
+  return rope_scatter_impl(q, k, nullptr, tokens, in_stride_t, q_weight, k_weight, weight_dtype, eps, nullptr,
+                           nullptr, OGX_DTYPE_BF16, 0, 0, &src, q_out, k_out, nullptr, out_stride_t, 0, 32, stream);
+}
+
+int ogx_video_qkv_rmsnorm_rope_positions_scatter(const void* q, const void* k, const void* v, int64_t tokens,
+                                                 int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                                 int weight_dtype, float eps, const double* inv_freq,
+                                                 const unsigned char* slot_axis, int64_t grid_h, int64_t grid_w,
+                                                 int64_t token0, void* q_out, void* k_out, void* v_out,
+                                                 int64_t out_stride_t, int64_t out_stride_g, int heads_per_group,
+                                                 void* stream) {
+  ogx::rows::RopeSource src{};
+  const int rc = rope_source(inv_freq, slot_axis, grid_h, grid_w, token0, &src);
+  if (rc) return rc;
+  return rope_scatter_impl(q, k, v, tokens, in_stride_t, q_weight, k_weight, weight_dtype, eps, nullptr, nullptr,
+                           OGX_DTYPE_BF16, 0, 0, &src, q_out, k_out, v_out, out_stride_t, out_stride_g,
+                           heads_per_group, stream);
+}
+
+int ogx_rope_tables_from_positions(const double* inv_freq, const unsigned char* slot_axis, int64_t grid_h,
+                                   int64_t grid_w, int64_t token0, int64_t tokens, int cs_dtype, void* cos_out,
+                                   void* sin_out, void* stream) {
+  ogx::rows::RopeSource src{};
+  int rc = rope_source(inv_freq, slot_axis, grid_h, grid_w, token0, &src);
+  if (rc) return rc;
+  if (tokens < 1) return fail(OGX_EINVAL, "empty_tokens");
+  if (!dtype_ok(cs_dtype)) return fail(OGX_EINVAL, "qk_device_or_dtype");
+  if (cos_out == nullptr || sin_out == nullptr || !aligned16(cos_out) || !aligned16(sin_out))
+    return fail(OGX_EINVAL, "output");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(32 * tokens * 8);
+  if (cs_dtype == OGX_DTYPE_F32)
+    ogx::rows::rope_tables_kernel<float><<<grid, 256, 0, s>>>(src, tokens, static_cast<float*>(cos_out),
+                                                              static_cast<float*>(sin_out));
+  else
+    ogx::rows::rope_tables_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        src, tokens, static_cast<__nv_bfloat16*>(cos_out), static_cast<__nv_bfloat16*>(sin_out));
+  return check_launch("rope_tables_kernel");
 }
 
 int ogx_video_qk_rmsnorm_rope(const void* q, const void* k, int64_t tokens, int64_t in_stride_t,
@@ -990,21 +1100,30 @@ int ogx_peer_barrier(unsigned int* local_signals, void* const* peer_signals, int
   return check_launch("peer_barrier_kernel");
 }
 
-int ogx_video_qkv_rmsnorm_rope_to_peers(const void* q, const void* k, const void* v, int64_t tokens,
-                                        int64_t in_stride_t, const void* q_weight, const void* k_weight,
-                                        int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
-                                        int64_t cs_stride_h, int64_t cs_stride_t, void* const* group_bases,
-                                        int groups, int64_t out_stride_t, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int rope_to_peers_impl(const void* q, const void* k, const void* v, int64_t tokens, int64_t in_stride_t,
+                       const void* q_weight, const void* k_weight, int weight_dtype, float eps, const void* cos,
+                       const void* sin, int cs_dtype, int64_t cs_stride_h, int64_t cs_stride_t,
+                       const ogx::rows::RopeSource* src, void* const* group_bases, int groups, int64_t out_stride_t,
+                       void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || group_bases == nullptr) return fail(OGX_EINVAL, "null_pointer");
   if (groups < 1 || groups > 8 || 32 % groups) return fail(OGX_EINVAL, "groups");
   const int hpg = 32 / groups;
   if (q_weight == nullptr || k_weight == nullptr) return fail(OGX_EINVAL, "qk_weight_shape");
-  if (cos == nullptr || sin == nullptr) return fail(OGX_EINVAL, "rope_shape");
+  if (src == nullptr && (cos == nullptr || sin == nullptr)) return fail(OGX_EINVAL, "rope_shape");
   if (tokens < 1) return fail(OGX_EINVAL, "empty_tokens");
-  if (!dtype_ok(weight_dtype) || !dtype_ok(cs_dtype)) return fail(OGX_EINVAL, "qk_device_or_dtype");
+  if (!dtype_ok(weight_dtype) || (src == nullptr && !dtype_ok(cs_dtype))) return fail(OGX_EINVAL, "qk_device_or_dtype");
   if (in_stride_t % 8 || out_stride_t % 8 || out_stride_t < 3 * hpg * 128) return fail(OGX_EINVAL, "qk_noncontiguous");
-  const int cesz = cs_dtype == OGX_DTYPE_F32 ? 4 : 2;
-  if ((cs_stride_h * cesz) % 16 || (cs_stride_t * cesz) % 16) return fail(OGX_EINVAL, "rope_shape");
+  if (src == nullptr) {
+    const int cesz = cs_dtype == OGX_DTYPE_F32 ? 4 : 2;
+    if ((cs_stride_h * cesz) % 16 || (cs_stride_t * cesz) % 16) return fail(OGX_EINVAL, "rope_shape");
+    if (!aligned16(cos) || !aligned16(sin)) return fail(OGX_EINVAL, "alignment");
+  }
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(q_weight) || !aligned16(k_weight))
+    return fail(OGX_EINVAL, "alignment");
   ogx::RopeArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k = static_cast<const __nv_bfloat16*>(k);
@@ -1029,19 +1148,33 @@ int ogx_video_qkv_rmsnorm_rope_to_peers(const void* q, const void* k, const void
   a.heads_per_group = hpg;
   a.copy_v = 1;
   a.system_fence = 1;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 grid(static_cast<unsigned>(tokens));
-  const int threads = ogx::kRowThreads;
-  const bool wf = weight_dtype == OGX_DTYPE_F32;
-  const bool cf = cs_dtype == OGX_DTYPE_F32;
-  if (wf) {
-    if (cf) launch(ogx::qk_rmsnorm_rope_kernel<float, float>, grid, threads, 0, s, a);
-    else launch(ogx::qk_rmsnorm_rope_kernel<float, __nv_bfloat16>, grid, threads, 0, s, a);
-  } else {
-    if (cf) launch(ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, float>, grid, threads, 0, s, a);
-    else launch(ogx::qk_rmsnorm_rope_kernel<__nv_bfloat16, __nv_bfloat16>, grid, threads, 0, s, a);
-  }
-  return check_launch("qk_rmsnorm_rope_kernel");
+  return rope_dispatch(a, src, weight_dtype, cs_dtype, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+int ogx_video_qkv_rmsnorm_rope_to_peers(const void* q, const void* k, const void* v, int64_t tokens,
+                                        int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                        int weight_dtype, float eps, const void* cos, const void* sin, int cs_dtype,
+                                        int64_t cs_stride_h, int64_t cs_stride_t, void* const* group_bases,
+                                        int groups, int64_t out_stride_t, void* stream) {
+  return rope_to_peers_impl(q, k, v, tokens, in_stride_t, q_weight, k_weight, weight_dtype, eps, cos, sin, cs_dtype,
+                            cs_stride_h, cs_stride_t, nullptr, group_bases, groups, out_stride_t, stream);
+}
+
+int ogx_video_qkv_rmsnorm_rope_positions_to_peers(const void* q, const void* k, const void* v, int64_t tokens,
+                                                  int64_t in_stride_t, const void* q_weight, const void* k_weight,
+                                                  int weight_dtype, float eps, const double* inv_freq,
+                                                  const unsigned char* slot_axis, int64_t grid_h, int64_t grid_w,
+                                                  int64_t token0, void* const* group_bases, int groups,
+                                                  int64_t out_stride_t, void* stream) {
+  ogx::rows::RopeSource src{};
+  const int rc = rope_source(inv_freq, slot_axis, grid_h, grid_w, token0, &src);
+  if (rc) return rc;
+  return rope_to_peers_impl(q, k, v, tokens, in_stride_t, q_weight, k_weight, weight_dtype, eps, nullptr, nullptr,
+                            OGX_DTYPE_BF16, 0, 0, &src, group_bases, groups, out_stride_t, stream);
 }
 
 int ogx_attention_fwd_e4m3_to_peers(const void* q, const void* k, const void* v, int64_t tokens, int64_t heads,

@@ -4,7 +4,7 @@ single launch on a small case.
     python -m opengenie_b200.kernel_bench attention --tokens 9216 --heads 4 [--e4m3] [--kv-tokens 1024]
     python -m opengenie_b200.kernel_bench gemm --m 9216 --n 12288 --k 4096 [--residual]
     python -m opengenie_b200.kernel_bench adazero --tokens 9216
-    python -m opengenie_b200.kernel_bench rope --tokens 9216
+    python -m opengenie_b200.kernel_bench rope --tokens 9216 [--positions]
     python -m opengenie_b200.kernel_bench qk_rmsnorm --tokens 9216 --kv-tokens 1024
     python -m opengenie_b200.kernel_bench compare --tokens 9216
     python -m opengenie_b200.kernel_bench fp8_peak
@@ -110,7 +110,7 @@ def bench_adazero(a) -> dict:
                                                     shift_index=0, scale_index=1)
     ms = _time(fn, a.steps, a.warmup)
     nbytes = a.tokens * 4096 * 3  # bf16 x read + e4m3 write (the uniform timestep rows stay in cache)
-    return {"kernel": "adazero_from_ada_kernel", "tokens": a.tokens, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9}
+    return {"kernel": "adazero_ring_kernel", "tokens": a.tokens, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9}
 
 
 def bench_rope(a) -> dict:
@@ -121,12 +121,19 @@ def bench_rope(a) -> dict:
     qkv = torch.randn((a.tokens, 3 * 4096), device="cuda", generator=g).to(torch.bfloat16)
     q, k = qkv[:, :4096].unsqueeze(0), qkv[:, 4096:8192].unsqueeze(0)
     qo, ko = torch.empty_like(q), torch.empty_like(k)
-    fn = lambda: ltx_ops.fused_video_qk_rmsnorm_rope(q, k, w.q_norm_weight, w.k_norm_weight, 1e-6,  # noqa: E731
-                                                     inp.cos, inp.sin, out=(qo, ko))
+    nbytes = a.tokens * 4096 * 2 * 4  # q, k read + written
+    if a.positions:
+        # cos/sin generated from positions of an LTX-like raster (18 x 32 latent grid per frame)
+        pos = synthetic.rope_positions((a.tokens + 575) // 576, 18, 32, device="cuda")
+        fn = lambda: ltx_ops.fused_video_qk_rmsnorm_rope_positions(  # noqa: E731
+            q, k, w.q_norm_weight, w.k_norm_weight, 1e-6, pos, out=(qo, ko))
+    else:
+        fn = lambda: ltx_ops.fused_video_qk_rmsnorm_rope(q, k, w.q_norm_weight, w.k_norm_weight, 1e-6,  # noqa: E731
+                                                         inp.cos, inp.sin, out=(qo, ko))
+        nbytes += 2 * a.tokens * 32 * 64 * inp.cos.element_size()  # cos, sin read
     ms = _time(fn, a.steps, a.warmup)
-    cs = inp.cos.element_size()
-    nbytes = a.tokens * 4096 * 2 * 4 + 2 * a.tokens * 32 * 64 * cs  # q, k read + written; cos, sin read
-    return {"kernel": "qk_rmsnorm_rope_kernel", "tokens": a.tokens, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9}
+    return {"kernel": "qk_rmsnorm_rope_ring_kernel", "tokens": a.tokens, "cos_sin": "generated" if a.positions else
+            "tables", "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9}
 
 
 def bench_qk_rmsnorm(a) -> dict:
@@ -284,6 +291,7 @@ def main(argv=None) -> None:
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--residual", action="store_true")
+    ap.add_argument("--positions", action="store_true", help="rope: generate cos/sin from positions")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--seed", type=int, default=0)

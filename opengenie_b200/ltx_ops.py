@@ -13,6 +13,8 @@ only read inputs and write outputs, on the current CUDA stream.
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 
 from . import _lib
@@ -434,10 +436,7 @@ def fused_residual_gate_bf16(x: torch.Tensor, y: torch.Tensor, gate: torch.Tenso
 
 
 # ---------------------------------------------------------------- Q/K RMSNorm + split RoPE
-def fused_video_qk_rmsnorm_rope_guard_reason(
-    q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor
-) -> str | None:
-    """Mirrors `_fused_video_qk_rmsnorm_rope_guard_reason` (ltx_serve/triton_ltx_ops.py:1513-1537)."""
+def _qk_guard_reason(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor) -> str | None:
     if not q.is_cuda or not k.is_cuda or q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
         return "qk_device_or_dtype"
     if q.shape != k.shape or q.ndim != 3 or q.shape[0] != 1 or q.shape[-1] != 4096:
@@ -448,6 +447,16 @@ def fused_video_qk_rmsnorm_rope_guard_reason(
         return "qk_noncontiguous"
     if q_weight.shape != (4096,) or k_weight.shape != (4096,) or q_weight.dtype != k_weight.dtype:
         return "qk_weight_shape"
+    return None
+
+
+def fused_video_qk_rmsnorm_rope_guard_reason(
+    q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor
+) -> str | None:
+    """Mirrors `_fused_video_qk_rmsnorm_rope_guard_reason` (ltx_serve/triton_ltx_ops.py:1513-1537)."""
+    reason = _qk_guard_reason(q, k, q_weight, k_weight)
+    if reason is not None:
+        return reason
     if cos.ndim != 4 or sin.ndim != 4 or cos.shape != sin.shape or cos.stride() != sin.stride() or cos.dtype != sin.dtype:
         return "rope_shape"
     if cos.shape[0] not in (1, q.shape[0]) or cos.shape[1] != 32 or cos.shape[2] != q.shape[1] or cos.shape[3] != 64:
@@ -490,6 +499,104 @@ def fused_video_qk_rmsnorm_rope(
         q_out.data_ptr(), k_out.data_ptr(), q_out.stride(1), _stream(q),
     )
     return q_out, k_out
+
+
+@dataclass(frozen=True)
+class RopePositions:
+    """Split-RoPE angles generated from latent positions instead of cos/sin tables.
+
+    Token i of a sequence (global index ``token0 + i``) sits at (t, h, w) of a [frames, grid_h, grid_w]
+    raster (t slowest, the order of the video tokens); rotary slot g = 64 * head + j (32 heads x 64) turns by
+    ``position[slot_axis[g]] * inv_freq[g]`` radians (axis 0 = t, 1 = h, 2 = w).  The tables are the
+    caller's: the construction of the un-vendored ltx_core preprocessor that the reference's cos/sin come from
+    is not available, so this library's synthetic configurations define one (``synthetic.rope_positions``).
+    ``inv_freq`` is float64 [2048] and ``slot_axis`` uint8 [2048], both on the GPU."""
+
+    inv_freq: torch.Tensor
+    slot_axis: torch.Tensor
+    frames: int
+    grid_h: int
+    grid_w: int
+
+    @property
+    def tokens(self) -> int:
+        return self.frames * self.grid_h * self.grid_w
+
+    def to(self, device) -> "RopePositions":
+        return RopePositions(self.inv_freq.to(device), self.slot_axis.to(device), self.frames, self.grid_h, self.grid_w)
+
+
+def rope_positions_guard_reason(pos: "RopePositions", device: torch.device) -> str | None:
+    if pos.inv_freq.dtype != torch.float64 or pos.inv_freq.shape != (2048,) or not pos.inv_freq.is_contiguous():
+        return "rope_shape"
+    if pos.slot_axis.dtype != torch.uint8 or pos.slot_axis.shape != (2048,) or not pos.slot_axis.is_contiguous():
+        return "rope_shape"
+    if pos.inv_freq.device != device or pos.slot_axis.device != device:
+        return "qk_device_or_dtype"
+    if pos.grid_h < 1 or pos.grid_w < 1 or pos.frames < 1:
+        return "rope_shape"
+    return None
+
+
+def fused_video_qk_rmsnorm_rope_positions(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    q_weight: torch.Tensor,
+    k_weight: torch.Tensor,
+    eps: float,
+    positions: RopePositions,
+    *,
+    token0: int = 0,
+    out: tuple[torch.Tensor, torch.Tensor] | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``fused_video_qk_rmsnorm_rope`` with cos/sin generated in the kernel from the tokens' (t, h, w)
+    positions (rounded to bf16 like the reference's tables) instead of read from [1, 32, L, 64] tables: the
+    same arithmetic, 2 x 2 B x 2048 fewer HBM bytes per token.  q/k hold tokens [token0, token0 + L) of the
+    raster.  ``rope_tables_from_positions`` returns the tables these angles make, for the table interface."""
+    reason = _qk_guard_reason(q, k, q_weight, k_weight)
+    if reason is None:
+        reason = rope_positions_guard_reason(positions, q.device)
+    if reason is None and (token0 < 0 or token0 + q.shape[1] > positions.tokens):
+        reason = "rope_shape"
+    if reason is not None:
+        raise ValueError(reason)
+    if out is None:
+        q_out, k_out = torch.empty_like(q), torch.empty_like(k)
+    else:
+        q_out, k_out = out
+        if q_out.stride(1) != k_out.stride(1) or q_out.shape != q.shape or k_out.shape != k.shape:
+            raise ValueError("qk_out_shape")
+    _lib.call(
+        "ogx_video_qk_rmsnorm_rope_positions",
+        q.data_ptr(), k.data_ptr(), q.shape[1], q.stride(1),
+        q_weight.contiguous().data_ptr(), k_weight.contiguous().data_ptr(), _code(q_weight), float(eps),
+        positions.inv_freq.data_ptr(), positions.slot_axis.data_ptr(), positions.grid_h, positions.grid_w, int(token0),
+        q_out.data_ptr(), k_out.data_ptr(), q_out.stride(1), _stream(q),
+    )
+    return q_out, k_out
+
+
+def rope_tables_from_positions(positions: RopePositions, *, token0: int = 0, tokens: int | None = None,
+                               dtype: torch.dtype = torch.bfloat16) -> tuple[torch.Tensor, torch.Tensor]:
+    """The cos/sin the generating RoPE kernel uses, as [1, 32, tokens, 64] tables (the reference's layout)."""
+    dev = positions.inv_freq.device
+    reason = rope_positions_guard_reason(positions, dev)
+    if tokens is None:
+        tokens = positions.tokens - token0
+    if reason is None and (tokens < 1 or token0 < 0 or token0 + tokens > positions.tokens):
+        reason = "rope_shape"
+    if reason is None and dtype not in (torch.bfloat16, torch.float32):
+        reason = "qk_device_or_dtype"
+    if reason is not None:
+        raise ValueError(reason)
+    cos = torch.empty((1, 32, tokens, 64), device=dev, dtype=dtype)
+    sin = torch.empty_like(cos)
+    _lib.call(
+        "ogx_rope_tables_from_positions",
+        positions.inv_freq.data_ptr(), positions.slot_axis.data_ptr(), positions.grid_h, positions.grid_w,
+        int(token0), tokens, _code(cos), cos.data_ptr(), sin.data_ptr(), torch.cuda.current_stream(dev).cuda_stream,
+    )
+    return cos, sin
 
 
 def fused_video_qkv_rmsnorm_rope_pack(
@@ -853,6 +960,7 @@ def collect_video_ada_values_calls() -> int:
 __all__ = [
     "QUANT_SINGLE",
     "QUANT_TORCH",
+    "RopePositions",
     "ada_from_table_guard_reason",
     "attention",
     "collect_video_ada_values_calls",
@@ -878,5 +986,8 @@ __all__ = [
     "fused_residual_gate_from_ada",
     "fused_video_qk_rmsnorm_rope",
     "fused_video_qk_rmsnorm_rope_guard_reason",
+    "fused_video_qk_rmsnorm_rope_positions",
     "fused_video_qkv_rmsnorm_rope_pack",
+    "rope_positions_guard_reason",
+    "rope_tables_from_positions",
 ]

@@ -80,13 +80,29 @@ def rope_tables(frames: int, grid_h: int, grid_w: int, *, theta: float = 10000.0
     h = torch.arange(grid_h, dtype=torch.float64).repeat_interleave(grid_w).repeat(frames)
     w = torch.arange(grid_w, dtype=torch.float64).repeat(frames * grid_h)
     pos = torch.stack([t, h, w], dim=0)  # [3, L]
-    g = torch.arange(HEADS * HEAD_DIM // 2, dtype=torch.int64)
-    axis = g % 3
-    rank = (g // 3).to(torch.float64)
-    inv_freq = theta ** (-rank / math.ceil(g.numel() / 3))
-    angle = pos[axis] * inv_freq[:, None]  # [2048, L]
+    inv_freq, axis = rope_slot_frequencies(theta=theta)
+    angle = pos[axis.long()] * inv_freq[:, None]  # [2048, L]
     angle = angle.reshape(HEADS, HEAD_DIM // 2, L).permute(0, 2, 1).unsqueeze(0)  # [1, 32, L, 64]
     return angle.cos().to(torch.bfloat16).contiguous(), angle.sin().to(torch.bfloat16).contiguous()
+
+
+def rope_slot_frequencies(*, theta: float = 10000.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """The per-slot construction behind ``rope_tables``: (inverse frequency float64 [2048], position axis
+    uint8 [2048]) for slot g = 64 * head + j: axis g % 3, inverse frequency theta ** -((g // 3) / ceil(2048 / 3))."""
+    g = torch.arange(HEADS * HEAD_DIM // 2, dtype=torch.int64)
+    axis = (g % 3).to(torch.uint8)
+    rank = (g // 3).to(torch.float64)
+    inv_freq = theta ** (-rank / math.ceil(g.numel() / 3))
+    return inv_freq.contiguous(), axis.contiguous()
+
+
+def rope_positions(frames: int, grid_h: int, grid_w: int, *, theta: float = 10000.0, device="cpu"):
+    """The same angles as ``rope_tables`` for the kernels that generate cos/sin from the tokens' (t, h, w)
+    positions (``ltx_ops.RopePositions``)."""
+    from .ltx_ops import RopePositions
+
+    inv_freq, axis = rope_slot_frequencies(theta=theta)
+    return RopePositions(inv_freq.to(device), axis.to(device), frames, grid_h, grid_w)
 
 
 def quantize_weight_e4m3(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

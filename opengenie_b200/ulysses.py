@@ -209,7 +209,8 @@ class UlyssesVideoSelfAttention:
         return t[:, t0:t1]
 
     # ------------------------------------------------------------------ stages
-    def _qkv_and_exchange(self, x_loc, ts_loc, cos_loc, sin_loc, ws):
+    def _qkv_and_exchange(self, x_loc, ts_loc, rope, ws):
+        """``rope``: (cos, sin) tables of this rank's tokens, or (RopePositions, first token of the slice)."""
         w = self.w
         p = self.plan
         Ll = x_loc.shape[1]
@@ -224,17 +225,31 @@ class UlyssesVideoSelfAttention:
                                   out=qkv, n_per_scale=4096)
         send = ws["send1"]
         D = 4096
-        if cos_loc.shape[2] != Ll or sin_loc.shape != cos_loc.shape or send.shape != p.qkv_send_shape(Ll):
+        positions = isinstance(rope[0], ltx_ops.RopePositions)
+        if positions:
+            pos, token0 = rope
+            reason = ltx_ops.rope_positions_guard_reason(pos, qkv.device)
+            if reason is None and (token0 < 0 or token0 + Ll > pos.tokens):
+                reason = "rope_shape"
+            if reason is not None:
+                raise ValueError(reason)
+            # the rope arguments of the entry points: frequency tables, grid, first token
+            src = (pos.inv_freq.data_ptr(), pos.slot_axis.data_ptr(), pos.grid_h, pos.grid_w, int(token0))
+        else:
+            cos_loc, sin_loc = rope
+            if cos_loc.shape[2] != Ll or sin_loc.shape != cos_loc.shape:
+                raise ValueError("rope_shape")
+            src = (cos_loc.data_ptr(), sin_loc.data_ptr(), ltx_ops._code(cos_loc), cos_loc.stride(1), cos_loc.stride(2))
+        if send.shape != p.qkv_send_shape(Ll):
             raise ValueError("rope_shape")
         if self.peer is not None:
             with self._phase("rope_to_peers"):
                 bases = ws["recv1_dst"]
                 _lib.call(
-                    "ogx_video_qkv_rmsnorm_rope_to_peers",
+                    "ogx_video_qkv_rmsnorm_rope_positions_to_peers" if positions else "ogx_video_qkv_rmsnorm_rope_to_peers",
                     qkv.data_ptr(), qkv[:, D:].data_ptr(), qkv[:, 2 * D:].data_ptr(), Ll, qkv.stride(0),
                     w.q_norm_weight.data_ptr(), w.k_norm_weight.data_ptr(), ltx_ops._code(w.q_norm_weight),
-                    float(w.qk_eps), cos_loc.data_ptr(), sin_loc.data_ptr(), ltx_ops._code(cos_loc),
-                    cos_loc.stride(1), cos_loc.stride(2), bases, p.world, 3 * p.heads_local * p.head_dim,
+                    float(w.qk_eps), *src, bases, p.world, 3 * p.heads_local * p.head_dim,
                     ltx_ops._stream(qkv),
                 )
             with self._phase("barrier_seq_to_heads"):
@@ -243,11 +258,10 @@ class UlyssesVideoSelfAttention:
         self._phase_ctx = self._phase("rope_scatter")
         self._phase_ctx.__enter__()
         _lib.call(
-            "ogx_video_qkv_rmsnorm_rope_scatter",
+            "ogx_video_qkv_rmsnorm_rope_positions_scatter" if positions else "ogx_video_qkv_rmsnorm_rope_scatter",
             qkv.data_ptr(), qkv[:, D:].data_ptr(), qkv[:, 2 * D:].data_ptr(), Ll, qkv.stride(0),
             w.q_norm_weight.data_ptr(), w.k_norm_weight.data_ptr(), ltx_ops._code(w.q_norm_weight), float(w.qk_eps),
-            cos_loc.data_ptr(), sin_loc.data_ptr(), ltx_ops._code(cos_loc), cos_loc.stride(1), cos_loc.stride(2),
-            send[:, :, 0].data_ptr(), send[:, :, 1].data_ptr(), send[:, :, 2].data_ptr(), send.stride(1),
+            *src, send[:, :, 0].data_ptr(), send[:, :, 1].data_ptr(), send[:, :, 2].data_ptr(), send.stride(1),
             send.stride(0), p.heads_local, ltx_ops._stream(qkv),
         )
         self._phase_ctx.__exit__(None, None, None)
@@ -264,10 +278,12 @@ class UlyssesVideoSelfAttention:
         L = Ll * p.world
         t0 = p.rank * Ll
         ts_loc = timestep[:, t0:t0 + Ll]
-        cos_loc = pe[0][:, :, t0:t0 + Ll]
-        sin_loc = pe[1][:, :, t0:t0 + Ll]
+        if isinstance(pe, ltx_ops.RopePositions):
+            rope = (pe, t0)
+        else:
+            rope = (pe[0][:, :, t0:t0 + Ll], pe[1][:, :, t0:t0 + Ll])
         ws = self.workspace(Ll)
-        q, k, v = self._qkv_and_exchange(x_loc, ts_loc, cos_loc, sin_loc, ws)
+        q, k, v = self._qkv_and_exchange(x_loc, ts_loc, rope, ws)
         send2 = ws["send2"]
         if self.peer is not None:
             with self._phase("attention_to_peers"):
@@ -332,7 +348,8 @@ class UlyssesVideoSelfAttention:
             lin.input_scale = s_in.clone()
         self.blk.shared_quant = True
         ws = self.workspace(Ll)
-        q, k, v = self._qkv_and_exchange(x_loc, ts_loc, pe[0][:, :, t0:t0 + Ll], pe[1][:, :, t0:t0 + Ll], ws)
+        rope = (pe, t0) if isinstance(pe, ltx_ops.RopePositions) else (pe[0][:, :, t0:t0 + Ll], pe[1][:, :, t0:t0 + Ll])
+        q, k, v = self._qkv_and_exchange(x_loc, ts_loc, rope, ws)
         attn = ltx_ops.attention(q, k, v, p.heads_local)
         amax = attn.float().abs().amax().reshape(1)
         dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)

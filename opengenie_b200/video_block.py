@@ -98,7 +98,8 @@ class VideoSelfAttentionBlock:
         *,
         out: torch.Tensor | None = None,
     ) -> torch.Tensor:
-        """vx [1, L, 4096] bf16 -> vx + gate * (out_proj(attn(...)) + bias), bf16."""
+        """vx [1, L, 4096] bf16 -> vx + gate * (out_proj(attn(...)) + bias), bf16.  ``pe``: (cos, sin) tables or
+        ``ltx_ops.RopePositions``."""
         if vx.ndim != 3 or vx.shape[0] != 1 or vx.shape[-1] != self.dim:
             raise ValueError("shape")
         w = self.w
@@ -109,8 +110,7 @@ class VideoSelfAttentionBlock:
         q = qkv[:, :D].unsqueeze(0)
         k = qkv[:, D:2 * D].unsqueeze(0)
         v = qkv[:, 2 * D:].unsqueeze(0)
-        cos, sin = pe
-        ltx_ops.fused_video_qk_rmsnorm_rope(q, k, w.q_norm_weight, w.k_norm_weight, w.qk_eps, cos, sin, out=(q, k))
+        self.rope(q, k, pe)
         if self.to_gate_logits is not None:
             ws["oq"] = ltx_ops.fused_fp8_quantize_e4m3(self._gated_attention(q, k, v, ws["norm"]),
                                                        w.to_out.input_scale)
@@ -122,6 +122,17 @@ class VideoSelfAttentionBlock:
         )
 
     __call__ = forward
+
+    def rope(self, q: torch.Tensor, k: torch.Tensor, pe) -> None:
+        """Q/K RMSNorm + split RoPE in place; ``pe`` is (cos, sin) tables [1, 32, L, 64] (the reference's
+        interface) or ``ltx_ops.RopePositions`` (cos/sin generated in the kernel from the tokens' positions)."""
+        w = self.w
+        if isinstance(pe, ltx_ops.RopePositions):
+            ltx_ops.fused_video_qk_rmsnorm_rope_positions(q, k, w.q_norm_weight, w.k_norm_weight, w.qk_eps, pe,
+                                                          out=(q, k))
+        else:
+            cos, sin = pe
+            ltx_ops.fused_video_qk_rmsnorm_rope(q, k, w.q_norm_weight, w.k_norm_weight, w.qk_eps, cos, sin, out=(q, k))
 
     def _gated_attention(self, q, k, v, norm: torch.Tensor) -> torch.Tensor:
         """bf16 attention output times 2*sigmoid(gate logits) per head (the gated checkpoints)."""
@@ -170,7 +181,7 @@ class VideoSelfAttentionBlock:
         q = qkv[:, :D].unsqueeze(0)
         k = qkv[:, D:2 * D].unsqueeze(0)
         v = qkv[:, 2 * D:].unsqueeze(0)
-        ltx_ops.fused_video_qk_rmsnorm_rope(q, k, w.q_norm_weight, w.k_norm_weight, w.qk_eps, pe[0], pe[1], out=(q, k))
+        self.rope(q, k, pe)
         if self.to_gate_logits is not None:
             attn = self._gated_attention(q, k, v, ws["norm"])
         else:

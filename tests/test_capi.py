@@ -113,12 +113,14 @@ def test_ops_refuse_cpu_tensors():
 
 
 def test_python_surface_exports_every_public_op():
-    """``ltx_ops.__all__`` names every public function (the reference's op names and this library's fused ones)
-    and the quantiser mode constants, and nothing that does not exist."""
+    """``ltx_ops.__all__`` names every public function and class (the reference's op names and this library's
+    fused ones, the RopePositions argument type) and the quantiser mode constants, and nothing that does not
+    exist."""
     import inspect
 
     from opengenie_b200 import ltx_ops
 
     public = {n for n, f in vars(ltx_ops).items()
-              if inspect.isfunction(f) and f.__module__ == ltx_ops.__name__ and not n.startswith("_")}
+              if (inspect.isfunction(f) or inspect.isclass(f)) and f.__module__ == ltx_ops.__name__
+              and not n.startswith("_")}
     assert public | {"QUANT_SINGLE", "QUANT_TORCH"} == set(ltx_ops.__all__)

@@ -140,16 +140,49 @@ def test_block_zero_gate_is_identity(ogx_lib):
     assert torch.equal(out, dev.x)
 
 
+def _epilogue_fp32_from_codes(oq, w, x, ts_view):
+    """The out-projection + bias + Ada gate + residual in fp32 stages on the GPU, fed given attention codes,
+    and the per-element allowance for fp32 accumulation order and the four bf16 roundings that follow it."""
+    def r16(t):
+        return t.to(torch.bfloat16).float()
+
+    a = oq.reshape(-1, oq.shape[-1]).float()
+    wf = w.to_out.weight.float()
+    s = (w.to_out.input_scale.float() * w.to_out.weight_scale.float())
+    y = r16((a @ wf.T) * s)
+    absdot = (a.abs() @ wf.abs().T) * s
+    table = w.scale_shift_table.float()
+    gate = r16(table[2].view(1, -1) + ts_view[0, :, 2, :].float())
+    yb = r16(y + r16(w.to_out.bias.float()))
+    prod = r16(yb * gate)
+    ref = r16(x.reshape(-1, x.shape[-1]).float() + prod)
+
+    def ulp(t):
+        return torch.exp2(torch.floor(torch.log2(t.abs().clamp_min(2.0 ** -126))) - 7.0)
+
+    bound = gate.abs() * (ulp(y) + ulp(yb) + 2.0 ** -17 * absdot) + ulp(prod) + ulp(ref)
+    return ref.view(x.shape), bound.view(x.shape)
+
+
 @pytest.mark.parametrize("name", ["c1_l9216", "c2_df_l9216", "c4_l28800"])
 def test_block_full_size_vs_fp32_reference_on_gpu(ogx_lib, name):
-    """L=9216 (uniform and diffusion-forcing timesteps): the fused block against the same stages in
-    torch fp32 on the GPU (fp32 matmuls on the dequantised e4m3 operands, fp32 SDPA).
+    """L=9216 (uniform and diffusion-forcing timesteps) and L=28800: the fused block against the same stages in
+    torch fp32 on the GPU (fp32 matmuls on the dequantised e4m3 operands, fp32 SDPA), with the north-star bound
+    max|d| <= 2e-2 (+1 bf16 ulp of |ref|) and sum|d|/sum|ref| <= 1e-2.
 
-    Tolerance: sum|d|/sum|ref| <= 1e-2 (the north-star mean-relative bound) and max|d| no larger than
-    the reference's own GPU path (Triton quantiser, cuBLAS FP8, cuDNN SDPA; measured here beside ours)
-    shows against the same fp32 evaluation.  The 2e-2 max-abs bound is reported, not asserted: the
-    block's outputs reach |out| ~ 10 (bf16 ulp 0.0625) and any e4m3 pipeline flips some codes against
-    an fp32 evaluation, the reference path by more than ours."""
+    What holds and is asserted:
+    * sum|d|/sum|ref| <= 1e-2 end to end (measured 1.2e-3 at L=9216, 2.1e-3 at L=28800);
+    * max|d| no larger than that of the reference's own GPU path on the same inputs (its Triton-semantics
+      quantiser, cuBLAS FP8 and cuDNN SDPA: 0.34-0.52 against ours 0.125-0.16);
+    * once both sides quantise the same attention output, the out-projection, bias, gate and residual fed this
+      block's own attention codes are within the fp32-accumulation and bf16-rounding allowance of the fp32
+      stages (the roundings the reference performs: y, y + bias, (y + bias) * gate, x + that).
+    What does not hold end to end, and why: the 2e-2 (+1 ulp) max-abs bound fails by up to ~0.06-0.13
+    (tens of thousands of the 37.7M outputs at L=9216).  Its cause is the E4M3 quantiser of the attention
+    output: where the attention output differs from the fp32 one by one bf16 ulp it can round to the next
+    e4m3 code, one e4m3 step (1/16-1/8 of the value), and the out-projection carries that step into outputs of
+    any magnitude.  The fp32 reference flips the other way there; any FP8 pipeline, the reference's included,
+    shows it."""
     from opengenie_b200 import synthetic
     from opengenie_b200.video_block import VideoSelfAttentionBlock
 
@@ -159,15 +192,42 @@ def test_block_full_size_vs_fp32_reference_on_gpu(ogx_lib, name):
     blk = VideoSelfAttentionBlock(w, "cuda")
     blk.calibrate_input_scales(inp.x, inp.timestep, (inp.cos, inp.sin))
     out = blk(inp.x, inp.timestep, (inp.cos, inp.sin))
+    oq = blk.workspace(cfg.tokens)["oq"]
     ts_view = inp.timestep.reshape(1, cfg.tokens, 6, 4096)
     with torch.no_grad():
-        ref = to_np(O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, blk.w))
+        ref_t = O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, blk.w)
+        ref = to_np(ref_t)
         ref_path = to_np(reference_gpu_path_block(inp.x, ts_view, inp.cos, inp.sin, blk.w))
-    ours = block_tolerance(to_np(out), ref, ulps=2.0)
-    theirs = block_tolerance(ref_path, ref, ulps=2.0)
-    print(name, "ours vs fp32:", ours, "reference GPU path vs fp32:", theirs)
+        epi_ref, epi_bound = _epilogue_fp32_from_codes(oq, blk.w, inp.x, ts_view)
+    got = to_np(out)
+    ours = block_tolerance(got, ref, ulps=1.0)
+    theirs = block_tolerance(ref_path, ref, ulps=1.0)
+    d_epi = (out.float() - epi_ref).abs()
+    epi_excess = float((d_epi - epi_bound).max())
+    print(name, "ours vs fp32:", ours, "reference GPU path vs fp32:", theirs, "epilogue on our codes: max",
+          float(d_epi.max()), "excess over its allowance", epi_excess)
     assert ours["mean_rel"] <= 1e-2, ours
     assert ours["max_abs"] <= theirs["max_abs"], (ours, theirs)
+    assert epi_excess <= 0.0, epi_excess
+    assert status_clean()
+
+
+@pytest.mark.parametrize("name", ["c1_l9216", "c2_df_l9216"])
+def test_block_with_generated_rope_equals_block_with_tables(ogx_lib, name):
+    """The block given RopePositions (cos/sin generated in the RoPE kernel) equals, bit for bit, the block
+    given the tables of the same values through the reference's table interface."""
+    from opengenie_b200 import ltx_ops, synthetic
+    from opengenie_b200.video_block import VideoSelfAttentionBlock
+
+    cfg = synthetic.CONFIGS[name]
+    inp = synthetic.make_inputs(cfg, seed=45).to("cuda")
+    pos = synthetic.rope_positions(cfg.frames, cfg.grid_h, cfg.grid_w, device="cuda")
+    tables = ltx_ops.rope_tables_from_positions(pos)
+    blk = VideoSelfAttentionBlock(synthetic.make_weights(seed=46), "cuda")
+    blk.calibrate_input_scales(inp.x, inp.timestep, tables)
+    out_t = blk(inp.x, inp.timestep, tables)
+    out_p = blk(inp.x, inp.timestep, pos)
+    assert torch.equal(out_t, out_p)
     assert status_clean()
 
 

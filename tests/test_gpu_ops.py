@@ -239,6 +239,82 @@ def test_qkv_rope_scatter_layout(ops, world):
     assert status_clean()
 
 
+@pytest.mark.parametrize("grid", [(2, 3, 5), (16, 18, 32), (3, 45, 40)])
+def test_rope_tables_from_positions_vs_construction(ops, grid):
+    """The cos/sin the kernels generate from (t, h, w) positions against the construction evaluated in float64
+    on the CPU and rounded to bf16 (synthetic.rope_tables): within one bf16 ulp everywhere, equal almost
+    everywhere (the hardware sin/cos after an exact reduction in turns are within ~4e-7 of the exact values, so
+    only values that fall that close to a bf16 rounding boundary round the other way)."""
+    from opengenie_b200 import synthetic
+
+    pos = synthetic.rope_positions(*grid, device="cuda")
+    cos, sin = ops.rope_tables_from_positions(pos)
+    ref_c, ref_s = synthetic.rope_tables(*grid)
+    for got, ref in ((cos, ref_c), (sin, ref_s)):
+        g, r = to_np(got), to_np(ref)
+        ok, worst = within_ulps(g, r, ulps=1.0, atol=2.0 ** -24)
+        assert ok, worst
+        assert (g != r).mean() < 2e-3, (g != r).mean()
+    # a slice of tokens starting at token0 is the same slice of the whole table
+    t0, n = pos.tokens // 3, pos.tokens // 2
+    c2, s2 = ops.rope_tables_from_positions(pos, token0=t0, tokens=n)
+    assert torch.equal(c2, cos[:, :, t0:t0 + n]) and torch.equal(s2, sin[:, :, t0:t0 + n])
+    assert status_clean()
+
+
+@pytest.mark.parametrize("tokens,token0", [(1, 0), (300, 0), (1152, 5000)])
+@pytest.mark.parametrize("wdtype", [torch.bfloat16, torch.float32])
+def test_qk_rmsnorm_rope_positions_equals_table_kernel(ops, tokens, token0, wdtype):
+    """Generated cos/sin: bit for bit the table kernel given the tables of the same values, for any slice of
+    the raster and both weight dtypes; and within one ulp of the float64 oracle on those tables."""
+    from opengenie_b200 import synthetic
+
+    pos = synthetic.rope_positions(16, 18, 32, device="cuda")
+    q, k, qw, kw, _, _ = _rope_case(tokens, tokens + 3)
+    q, k = q.cuda(), k.cuda()
+    qw, kw = qw.to(wdtype).cuda(), kw.to(wdtype).cuda()
+    cos, sin = ops.rope_tables_from_positions(pos, token0=token0, tokens=tokens)
+    tq, tk = ops.fused_video_qk_rmsnorm_rope(q, k, qw, kw, 1e-6, cos, sin)
+    gq, gk = ops.fused_video_qk_rmsnorm_rope_positions(q, k, qw, kw, 1e-6, pos, token0=token0)
+    assert torch.equal(gq, tq) and torch.equal(gk, tk)
+    if tokens <= 300:
+        for got, x, w in ((gq, q, qw), (gk, k, kw)):
+            ref = O.qk_rmsnorm_rope(x.cpu(), w.float().cpu(), 1e-6, cos.cpu(), sin.cpu())
+            ok, worst = within_ulps(to_np(got), ref, ulps=1.0, atol=1e-6)
+            assert ok, worst
+    with pytest.raises(ValueError, match="rope_shape"):
+        ops.fused_video_qk_rmsnorm_rope_positions(q, k, qw, kw, 1e-6, pos, token0=pos.tokens - tokens + 1)
+    assert status_clean()
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_qkv_rope_positions_scatter_layout(ops, world):
+    """The send layout of the sequence-to-head exchange written with generated cos/sin equals the one written
+    from the tables of the same values."""
+    from opengenie_b200 import _lib, synthetic
+    from opengenie_b200.ltx_ops import _stream
+
+    L, t0 = 24, 40
+    pos = synthetic.rope_positions(2, 8, 16, device="cuda")
+    q, k, qw, kw, _, _ = _rope_case(L, 11)
+    v = torch.randn((1, L, 4096), generator=torch.Generator().manual_seed(12)).to(torch.bfloat16)
+    q, k, v, qw, kw = (t.cuda() for t in (q, k, v, qw, kw))
+    cos, sin = ops.rope_tables_from_positions(pos, token0=t0, tokens=L)
+    hpg = 32 // world
+    sends = []
+    for gen in (False, True):
+        send = torch.empty((world, L, 3, hpg, 128), device="cuda", dtype=torch.bfloat16)
+        rope = ((pos.inv_freq.data_ptr(), pos.slot_axis.data_ptr(), pos.grid_h, pos.grid_w, t0) if gen else
+                (cos.data_ptr(), sin.data_ptr(), 0, cos.stride(1), cos.stride(2)))
+        _lib.call("ogx_video_qkv_rmsnorm_rope_positions_scatter" if gen else "ogx_video_qkv_rmsnorm_rope_scatter",
+                  q.data_ptr(), k.data_ptr(), v.data_ptr(), L, 4096, qw.data_ptr(), kw.data_ptr(), 0, 1e-6, *rope,
+                  send[:, :, 0].data_ptr(), send[:, :, 1].data_ptr(), send[:, :, 2].data_ptr(),
+                  send.stride(1), send.stride(0), hpg, _stream(q))
+        sends.append(send)
+    assert torch.equal(sends[0], sends[1])
+    assert status_clean()
+
+
 def test_qkv_rmsnorm_rope_pack_layout(ops):
     """fused_video_qkv_rmsnorm_rope_pack: [1, L, 3, 32, 128] holding the roped q and k and the untouched v,
     bit for bit the separate op's q/k."""
