@@ -95,35 +95,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Packed two-lane fp32 arithmetic (sm_100 f32x2 instructions): one issue slot for two values.
-struct f2 {
-  float x, y;
-};
-__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
-  f2 d;
-  asm("{.reg .b64 A, B, C, D;\n\t"
-      "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\tmov.b64 C, {%6, %7};\n\t"
-      "fma.rn.f32x2 D, A, B, C;\n\tmov.b64 {%0, %1}, D;}\n"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-__device__ __forceinline__ f2 add2(f2 a, f2 b) {
-  f2 d;
-  asm("{.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
-      "add.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;}\n"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
-  f2 d;
-  asm("{.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
-      "sub.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;}\n"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

@@ -183,17 +183,6 @@ struct AdaArgs {
   uint8_t* q;                // e4m3 output (QUANT only)
 };
 
-constexpr int kRowThreads = 128;
-
-// Sum over the 128 threads of a row CTA.
-__device__ __forceinline__ float row_sum(float v, float* red) {
-  v = warp_sum(v);
-  const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) red[w] = v;
-  __syncthreads();
-  return red[0] + red[1] + red[2] + red[3];
-}
-
 // ----------------------------------------------------------------- per-head gate
 // y = bf16(x * gate[row, col / dim_head]) for bf16 x [rows, cols] and bf16 gates: the optional gated
 // attention of the video self-attention branch (fused_head_gate_mul_bf16, triton_ltx_ops.py:614-637,
@@ -477,55 +466,17 @@ __device__ __forceinline__ __nv_bfloat16* group_base(__nv_bfloat16* const (&base
 
 // Q/K RMSNorm without rotary embedding (attention whose keys come from another sequence): rows
 // [0, rows_q) are Q rows, [rows_q, rows_q + rows_k) K rows, each normalised over its 4096 columns and
-// multiplied by its tensor's weight with the arithmetic of rmsnorm_rope_row (fp32, one bf16 rounding).
+// multiplied by its tensor's weight with the arithmetic of the RoPE kernel (fp32, one bf16 rounding, the
+// same order of the sum of squares), so with cos = 1 and sin = 0 the two agree bit for bit.  The kernel is
+// the row-pipeline qk_rmsnorm_ring_kernel (rows.cuh).
 struct RmsRowsArgs {
   const __nv_bfloat16* in[2];
   int64_t in_stride[2];  // elements between rows
   __nv_bfloat16* out[2];
   int64_t out_stride[2];
   const void* weight[2];
-  int64_t rows_q;
+  int64_t rows_q, rows;  // Q rows, all rows
   float eps;
 };
-
-// One 128-thread CTA per row; a row is read whole into registers before its first store, so the output
-// may alias the input.
-template <typename WT>
-__global__ void __launch_bounds__(kRowThreads) qk_rmsnorm_rows_kernel(RmsRowsArgs a) {
-  pdl_trigger();
-  pdl_wait();
-  constexpr int VPT = 4096 / 8 / kRowThreads;  // 4
-  __shared__ float red[4];
-  const int tid = threadIdx.x;
-  const int64_t r = blockIdx.x;
-  // selects, not a.in[j]: a runtime index into the parameter arrays would copy them to local memory
-  const bool is_k = r >= a.rows_q;
-  const int64_t t = is_k ? r - a.rows_q : r;
-  const __nv_bfloat16* in = (is_k ? a.in[1] : a.in[0]) + t * (is_k ? a.in_stride[1] : a.in_stride[0]);
-  const WT* w = static_cast<const WT*>(is_k ? a.weight[1] : a.weight[0]);
-  uint4 xv[VPT];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    xv[i] = __ldg(reinterpret_cast<const uint4*>(in) + i * kRowThreads + tid);
-    float f[8];
-    unpack8(xv[i], f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
-  }
-  ss = row_sum(ss, red);
-  const float inv_rms = rsqrtf(ss / 4096.f + a.eps);
-  __nv_bfloat16* out = (is_k ? a.out[1] : a.out[0]) + t * (is_k ? a.out_stride[1] : a.out_stride[0]);
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int vec = i * kRowThreads + tid;
-    float f[8], wv[8], n[8];
-    unpack8(xv[i], f);
-    load8<WT>(w + vec * 8, wv);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) n[e] = f[e] * inv_rms * wv[e];
-    reinterpret_cast<uint4*>(out)[vec] = pack8(n);
-  }
-}
 
 }  // namespace ogx

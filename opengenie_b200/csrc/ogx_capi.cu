@@ -228,7 +228,7 @@ int ada_dispatch(const ogx::AdaArgs& a, int64_t cols, int table_dtype, int ts_dt
 template <typename WT, typename CsT, bool GEN, bool COPY_V>
 int launch_rope_ring(const ogx::RopeArgs& a, const ogx::rows::RopeSource& src, cudaStream_t s) {
   auto kern = ogx::rows::qk_rmsnorm_rope_ring_kernel<WT, CsT, GEN, COPY_V>;
-  const int smem = ogx::rows::RopeLayout<WT>::smem_bytes(COPY_V) + 128;
+  const int smem = ogx::rows::RopeLayout::smem_bytes(COPY_V) + 128;
   int rc = ensure_smem(kern, smem);
   if (rc) return rc;
   const int64_t sms = sm_count();
@@ -691,14 +691,23 @@ int ogx_qk_rmsnorm(const void* q, int64_t q_rows, int64_t q_stride, const void* 
   a.weight[0] = q_weight;
   a.weight[1] = k_weight;
   a.rows_q = q_rows;
+  a.rows = q_rows + k_rows;
   a.eps = eps;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 grid(static_cast<unsigned>(q_rows + k_rows));
-  if (weight_dtype == OGX_DTYPE_F32)
-    launch(ogx::qk_rmsnorm_rows_kernel<float>, grid, ogx::kRowThreads, 0, s, a);
-  else
-    launch(ogx::qk_rmsnorm_rows_kernel<__nv_bfloat16>, grid, ogx::kRowThreads, 0, s, a);
-  return check_launch("qk_rmsnorm_rows_kernel");
+  const int64_t sms = sm_count();
+  const dim3 grid(static_cast<unsigned>(a.rows < sms ? a.rows : sms));
+  const size_t smem = ogx::rows::kRmsSmem + 128;
+  int rc;
+  if (weight_dtype == OGX_DTYPE_F32) {
+    rc = ensure_smem(ogx::rows::qk_rmsnorm_ring_kernel<float>, static_cast<int>(smem));
+    if (rc) return rc;
+    launch(ogx::rows::qk_rmsnorm_ring_kernel<float>, grid, ogx::rows::kThreads, smem, s, a);
+  } else {
+    rc = ensure_smem(ogx::rows::qk_rmsnorm_ring_kernel<__nv_bfloat16>, static_cast<int>(smem));
+    if (rc) return rc;
+    launch(ogx::rows::qk_rmsnorm_ring_kernel<__nv_bfloat16>, grid, ogx::rows::kThreads, smem, s, a);
+  }
+  return check_launch("qk_rmsnorm_ring_kernel");
 }
 
 }  // extern "C"

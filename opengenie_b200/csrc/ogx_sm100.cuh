@@ -377,4 +377,43 @@ __device__ __forceinline__ void bf16_round2(float& a, float& b) {
   b = __uint_as_float(p & 0xFFFF0000u);
 }
 
+// ---------------------------------------------------------------- packed fp32 pairs
+// Packed two-lane fp32 arithmetic (sm_100 f32x2 instructions): one issue slot for two values.
+struct f2 {
+  float x, y;
+};
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("{.reg .b64 A, B, C, D;\n\t"
+      "mov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\tmov.b64 C, {%6, %7};\n\t"
+      "fma.rn.f32x2 D, A, B, C;\n\tmov.b64 {%0, %1}, D;}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 d;
+  asm("{.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "add.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 d;
+  asm("{.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "sub.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 d;
+  asm("{.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "mul.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 }  // namespace ogx

@@ -9,8 +9,8 @@
 //   warps 0..7                   each take every eighth row of the CTA: wait for its stage, reduce the
 //                                sum of squares from shared memory (warp shuffles, no block barrier),
 //                                write the outputs with 16-byte stores, free the stage.
-// With 11-16 stages a SM keeps 128-176 KB of row loads in flight, which is what the HBM latency needs;
-// no register holds a row.  Every wait is bounded (a wait that runs out records OGX_ERR_TIMEOUT, the
+// With 11-24 stages (up to ~190 KB) a SM keeps enough row loads in flight for the HBM latency; no
+// register holds a row.  Every wait is bounded (a wait that runs out records OGX_ERR_TIMEOUT, the
 // CTA stops and lets its copies in flight land before it exits).
 //
 // The split-RoPE cos/sin are either read from [heads, tokens, 64] tables (the reference's interface,
@@ -42,9 +42,11 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
                : "memory");
 }
 
+constexpr int kMaxStages = 24;
+
 struct Ring {
-  uint64_t full[16];
-  uint64_t empty[16];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   int abort;
 };
 
@@ -80,6 +82,34 @@ __device__ __forceinline__ void ring_produce(Ring& r, uint8_t* ring, int stages,
   }
 }
 
+// The two bf16 values of a packed word as fp32 (low half first).
+__device__ __forceinline__ f2 bf16x2_to_f2(uint32_t w) { return f2{__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u)}; }
+
+// Sum of squares of the 8 bf16 values of a 16-byte vector into two packed accumulators.
+__device__ __forceinline__ void sumsq8(const uint4& v, f2& a, f2& b) {
+  const f2 p0 = bf16x2_to_f2(v.x), p1 = bf16x2_to_f2(v.y), p2 = bf16x2_to_f2(v.z), p3 = bf16x2_to_f2(v.w);
+  a = fma2(p0, p0, a);
+  b = fma2(p1, p1, b);
+  a = fma2(p2, p2, a);
+  b = fma2(p3, p3, b);
+}
+
+// The reference's torch-path quantiser (triton_ltx_ops.py:146-148) of two bf16-valued floats: t = bf16(y * r)
+// by a packed RNE conversion, then the saturating e4m3 conversion, which also performs the clamp to +-448
+// (finite values past 448 and infinities saturate, as clamp then cast does).  NaN comes out as an e4m3 NaN
+// code (low 7 bits 0x7F) and is patched to 0xFF per byte by the caller (torch's bf16 path, bf16 NaN -> 0xFF).
+__device__ __forceinline__ uint32_t quant2_torch(f2 yb, f2 r2) {
+  const f2 t = mul2(yb, r2);
+  const f2 tb = bf16x2_to_f2(pack_bf16x2(t.x, t.y));
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(tb.x, tb.y), __NV_SATFINITE, __NV_E4M3)) & 0xFFFFu;
+}
+
+// Every byte of w whose low 7 bits are all ones (an e4m3 NaN code) becomes 0xFF.
+__device__ __forceinline__ uint32_t nan_bytes_to_ff(uint32_t w) {
+  const uint32_t hit = ((w & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u;
+  return w | (hit - (hit >> 7)) | hit;
+}
+
 __device__ __forceinline__ float warp_allsum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -100,12 +130,12 @@ __device__ __forceinline__ void cta_rows(int64_t rows, int64_t& r0, int64_t& r1)
 // copied into each stage with its x row), then the ring.
 template <int COLS, typename TsT>
 struct AdaLayout {
-  static constexpr int kAda = 2 * COLS * static_cast<int>(sizeof(TsT));  // shift, scale (bf16-exact for bf16 ts)
+  static constexpr int kAda = 2 * COLS * 4;  // fp32 per column: shift and 1 + scale (uniform) or the table parts
   static constexpr int kStageUniform = COLS * 2;
   static constexpr int kStagePerToken = COLS * 2 + 2 * COLS * static_cast<int>(sizeof(TsT));
   __host__ __device__ static constexpr int stage_bytes(bool uniform) { return uniform ? kStageUniform : kStagePerToken; }
   __host__ __device__ static constexpr int stages(bool uniform) {
-    return ((kDynLimit - kAda) / stage_bytes(uniform)) > 16 ? 16 : ((kDynLimit - kAda) / stage_bytes(uniform));
+    return ((kDynLimit - kAda) / stage_bytes(uniform)) > kMaxStages ? kMaxStages : ((kDynLimit - kAda) / stage_bytes(uniform));
   }
   __host__ __device__ static constexpr int smem_bytes(bool uniform) { return kAda + stages(uniform) * stage_bytes(uniform); }
 };
@@ -132,8 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Ring ring;
   uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 127u) & ~127u) - smem_u32(smem_raw));
-  TsT* ada_shift = reinterpret_cast<TsT*>(smem);
-  TsT* ada_scale = ada_shift + COLS;
+  // uniform timestep: ada0 = shift, ada1 = 1 + scale; per-token timestep: ada0 / ada1 = the table parts of
+  // shift / scale (rounded to the timestep's dtype when the dtypes differ)
+  float* ada0 = reinterpret_cast<float*>(smem);
+  float* ada1 = ada0 + COLS;
   uint8_t* stages = smem + Lay::kAda;
   ring_init(ring, S);
   int64_t r0, r1;
@@ -141,7 +173,6 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
   const int n = static_cast<int>(r1 - r0);
   pdl_wait();  // the table, timestep and x may be written by the previous kernel
 
-  // Ada values per column: uniform -> round(table + ts); per token -> the (rounded) table part only
   {
     constexpr bool round_table = !std::is_same<TableT, TsT>::value;
     const TableT* table = static_cast<const TableT*>(a.table);
@@ -152,6 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
       if (UNIFORM) {
         ada_values8<TableT, TsT>(table + a.shift_index * a.table_stride_row + col, ts + a.shift_index * a.ts_stride_p + col, sh);
         ada_values8<TableT, TsT>(table + a.scale_index * a.table_stride_row + col, ts + a.scale_index * a.ts_stride_p + col, sc);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sc[i] = 1.0f + sc[i];
       } else {
         load8<TableT>(table + a.shift_index * a.table_stride_row + col, sh);
         load8<TableT>(table + a.scale_index * a.table_stride_row + col, sc);
@@ -161,8 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
           sc[i] = round_table ? bf16_round(sc[i]) : sc[i];
         }
       }
-      store8<TsT>(ada_shift + col, sh);
-      store8<TsT>(ada_scale + col, sc);
+      store8<float>(ada0 + col, sh);
+      store8<float>(ada1 + col, sc);
     }
   }
   __syncthreads();
@@ -186,36 +219,35 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
     }
   } else {
     constexpr bool round_ada = std::is_same<TsT, __nv_bfloat16>::value;
+    constexpr bool fast_quant = QUANT && QMODE == kQuantTorch;
     float s = 0.f, r = 0.f;
     if (QUANT) {
       s = __ldg(a.input_scale);
       r = __frcp_rn(s);
     }
+    const f2 r2{r, r};
     volatile int* abort = &ring.abort;
     for (int k = static_cast<int>(warp); k < n; k += kConsumerWarps) {
       const int st = k % S;
       if (!mbar_wait(&ring.full[st], (k / S) & 1, abort)) break;
       const uint8_t* stage = stages + static_cast<size_t>(st) * SB;
       const uint4* xs = reinterpret_cast<const uint4*>(stage);
-      float ss = 0.f;
+      f2 acc0{0.f, 0.f}, acc1{0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        float f[8];
-        unpack8(xs[j * 32 + lane], f);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
-      }
-      ss = warp_allsum(ss);
+      for (int j = 0; j < VPL; ++j) sumsq8(xs[j * 32 + lane], acc0, acc1);
+      const float ss = warp_allsum((acc0.x + acc0.y) + (acc1.x + acc1.y));
       const float inv_rms = rsqrtf(ss / static_cast<float>(COLS) + a.eps);
+      const f2 inv2{inv_rms, inv_rms};
       const int64_t row = r0 + k;
 #pragma unroll 4
       for (int j = 0; j < VPL; ++j) {
         const int vec = j * 32 + static_cast<int>(lane);
         const int col = vec * 8;
-        float f[8], sh[8], sc[8], y[8];
-        unpack8(xs[vec], f);
-        load8<TsT>(ada_shift + col, sh);
-        load8<TsT>(ada_scale + col, sc);
+        const uint4 xv = xs[vec];
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+        float sh[8], sc1[8];
+        load8<float>(ada0 + col, sh);
+        load8<float>(ada1 + col, sc1);
         if (!UNIFORM) {
           const TsT* tsh = reinterpret_cast<const TsT*>(stage + COLS * 2);
           const TsT* tsc = tsh + COLS;
@@ -225,16 +257,25 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             sh[i] = round_ada ? bf16_round(sh[i] + a0[i]) : sh[i] + a0[i];
-            sc[i] = round_ada ? bf16_round(sc[i] + a1[i]) : sc[i] + a1[i];
+            const float scv = round_ada ? bf16_round(sc1[i] + a1[i]) : sc1[i] + a1[i];
+            sc1[i] = 1.0f + scv;
           }
         }
+        uint32_t yw[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = fmaf(f[i] * inv_rms, 1.0f + sc[i], sh[i]);
-        const uint4 yv = pack8(y);
-        if (a.y != nullptr) reinterpret_cast<uint4*>(a.y + row * COLS)[vec] = yv;
-        if (QUANT) {
+        for (int i = 0; i < 4; ++i) {
+          // y = (x * inv_rms) * (1 + scale) + shift, one rounding to bf16
+          const f2 y = fma2(mul2(bf16x2_to_f2(xw[i]), inv2), f2{sc1[2 * i], sc1[2 * i + 1]}, f2{sh[2 * i], sh[2 * i + 1]});
+          yw[i] = pack_bf16x2(y.x, y.y);
+        }
+        if (a.y != nullptr) reinterpret_cast<uint4*>(a.y + row * COLS)[vec] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+        if (fast_quant) {
+          const uint32_t lo = quant2_torch(bf16x2_to_f2(yw[0]), r2) | (quant2_torch(bf16x2_to_f2(yw[1]), r2) << 16);
+          const uint32_t hi = quant2_torch(bf16x2_to_f2(yw[2]), r2) | (quant2_torch(bf16x2_to_f2(yw[3]), r2) << 16);
+          reinterpret_cast<uint2*>(a.q + row * COLS)[vec] = make_uint2(nan_bytes_to_ff(lo), nan_bytes_to_ff(hi));
+        } else if (QUANT) {
           float yb[8];
-          unpack8(yv, yb);
+          unpack8(make_uint4(yw[0], yw[1], yw[2], yw[3]), yb);
           reinterpret_cast<uint2*>(a.q + row * COLS)[vec] = quant8<__nv_bfloat16, QMODE>(yb, s, r);
         }
       }
@@ -264,67 +305,72 @@ struct RopeSource {
 
 constexpr int kRopeSlots = 2048;  // 32 heads x 64 rotary frequencies
 constexpr int kRopePairs = 256;   // 32 heads x 8 eight-column half-blocks
-// shared memory ahead of the ring: Q and K weights (bf16 or fp32) and the frequency table
-// (per pair: 8 (hi, lo) turn frequencies laid out [8][256] so a warp's lanes read consecutive words,
-// and the 8 axes packed 2 bits each)
-template <typename WT>
+// shared memory ahead of the ring: Q and K weights as fp32 and the frequency table (per pair p and angle
+// pair k = e / 2 of its 8 angles: (hi, hi, lo, lo) of angles 2k and 2k + 1, laid out [4][256] so a warp's
+// lanes read consecutive 16-byte words; then the 8 position axes of each pair packed 2 bits each)
 struct RopeLayout {
-  static constexpr int kWeights = 2 * 4096 * static_cast<int>(sizeof(WT));
-  static constexpr int kFreq = 8 * kRopePairs * 8 + kRopePairs * 4;
+  static constexpr int kWeights = 2 * 4096 * 4;
+  static constexpr int kFreq = 4 * kRopePairs * 16 + kRopePairs * 4;
   static constexpr int kFixed = kWeights + kFreq;
   __host__ __device__ static constexpr int stage_bytes(bool copy_v) { return (copy_v ? 3 : 2) * 4096 * 2; }
   __host__ __device__ static constexpr int stages(bool copy_v) {
-    return ((kDynLimit - kFixed) / stage_bytes(copy_v)) > 16 ? 16 : ((kDynLimit - kFixed) / stage_bytes(copy_v));
+    return ((kDynLimit - kFixed) / stage_bytes(copy_v)) > kMaxStages ? kMaxStages : ((kDynLimit - kFixed) / stage_bytes(copy_v));
   }
   __host__ __device__ static constexpr int smem_bytes(bool copy_v) { return kFixed + stages(copy_v) * stage_bytes(copy_v); }
 };
 
-// cos and sin (bf16-rounded, as fp32) of position * inverse frequency, the frequency given in turns as
-// hi + lo with hi holding at most 16 significant bits: pos * hi is exact for integer positions below 2^8,
-// its fractional part is exact, and lo adds the rest, so the reduced angle rt is within a few 2^-24 turns.
-// Then the quadrant q = rint(4 rt) leaves x = 2 pi (rt - q / 4) in [-pi/4, pi/4], where the Taylor series
+// Two angles at once: cos and sin (bf16-rounded, as fp32) of pos * inverse frequency, the frequency given in
+// turns as hi + lo with hi holding at most 16 significant bits: pos * hi is exact for integer positions below
+// 2^8, its fractional part is exact, and lo adds the rest, so the reduced angle rt is within a few 2^-24
+// turns.  The quadrant q = rint(4 rt) leaves x = 2 pi (rt - q / 4) in [-pi/4, pi/4], where the Taylor series
 // of sin to x^9 and of cos to x^10 are within 2e-10 (the next terms' size at pi/4), so cos and sin come out
-// within a few fp32 ulps, relative to the value for small angles too; cos(x + q pi/2), sin(x + q pi/2) by
+// within a few fp32 ulps, relative to the value for small angles too; cos(x + q pi/2) and sin(x + q pi/2) by
 // swapping and negating.
-__device__ __forceinline__ void rope_cos_sin(float pos, float hi, float lo, float& c, float& s) {
-  const float a = pos * hi;
-  const float rt = fmaf(pos, lo, a - rintf(a));  // turns, in [-1/2, 1/2] up to rounding
-  const float qf = rintf(rt * 4.0f);             // quadrant, -2..2
-  const float x = fmaf(qf, -0.25f, rt) * 6.28318530717958647692f;
-  const float x2 = x * x;
+__device__ __forceinline__ void rope_cos_sin2(f2 pos, f2 hi, f2 lo, f2& c, f2& s) {
+  const f2 a = mul2(pos, hi);
+  const f2 rt = fma2(pos, lo, sub2(a, f2{rintf(a.x), rintf(a.y)}));  // turns, in [-1/2, 1/2] up to rounding
+  const f2 r4 = mul2(rt, f2{4.0f, 4.0f});
+  const f2 qf{rintf(r4.x), rintf(r4.y)};  // quadrants, -2..2
+  const f2 x = mul2(fma2(qf, f2{-0.25f, -0.25f}, rt), f2{6.28318530717958647692f, 6.28318530717958647692f});
+  const f2 x2 = mul2(x, x);
   // Taylor coefficients: 1/9!, -1/7!, 1/5!, -1/3!  and  -1/10!, 1/8!, -1/6!, 1/4!, -1/2
-  float ps = fmaf(x2, 2.75573192e-6f, -1.98412698e-4f);
-  ps = fmaf(x2, ps, 8.33333333e-3f);
-  ps = fmaf(x2, ps, -1.66666667e-1f);
-  const float sn = fmaf(x * x2, ps, x);
-  float pc = fmaf(x2, -2.75573192e-7f, 2.48015873e-5f);
-  pc = fmaf(x2, pc, -1.38888889e-3f);
-  pc = fmaf(x2, pc, 4.16666667e-2f);
-  pc = fmaf(x2, pc, -0.5f);
-  const float cs = fmaf(x2, pc, 1.0f);
-  const int q = static_cast<int>(qf);
-  const float c0 = (q & 1) ? sn : cs;
-  const float s0 = (q & 1) ? cs : sn;
-  float cv = ((q + 1) & 2) ? -c0 : c0;
-  float sv = (q & 2) ? -s0 : s0;
-  bf16_round2(cv, sv);
-  c = cv;
-  s = sv;
+  f2 ps = fma2(x2, f2{2.75573192e-6f, 2.75573192e-6f}, f2{-1.98412698e-4f, -1.98412698e-4f});
+  ps = fma2(x2, ps, f2{8.33333333e-3f, 8.33333333e-3f});
+  ps = fma2(x2, ps, f2{-1.66666667e-1f, -1.66666667e-1f});
+  const f2 sn = fma2(mul2(x, x2), ps, x);
+  f2 pc = fma2(x2, f2{-2.75573192e-7f, -2.75573192e-7f}, f2{2.48015873e-5f, 2.48015873e-5f});
+  pc = fma2(x2, pc, f2{-1.38888889e-3f, -1.38888889e-3f});
+  pc = fma2(x2, pc, f2{4.16666667e-2f, 4.16666667e-2f});
+  pc = fma2(x2, pc, f2{-0.5f, -0.5f});
+  const f2 cs = fma2(x2, pc, f2{1.0f, 1.0f});
+  const int q0 = static_cast<int>(qf.x), q1 = static_cast<int>(qf.y);
+  // odd quadrants swap cos and sin; cos is negated in quadrants 1 and 2, sin in 2 and 3 (= -1 and -2)
+  float c0 = (q0 & 1) ? sn.x : cs.x, s0 = (q0 & 1) ? cs.x : sn.x;
+  float c1 = (q1 & 1) ? sn.y : cs.y, s1 = (q1 & 1) ? cs.y : sn.y;
+  c0 = __uint_as_float(__float_as_uint(c0) ^ ((static_cast<uint32_t>(q0 + 1) & 2u) << 30));
+  c1 = __uint_as_float(__float_as_uint(c1) ^ ((static_cast<uint32_t>(q1 + 1) & 2u) << 30));
+  s0 = __uint_as_float(__float_as_uint(s0) ^ ((static_cast<uint32_t>(q0) & 2u) << 30));
+  s1 = __uint_as_float(__float_as_uint(s1) ^ ((static_cast<uint32_t>(q1) & 2u) << 30));
+  c = bf16x2_to_f2(pack_bf16x2(c0, c1));
+  s = bf16x2_to_f2(pack_bf16x2(s0, s1));
 }
 
-// Splits inv_freq / 2pi (turns per position unit) into the (hi, lo) pair rope_cos_sin expects.
+// Splits inv_freq / 2pi (turns per position unit) into the (hi, lo) pair rope_cos_sin2 expects.
 __device__ __forceinline__ float2 turns_split(double inv_freq) {
   const double t = inv_freq * 0.15915494309189533577;  // 1 / (2 pi)
   const float hi = __uint_as_float(__float_as_uint(static_cast<float>(t)) & 0xFFFFFF00u);
   return make_float2(hi, static_cast<float>(t - static_cast<double>(hi)));
 }
 
-// Fills the frequency table of this CTA: fr[e][p] = turns of slot 64 * (p / 8) + 8 * (p % 8) + e, ax[p] the
-// packed axes.
-__device__ __forceinline__ void rope_freq_table(const RopeSource& src, float2* fr, uint32_t* ax) {
-  for (int i = threadIdx.x; i < kRopeSlots; i += blockDim.x) {
-    const int p = i >> 3, e = i & 7;  // slot i = 64 * head + j, j = 8 * (p % 8) + e  ->  p = i / 8
-    fr[e * kRopePairs + p] = turns_split(src.inv_freq[i]);
+// Fills the frequency table of this CTA: fr[k][p] = (hi, hi, lo, lo) of slots 8 p + 2 k and 8 p + 2 k + 1
+// (slot 64 * head + j with j = 8 * (p % 8) + e, so slot = 8 p + e), ax[p] the packed axes of slots 8 p ..
+// 8 p + 7.
+__device__ __forceinline__ void rope_freq_table(const RopeSource& src, float4* fr, uint32_t* ax) {
+  for (int i = threadIdx.x; i < kRopeSlots / 2; i += blockDim.x) {
+    const int p = i >> 2, k = i & 3;
+    const float2 f0 = turns_split(src.inv_freq[p * 8 + 2 * k]);
+    const float2 f1 = turns_split(src.inv_freq[p * 8 + 2 * k + 1]);
+    fr[k * kRopePairs + p] = make_float4(f0.x, f1.x, f0.y, f1.y);
   }
   for (int p = threadIdx.x; p < kRopePairs; p += blockDim.x) {
     uint32_t packed = 0;
@@ -345,20 +391,59 @@ __device__ __forceinline__ void token_position(const RopeSource& src, int64_t lo
   pos[2] = static_cast<float>(rem - h * src.grid_w);
 }
 
+__device__ __forceinline__ float axis_pos(const float (&pos)[3], uint32_t axe) {
+  return axe == 0 ? pos[0] : (axe == 1 ? pos[1] : pos[2]);
+}
+
+// The 8 cos/sin of pair p for a token at `pos` (generated), as 4 packed pairs each.
+__device__ __forceinline__ void pair_cos_sin_gen(const float4* fr, const uint32_t* ax, int p, const float (&pos)[3],
+                                                 f2 (&c)[4], f2 (&s)[4]) {
+  const uint32_t axes = ax[p];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 f = fr[k * kRopePairs + p];
+    const f2 ps{axis_pos(pos, (axes >> (4 * k)) & 3u), axis_pos(pos, (axes >> (4 * k + 2)) & 3u)};
+    rope_cos_sin2(ps, f2{f.x, f.y}, f2{f.z, f.w}, c[k], s[k]);
+  }
+}
+
+// Normalises, weights and rotates the 16 columns of pair p of one tensor's staged row and stores them.
+__device__ __forceinline__ void rope_pair(const uint4* row, const float* w, int c0, f2 inv2, const f2 (&c)[4],
+                                          const f2 (&s)[4], __nv_bfloat16* dst) {
+  const uint4 x0 = row[c0 / 8], x1 = row[c0 / 8 + 8];
+  const uint32_t w0[4] = {x0.x, x0.y, x0.z, x0.w}, w1[4] = {x1.x, x1.y, x1.z, x1.w};
+  const float4* wv = reinterpret_cast<const float4*>(w + c0);
+  const float4 wa0 = wv[0], wa1 = wv[1], wb0 = wv[16], wb1 = wv[17];  // columns c0..c0+7 and c0+64..c0+71
+  const f2 ww0[4] = {f2{wa0.x, wa0.y}, f2{wa0.z, wa0.w}, f2{wa1.x, wa1.y}, f2{wa1.z, wa1.w}};
+  const f2 ww1[4] = {f2{wb0.x, wb0.y}, f2{wb0.z, wb0.w}, f2{wb1.x, wb1.y}, f2{wb1.z, wb1.w}};
+  uint32_t o0[4], o1[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const f2 n0 = mul2(mul2(bf16x2_to_f2(w0[k]), inv2), ww0[k]);  // (x * inv_rms) * w
+    const f2 n1 = mul2(mul2(bf16x2_to_f2(w1[k]), inv2), ww1[k]);
+    // o[j] = n[j] cos - n[j+64] sin,  o[j+64] = n[j+64] cos + n[j] sin
+    const f2 a = fma2(n0, c[k], mul2(n1, f2{-s[k].x, -s[k].y}));
+    const f2 b = fma2(n1, c[k], mul2(n0, s[k]));
+    o0[k] = pack_bf16x2(a.x, a.y);
+    o1[k] = pack_bf16x2(b.x, b.y);
+  }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+  *reinterpret_cast<uint4*>(dst + 64) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+}
+
 template <typename WT, typename CsT, bool GEN, bool COPY_V>
 __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeArgs a, RopeSource src) {
   pdl_trigger();
-  using Lay = RopeLayout<WT>;
-  constexpr int S = Lay::stages(COPY_V);
-  constexpr uint32_t SB = Lay::stage_bytes(COPY_V);
+  constexpr int S = RopeLayout::stages(COPY_V);
+  constexpr uint32_t SB = RopeLayout::stage_bytes(COPY_V);
   extern __shared__ uint8_t smem_raw[];
   __shared__ Ring ring;
   uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 127u) & ~127u) - smem_u32(smem_raw));
-  WT* wq = reinterpret_cast<WT*>(smem);
-  WT* wk = wq + 4096;
-  float2* fr = reinterpret_cast<float2*>(smem + Lay::kWeights);
-  uint32_t* ax = reinterpret_cast<uint32_t*>(fr + 8 * kRopePairs);
-  uint8_t* stages = smem + Lay::kFixed;
+  float* wq = reinterpret_cast<float*>(smem);
+  float* wk = wq + 4096;
+  float4* fr = reinterpret_cast<float4*>(smem + RopeLayout::kWeights);
+  uint32_t* ax = reinterpret_cast<uint32_t*>(fr + 4 * kRopePairs);
+  uint8_t* stages = smem + RopeLayout::kFixed;
   ring_init(ring, S);
   int64_t r0, r1;
   cta_rows(a.tokens, r0, r1);
@@ -367,9 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeA
   for (int i = threadIdx.x; i < 4096 / 8; i += blockDim.x) {
     float f[8];
     load8<WT>(static_cast<const WT*>(a.q_weight) + i * 8, f);
-    store8<WT>(wq + i * 8, f);
+    store8<float>(wq + i * 8, f);
     load8<WT>(static_cast<const WT*>(a.k_weight) + i * 8, f);
-    store8<WT>(wk + i * 8, f);
+    store8<float>(wk + i * 8, f);
   }
   if (GEN) rope_freq_table(src, fr, ax);
   __syncthreads();
@@ -395,71 +480,43 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeA
       const uint8_t* stage = stages + static_cast<size_t>(st) * SB;
       const uint4* rq = reinterpret_cast<const uint4*>(stage);
       const uint4* rk = rq + 512;
-      float sq = 0.f, sk = 0.f;
-#pragma unroll 4
+      f2 aq0{0.f, 0.f}, aq1{0.f, 0.f}, ak0{0.f, 0.f}, ak1{0.f, 0.f};
+#pragma unroll 8
       for (int j = 0; j < 16; ++j) {
-        float f[8], g[8];
-        unpack8(rq[j * 32 + lane], f);
-        unpack8(rk[j * 32 + lane], g);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          sq = fmaf(f[i], f[i], sq);
-          sk = fmaf(g[i], g[i], sk);
-        }
+        sumsq8(rq[j * 32 + lane], aq0, aq1);
+        sumsq8(rk[j * 32 + lane], ak0, ak1);
       }
-      sq = warp_allsum(sq);
-      sk = warp_allsum(sk);
+      const float sq = warp_allsum((aq0.x + aq0.y) + (aq1.x + aq1.y));
+      const float sk = warp_allsum((ak0.x + ak0.y) + (ak1.x + ak1.y));
       const float inv_q = rsqrtf(sq / 4096.f + a.eps);
       const float inv_k = rsqrtf(sk / 4096.f + a.eps);
       const int64_t t = r0 + k;
       float pos[3] = {0.f, 0.f, 0.f};
       if (GEN) token_position(src, t, pos);
-#pragma unroll 1
+#pragma unroll 2
       for (int i = 0; i < 8; ++i) {
         const int p = i * 32 + static_cast<int>(lane);  // pair: head p / 8, columns 8 * (p % 8) + [0, 8) (+ 64)
         const int head = p >> 3;
         const int c0 = head * 128 + (p & 7) * 8;
-        float c[8], s[8];
+        f2 c[4], s[4];
         if (GEN) {
-          const uint32_t axes = ax[p];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const uint32_t axe = (axes >> (2 * e)) & 3u;
-            const float ps = axe == 0 ? pos[0] : (axe == 1 ? pos[1] : pos[2]);
-            const float2 f = fr[e * kRopePairs + p];
-            rope_cos_sin(ps, f.x, f.y, c[e], s[e]);
-          }
+          pair_cos_sin_gen(fr, ax, p, pos, c, s);
         } else {
           const int64_t off = head * a.cs_stride_h + t * a.cs_stride_t + (p & 7) * 8;
-          load8<CsT>(cosb + off, c);
-          load8<CsT>(sinb + off, s);
+          float cf[8], sf[8];
+          load8<CsT>(cosb + off, cf);
+          load8<CsT>(sinb + off, sf);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            c[e] = f2{cf[2 * e], cf[2 * e + 1]};
+            s[e] = f2{sf[2 * e], sf[2 * e + 1]};
+          }
         }
         const int g = head / a.heads_per_group;
         const int hl = head - g * a.heads_per_group;
-#pragma unroll
-        for (int which = 0; which < 2; ++which) {
-          const uint4* rr = which ? rk : rq;
-          const WT* w = which ? wk : wq;
-          const float inv = which ? inv_k : inv_q;
-          float x0[8], x1[8], w0[8], w1[8], n0[8], n1[8], o0[8], o1[8];
-          unpack8(rr[c0 / 8], x0);
-          unpack8(rr[c0 / 8 + 8], x1);
-          load8<WT>(w + c0, w0);
-          load8<WT>(w + c0 + 64, w1);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            n0[e] = x0[e] * inv * w0[e];
-            n1[e] = x1[e] * inv * w1[e];
-          }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            o0[e] = fmaf(n0[e], c[e], -(n1[e] * s[e]));
-            o1[e] = fmaf(n1[e], c[e], n0[e] * s[e]);
-          }
-          __nv_bfloat16* dst = group_base(a.dst[which], g) + t * a.out_stride_t + hl * 128 + (p & 7) * 8;
-          *reinterpret_cast<uint4*>(dst) = pack8(o0);
-          *reinterpret_cast<uint4*>(dst + 64) = pack8(o1);
-        }
+        const int64_t o = t * a.out_stride_t + hl * 128 + (p & 7) * 8;
+        rope_pair(rq, wq, c0, f2{inv_q, inv_q}, c, s, group_base(a.dst[0], g) + o);
+        rope_pair(rk, wk, c0, f2{inv_k, inv_k}, c, s, group_base(a.dst[1], g) + o);
       }
       if (COPY_V) {
         const uint4* rv = rq + 1024;
@@ -484,8 +541,89 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeA
   }
 }
 
+// ------------------------------------------------------------------------------------- Q/K RMSNorm only
+// RmsRowsArgs rows through the ring: a warp per row, the RoPE kernel's sum of squares and normalisation
+// ((x * inv_rms) * w, one bf16 rounding); the row is staged whole before its first store, so the output
+// may alias the input.
+constexpr int kRmsFixed = 2 * 4096 * 4;  // Q and K weights as fp32
+constexpr int kRmsStages = ((kDynLimit - kRmsFixed) / 8192) > kMaxStages ? kMaxStages : ((kDynLimit - kRmsFixed) / 8192);
+constexpr int kRmsSmem = kRmsFixed + kRmsStages * 8192;
+
+template <typename WT>
+__global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_ring_kernel(RmsRowsArgs a) {
+  pdl_trigger();
+  constexpr int S = kRmsStages;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ Ring ring;
+  uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 127u) & ~127u) - smem_u32(smem_raw));
+  float* wq = reinterpret_cast<float*>(smem);
+  float* wk = wq + 4096;
+  uint8_t* stages = smem + kRmsFixed;
+  ring_init(ring, S);
+  int64_t r0, r1;
+  cta_rows(a.rows, r0, r1);
+  const int n = static_cast<int>(r1 - r0);
+  pdl_wait();
+  for (int i = threadIdx.x; i < 4096 / 8; i += blockDim.x) {
+    float f[8];
+    load8<WT>(static_cast<const WT*>(a.weight[0]) + i * 8, f);
+    store8<float>(wq + i * 8, f);
+    load8<WT>(static_cast<const WT*>(a.weight[1]) + i * 8, f);
+    store8<float>(wk + i * 8, f);
+  }
+  __syncthreads();
+  const uint32_t warp = warp_idx();
+  const uint32_t lane = threadIdx.x & 31;
+  if (warp == kConsumerWarps) {
+    if (elect_one()) {
+      ring_produce(ring, stages, S, 8192u, n, 8192u, [&](int k, uint8_t* st, uint64_t* bar) {
+        const int64_t r = r0 + k;
+        // selects, not a.in[j]: a runtime index into the parameter arrays would copy them to local memory
+        const bool is_k = r >= a.rows_q;
+        const int64_t t = is_k ? r - a.rows_q : r;
+        bulk_load(st, (is_k ? a.in[1] : a.in[0]) + t * (is_k ? a.in_stride[1] : a.in_stride[0]), 8192, bar);
+      });
+    }
+  } else {
+    volatile int* abort = &ring.abort;
+    for (int k = static_cast<int>(warp); k < n; k += kConsumerWarps) {
+      const int st = k % S;
+      if (!mbar_wait(&ring.full[st], (k / S) & 1, abort)) break;
+      const uint4* row = reinterpret_cast<const uint4*>(stages + static_cast<size_t>(st) * 8192);
+      f2 a0{0.f, 0.f}, a1{0.f, 0.f};
+#pragma unroll 8
+      for (int j = 0; j < 16; ++j) sumsq8(row[j * 32 + lane], a0, a1);
+      const float ss = warp_allsum((a0.x + a0.y) + (a1.x + a1.y));
+      const f2 inv2{rsqrtf(ss / 4096.f + a.eps), rsqrtf(ss / 4096.f + a.eps)};
+      const int64_t r = r0 + k;
+      const bool is_k = r >= a.rows_q;
+      const int64_t t = is_k ? r - a.rows_q : r;
+      __nv_bfloat16* out = (is_k ? a.out[1] : a.out[0]) + t * (is_k ? a.out_stride[1] : a.out_stride[0]);
+      const float* w = is_k ? wk : wq;
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {
+        const int vec = j * 32 + static_cast<int>(lane);
+        const uint4 xv = row[vec];
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+        const float4 wa = reinterpret_cast<const float4*>(w + vec * 8)[0];
+        const float4 wb = reinterpret_cast<const float4*>(w + vec * 8)[1];
+        const f2 ww[4] = {f2{wa.x, wa.y}, f2{wa.z, wa.w}, f2{wb.x, wb.y}, f2{wb.z, wb.w}};
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const f2 nv = mul2(mul2(bf16x2_to_f2(xw[i]), inv2), ww[i]);
+          o[i] = pack_bf16x2(nv.x, nv.y);
+        }
+        reinterpret_cast<uint4*>(out)[vec] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ring.empty[st]);
+    }
+  }
+}
+
 // The cos/sin the generating RoPE kernel uses, written as [32, tokens, 64] tables (same element order as the
-// reference's tables): one thread per (head, token, 8 columns).
+// reference's tables): one thread per (head, token, 8 columns), the same arithmetic as the kernel.
 template <typename CsT>
 __global__ void __launch_bounds__(256) rope_tables_kernel(RopeSource src, int64_t tokens, CsT* cos_out, CsT* sin_out) {
   const int64_t total = 32 * tokens * 8;
@@ -499,11 +637,16 @@ __global__ void __launch_bounds__(256) rope_tables_kernel(RopeSource src, int64_
     token_position(src, t, pos);
     float c[8], s[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int slot = head * 64 + pv * 8 + e;
-      const float2 f = turns_split(src.inv_freq[slot]);
-      const uint32_t axe = src.slot_axis[slot] & 3u;
-      rope_cos_sin(axe == 0 ? pos[0] : (axe == 1 ? pos[1] : pos[2]), f.x, f.y, c[e], s[e]);
+    for (int k = 0; k < 4; ++k) {
+      const int slot = head * 64 + pv * 8 + 2 * k;
+      const float2 f0 = turns_split(src.inv_freq[slot]), f1 = turns_split(src.inv_freq[slot + 1]);
+      const f2 ps{axis_pos(pos, src.slot_axis[slot] & 3u), axis_pos(pos, src.slot_axis[slot + 1] & 3u)};
+      f2 cc, ss;
+      rope_cos_sin2(ps, f2{f0.x, f1.x}, f2{f0.y, f1.y}, cc, ss);
+      c[2 * k] = cc.x;
+      c[2 * k + 1] = cc.y;
+      s[2 * k] = ss.x;
+      s[2 * k + 1] = ss.y;
     }
     store8<CsT>(cos_out + ht * 64 + pv * 8, c);
     store8<CsT>(sin_out + ht * 64 + pv * 8, s);

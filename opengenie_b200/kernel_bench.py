@@ -149,7 +149,7 @@ def bench_qk_rmsnorm(a) -> dict:
     fn = lambda: ltx_ops.fused_qk_rmsnorm(q, k, qw, kw, 1e-6, out=(q, k))  # noqa: E731
     ms = _time(fn, a.steps, a.warmup)
     nbytes = (a.tokens + L_kv) * 4096 * 2 * 2  # rows read + written
-    return {"kernel": "qk_rmsnorm_rows_kernel", "tokens": a.tokens, "kv_tokens": L_kv, "ms": ms,
+    return {"kernel": "qk_rmsnorm_ring_kernel", "tokens": a.tokens, "kv_tokens": L_kv, "ms": ms,
             "gbs": nbytes / (ms * 1e-3) / 1e9}
 
 

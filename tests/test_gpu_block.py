@@ -152,7 +152,10 @@ def _epilogue_fp32_from_codes(oq, w, x, ts_view):
     y = r16((a @ wf.T) * s)
     absdot = (a.abs() @ wf.abs().T) * s
     table = w.scale_shift_table.float()
-    gate = r16(table[2].view(1, -1) + ts_view[0, :, 2, :].float())
+    if (w.scale_shift_table.dtype == torch.bfloat16) != (ts_view.dtype == torch.bfloat16):
+        table = r16(table)  # table.to(ts.dtype), as the reference's Ada values round it
+    gate = table[2].view(1, -1) + ts_view[0, :, 2, :].float()
+    gate = r16(gate) if ts_view.dtype == torch.bfloat16 else gate
     yb = r16(y + r16(w.to_out.bias.float()))
     prod = r16(yb * gate)
     ref = r16(x.reshape(-1, x.shape[-1]).float() + prod)
@@ -160,7 +163,9 @@ def _epilogue_fp32_from_codes(oq, w, x, ts_view):
     def ulp(t):
         return torch.exp2(torch.floor(torch.log2(t.abs().clamp_min(2.0 ** -126))) - 7.0)
 
-    bound = gate.abs() * (ulp(y) + ulp(yb) + 2.0 ** -17 * absdot) + ulp(prod) + ulp(ref)
+    # each rounding may land one bf16 ulp (of the larger of the two sides' values) away; the accumulation
+    # order of 4096 fp32 products moves y by at most ~2^-17 of sum |products|
+    bound = gate.abs() * (2 * ulp(y) + 2 * ulp(yb) + 2.0 ** -17 * absdot) + 2 * ulp(prod) + 2 * ulp(ref)
     return ref.view(x.shape), bound.view(x.shape)
 
 
