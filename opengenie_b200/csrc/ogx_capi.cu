@@ -819,6 +819,17 @@ int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::P
   return check_launch("fp8_gemm_kernel");
 }
 
+// The attention kernel: the single-CTA kernel with 64-key tiles (the default, the faster of the two on
+// B200 at L=9216), or CTA pairs (attn_fwd_pair_kernel, 128-key tiles, M=256 MMAs over two SMs) when
+// OGX_ATTN_PAIRS=1 is set in the environment.
+bool attn_use_pairs() {
+  static const bool on = [] {
+    const char* e = std::getenv("OGX_ATTN_PAIRS");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+
 int attention_common(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens, int64_t kv_tokens,
                      int64_t heads, int64_t head_dim, int64_t stride_b, int64_t stride_t, int64_t kv_stride_b,
                      int64_t kv_stride_t, CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv) {
@@ -836,17 +847,29 @@ int attention_common(const void* q, const void* k, const void* v, int64_t batch,
                               static_cast<uint64_t>(batch)};
   const uint64_t kvstrides[3] = {256, static_cast<uint64_t>(kv_stride_t) * 2, static_cast<uint64_t>(kv_stride_b) * 2};
   const uint32_t qbox[4] = {64, 1, static_cast<uint32_t>(ogx::attn::BQ), 1};
-  const uint32_t kvbox[4] = {64, 1, static_cast<uint32_t>(ogx::attn::BKV), 1};
+  // single CTA: K and V tiles of 64 keys; pairs: each CTA loads 64 keys of K and 128 keys of its V columns
+  const uint32_t kbox[4] = {64, 1, 64u, 1};
+  const uint32_t vbox[4] = {64, 1, attn_use_pairs() ? static_cast<uint32_t>(ogx::attn::PBKV) : 64u, 1};
   int rc = make_map(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, q, qdims, qstrides, qbox);
   if (rc) return rc;
-  rc = make_map(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k, kvdims, kvstrides, kvbox);
+  rc = make_map(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, k, kvdims, kvstrides, kbox);
   if (rc) return rc;
-  return make_map(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v, kvdims, kvstrides, kvbox);
+  return make_map(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, v, kvdims, kvstrides, vbox);
 }
 
 template <bool E4M3>
 int attention_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int64_t batch,
                      int64_t tokens, int64_t heads, const ogx::attn::Params& p, cudaStream_t s) {
+  if (attn_use_pairs()) {
+    auto kern = ogx::attn::attn_fwd_pair_kernel<E4M3>;
+    int rc = ensure_smem(kern, ogx::attn::PAIR_SMEM_BYTES);
+    if (rc) return rc;
+    // one pair of CTAs (a cluster of two) per 256 queries and head
+    const dim3 grid(static_cast<unsigned>(2 * ((tokens + 255) / 256)), static_cast<unsigned>(heads),
+                    static_cast<unsigned>(batch));
+    launch_cluster(kern, grid, dim3(ogx::attn::kPairThreads), ogx::attn::PAIR_SMEM_BYTES, s, 2u, mq, mk, mv, p);
+    return check_launch("attn_fwd_pair_kernel");
+  }
   auto kern = ogx::attn::attn_fwd_kernel<E4M3>;
   int rc = ensure_smem(kern, ogx::attn::SMEM_BYTES);
   if (rc) return rc;

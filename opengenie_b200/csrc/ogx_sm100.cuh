@@ -182,6 +182,20 @@ __device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const void* map
       "l"(map), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_4d_pair(void* smem_dst, const void* map, uint32_t bar_cluster, int32_t x,
+                                                 int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(bar_cluster), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+// Arrival on a barrier of the peer CTA with the default (CTA-scope) release: the form cluster pipelines use
+// for a consumer's per-stage signal, without the cluster-scope fence of mbar_arrive_remote.  The data it
+// orders here is tensor memory, ordered by tcgen05 fences around the barrier, not by the release.
+__device__ __forceinline__ void mbar_arrive_peer(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
 // TMEM of both CTAs, allocated and freed together by the same warp of each CTA.
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
@@ -203,6 +217,26 @@ __device__ __forceinline__ void mma_f8_ss_pair(uint32_t d_tmem, uint64_t a_desc,
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D (both CTAs' TMEM, M = 256) (+)= A (both CTAs' shared memory) * B^T (N split over the two CTAs), bf16.
+__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D (both CTAs' TMEM, M = 256) (+)= A (both CTAs' TMEM, each its 128 rows) * B (N split over the two CTAs), bf16.
+__device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // Arrive on the barrier at shared::cluster address `bar_cluster` (either CTA) once the pair MMAs issued

@@ -28,3 +28,28 @@ class StepGraph:
 
     def replay(self) -> None:
         self.graph.replay()
+
+
+def time_launches(fn: Callable[[], object], steps: int, warmup: int, device) -> float:
+    """Average device time (ms) of one ``fn()``: ``steps`` calls captured in one CUDA graph and replayed between
+    two CUDA events on the current stream, after ``warmup`` eager calls and one untimed replay, so host
+    overhead does not add to short launches."""
+    device = torch.device(device)
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        for _ in range(steps):
+            fn()
+    graph.replay()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    del graph
+    return e0.elapsed_time(e1) / steps
+

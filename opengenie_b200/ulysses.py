@@ -356,23 +356,18 @@ class UlyssesVideoSelfAttention:
         w.to_out.input_scale = (amax.clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
 
     def time_attention(self, steps: int, warmup: int = 3) -> float:
-        """Average device time (ms) of this rank's attention kernel (H/P heads over all L tokens)."""
+        """Average device time (ms) of this rank's attention kernel (H/P heads over all L tokens), launches
+        replayed from one CUDA graph."""
+        from .graphs import time_launches
+
         Ll = max(self._ws)
         ws = self._ws[Ll]
         L = Ll * self.plan.world
         q, k, v = self.plan.attention_views(ws["recv1"], L)
         out = ws["send2"].view(1, L, -1)
-        for _ in range(warmup):
-            ltx_ops.attention(q, k, v, self.plan.heads_local, out=out, out_e4m3_scale=self.w.to_out.input_scale)
-        stream = torch.cuda.current_stream(self.device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize(self.device)
-        e0.record(stream)
-        for _ in range(steps):
-            ltx_ops.attention(q, k, v, self.plan.heads_local, out=out, out_e4m3_scale=self.w.to_out.input_scale)
-        e1.record(stream)
-        torch.cuda.synchronize(self.device)
-        return e0.elapsed_time(e1) / steps
+        return time_launches(
+            lambda: ltx_ops.attention(q, k, v, self.plan.heads_local, out=out, out_e4m3_scale=self.w.to_out.input_scale),
+            steps, warmup, self.device)
 
 
 __all__ = ["UlyssesPlan", "UlyssesVideoSelfAttention", "DTYPE_BF16"]

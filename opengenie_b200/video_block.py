@@ -140,8 +140,10 @@ class VideoSelfAttentionBlock:
         return ltx_ops.fused_head_gate_mul_bf16(ltx_ops.attention(q, k, v, self.heads), gates, self.heads, 128)
 
     def time_attention(self, steps: int, warmup: int = 3, tokens: int | None = None) -> float:
-        """Average device time (ms) of the attention kernel alone on the current stream,
-        over the Q/K/V the last forward left in the workspace."""
+        """Average device time (ms) of the attention kernel alone (launches replayed from one CUDA graph on the
+        current stream) over the Q/K/V the last forward left in the workspace."""
+        from .graphs import time_launches
+
         if tokens is None:
             tokens = max(self._ws)
         ws = self.workspace(tokens)
@@ -149,17 +151,9 @@ class VideoSelfAttentionBlock:
         qkv = ws["qkv"]
         q, k, v = (qkv[:, i * D:(i + 1) * D].unsqueeze(0) for i in range(3))
         out = torch.empty((1, tokens, D), device=self.device, dtype=torch.float8_e4m3fn)
-        for _ in range(warmup):
-            ltx_ops.attention(q, k, v, self.heads, out=out, out_e4m3_scale=self.w.to_out.input_scale)
-        stream = torch.cuda.current_stream(self.device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize(self.device)
-        e0.record(stream)
-        for _ in range(steps):
-            ltx_ops.attention(q, k, v, self.heads, out=out, out_e4m3_scale=self.w.to_out.input_scale)
-        e1.record(stream)
-        torch.cuda.synchronize(self.device)
-        return e0.elapsed_time(e1) / steps
+        return time_launches(
+            lambda: ltx_ops.attention(q, k, v, self.heads, out=out, out_e4m3_scale=self.w.to_out.input_scale),
+            steps, warmup, self.device)
 
     # ------------------------------------------------------------------ calibration
     @torch.no_grad()
