@@ -257,18 +257,27 @@ def cpu_reference_branch(args, budget_s: float = REF_BUDGET_S) -> dict:
         flops, metric, what = text_flops(L, L_ctx), TEXT_METRIC, f"text cross-attention branch ({L_ctx} context tokens)"
         workload = f"LTX-2.3 video text cross-attention branch, {args.config}"
     else:  # layers: one layer's video branches, scaled by the layer count
-        inp = synthetic.make_inputs(cfg, seed=1)
+        L_ctx = args.context_tokens
+        inp = synthetic.make_layer_inputs(cfg, L_ctx, seed=1)
         w, fw = synthetic.make_weights(seed=100), synthetic.make_ffn_weights(seed=200)
-        ts_view = inp.timestep.reshape(1, L, 6, 4096)
+        tw = synthetic.make_text_attention_weights(seed=300)
+        table = torch.cat([w.scale_shift_table[0:3], fw.scale_shift_table[3:6], tw.scale_shift_table[6:9]]).float()
+        w.scale_shift_table = fw.scale_shift_table = tw.scale_shift_table = table  # the layer's one 9-slot table
+        ts_view = inp.timestep.reshape(1, L, 9, 4096)
+        pts_view = inp.prompt_timestep.reshape(1, L_ctx, 2, 4096)
         with torch.no_grad():
             y0 = O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w, calibrate=True).to(torch.bfloat16)
+            y0 = O.video_text_cross_attention_cpu_fp32(y0, ts_view, inp.context, pts_view, tw,
+                                                       calibrate=True).to(torch.bfloat16)
             O.video_ffn_cpu_fp32(y0, ts_view, fw, calibrate=True)
 
         def run():
             y = O.video_block_cpu_fp32(inp.x, ts_view, inp.cos, inp.sin, w).to(torch.bfloat16)
+            y = O.video_text_cross_attention_cpu_fp32(y, ts_view, inp.context, pts_view, tw).to(torch.bfloat16)
             O.video_ffn_cpu_fp32(y, ts_view, fw)
-        flops, metric, what = args.layers * layer_flops(L), layers_metric(args.layers, L), "layer (self-attention + FFN)"
-        workload = f"LTX-2.3 video DiT layers (self-attention + FFN), {args.config}"
+        flops, metric = args.layers * layer_flops(L, L_ctx), layers_metric(args.layers, L, L_ctx)
+        what = "layer (self-attention + text cross-attention + FFN)"
+        workload = f"LTX-2.3 video DiT layers (self-attention + text cross-attention + FFN), {args.config}"
     times, done_warm = time_cpu_steps(run, args.steps, args.warmup, budget_s)
     per = statistics.mean(times)
     ms = per * 1e3 * (args.layers if args.branch == "layers" else 1)
@@ -651,19 +660,22 @@ def run_text(args) -> None:
 
 
 # --------------------------------------------------------------------------- a stack of layers
-def layers_metric(layers: int, L: int) -> str:
-    return f"video branches of {layers} DiT layers (self-attention + FFN) ms per denoising step at L={L}, 1 B200"
+def layers_metric(layers: int, L: int, L_ctx: int) -> str:
+    return (f"video branches of {layers} DiT layers (self-attention + text cross-attention over {L_ctx} context "
+            f"tokens + FFN) ms per denoising step at L={L}, 1 B200")
 
 
-def layer_flops(L: int) -> float:
-    """Attention (bf16) + Q/K/V, out-projection and FFN projections (FP8) of one layer's video branches."""
-    return attn_flops(L) + 2.0 * L * 4096 * (3 * 4096 + 4096) + ffn_flops(L)
+def layer_flops(L: int, L_ctx: int) -> float:
+    """One layer's video branches: the self-attention (bf16 attention + FP8 Q/K/V and out-projection), the text
+    cross-attention and the FFN."""
+    return attn_flops(L) + 2.0 * L * 4096 * (3 * 4096 + 4096) + text_flops(L, L_ctx) + ffn_flops(L)
 
 
 def run_layers(args) -> None:
-    """``--branch layers``: the video branches (self-attention then FFN) of ``--layers`` DiT layers, one
-    denoising step through the stack per timed step, captured as one CUDA graph (1 GPU).  Layers cycle
-    through ``--distinct-weights`` random weight sets (every layer still holds its own device copy)."""
+    """``--branch layers``: the video branches (self-attention, text cross-attention over ``--context-tokens``
+    prompt tokens, FFN) of ``--layers`` DiT layers, one denoising step through the stack per timed step,
+    captured as one CUDA graph (1 GPU).  Layers cycle through ``--distinct-weights`` random weight sets (every
+    layer still holds its own device copy)."""
     from opengenie_b200 import _lib, synthetic
     from opengenie_b200.graphs import StepGraph
     from opengenie_b200.video_layer import VideoLayer, VideoLayerStack
@@ -674,16 +686,19 @@ def run_layers(args) -> None:
     dev = torch.device("cuda", local)
     cfg = synthetic.CONFIGS[args.config]
     L = cfg.tokens
-    inp = synthetic.make_inputs(cfg, seed=1).to(dev)
-    sets = [(synthetic.make_weights(seed=100 + i), synthetic.make_ffn_weights(seed=200 + i))
-            for i in range(max(1, args.distinct_weights))]
-    stack = VideoLayerStack([VideoLayer(*sets[i % len(sets)], dev) for i in range(args.layers)])
+    L_ctx = args.context_tokens
+    inp = synthetic.make_layer_inputs(cfg, L_ctx, seed=1).to(dev)
+    sets = [(synthetic.make_weights(seed=100 + i), synthetic.make_ffn_weights(seed=200 + i),
+             synthetic.make_text_attention_weights(seed=300 + i)) for i in range(max(1, args.distinct_weights))]
+    stack = VideoLayerStack([VideoLayer(*sets[i % len(sets)][:2], dev, text_weights=sets[i % len(sets)][2])
+                             for i in range(args.layers)])
     pe = rope_input(args, cfg, inp, dev)
-    stack.calibrate_input_scales(inp.x, inp.timestep, pe)
+    ctx = dict(context=inp.context, prompt_timestep=inp.prompt_timestep)
+    stack.calibrate_input_scales(inp.x, inp.timestep, pe, **ctx)
     out = torch.empty_like(inp.x)
 
     def step():
-        stack(inp.x, inp.timestep, pe, out=out)
+        stack(inp.x, inp.timestep, pe, out=out, **ctx)
 
     for _ in range(args.warmup):
         step()
@@ -702,17 +717,18 @@ def run_layers(args) -> None:
     ms = ev0.elapsed_time(ev1) / args.steps
     status = _lib.device_status(clear=True)
     finite = bool(torch.isfinite(out.float()).all())
-    per_layer = layer_flops(L)
+    per_layer = layer_flops(L, L_ctx)
     line = {
-        "metric": layers_metric(args.layers, L),
+        "metric": layers_metric(args.layers, L, L_ctx),
         "value": args.layers * per_layer / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3 / args.layers, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16 attention / e4m3 projections",
         "data": "synthetic (seeded inputs, random-init weights)",
-        "config": {"workload": f"LTX-2.3 video DiT layers (self-attention + FFN), {args.config}", "tokens": L,
+        "config": {"workload": f"LTX-2.3 video DiT layers (self-attention + text cross-attention + FFN), "
+                               f"{args.config}", "tokens": L, "context_tokens": L_ctx,
                    "layers": args.layers, "distinct_weight_sets": len(sets),
                    "flops_per_layer": per_layer, "launch": "one CUDA graph replay per step",
-                   "scope": "text and audio cross-attention branches of the layer are not included"},
+                   "scope": "the audio-video cross-attention branch of the layer is not part of this library"},
         "gpu_launches": stack.kernel_launches_per_step * args.steps, "clocks": clk.summary(),
         "device_status": status, "output_finite": finite,
     }
@@ -740,6 +756,9 @@ def main() -> None:
     ap.add_argument("--context-tokens", type=int, default=1024, help="--branch text: prompt context tokens")
     ap.add_argument("--layers", type=int, default=48, help="--branch layers: layers in the stack")
     ap.add_argument("--distinct-weights", type=int, default=2, help="--branch layers: random weight sets")
+    ap.add_argument("--distinct-input-scales", action="store_true",
+                    help="Q, K and V linears with different input scales (a checkpoint calibrated per linear): "
+                         "K's and V's are set to 1.25x and 0.8x the calibrated Q scale")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.branch == "ffn" and args.impl == "ours":
@@ -768,9 +787,17 @@ def main() -> None:
     inp = inp_cpu.to(dev)
     pe = rope_input(args, cfg, inp, dev)
 
+    def distinct_scales(block) -> None:
+        bw = block.w
+        bw.to_k.input_scale = (bw.to_q.input_scale * 1.25).contiguous()
+        bw.to_v.input_scale = (bw.to_q.input_scale * 0.8).contiguous()
+        block.input_scales_changed()
+
     if world == 1:
         blk = VideoSelfAttentionBlock(w, dev)
         blk.calibrate_input_scales(inp.x, inp.timestep, pe)
+        if args.distinct_input_scales:
+            distinct_scales(blk)
         launches_per_step = 5
         out_dev = torch.empty_like(inp.x)
 
@@ -781,6 +808,8 @@ def main() -> None:
 
         blk = UlyssesVideoSelfAttention(w, dev, pg, exchange=args.exchange)
         blk.calibrate_input_scales(inp.x, inp.timestep, pe)
+        if args.distinct_input_scales:
+            distinct_scales(blk.blk)
         launches_per_step = blk.kernel_launches_per_step
         x_loc = blk.local_slice(inp.x)
         out_dev = torch.empty_like(x_loc)
@@ -878,6 +907,8 @@ def main() -> None:
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 attention / e4m3 projections",
             "data": "synthetic (seeded inputs, random-init weights)", "config": config_dict(args.config, world, args.exchange),
             "launch": "one CUDA graph replay per step" if use_graph else "eager launches",
+            "qkv_input_scales": ("distinct per linear (three e4m3 copies from one AdaZero, one GEMM over the planes)"
+                                 if args.distinct_input_scales else "one shared scale"),
             "rope": ("cos/sin tables [1, 32, L, 64] read by the RoPE kernel" if args.rope_tables else
                      "cos/sin generated in the RoPE kernel from the tokens' (t, h, w) positions"),
             "roofline": {

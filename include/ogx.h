@@ -91,6 +91,17 @@ int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int6
                               int scale_index, float eps, const float* input_scale, int quant_mode, void* y,
                               void* q, void* stream);
 
+/* Same, with up to three e4m3 outputs of the one bf16 y: output i = quant_{input_scales[i]}(y) at
+ * q + i * q_plane_stride (bytes, a multiple of 16).  The checkpoint path whose Q, K and V linears carry
+ * different input scales: the reference quantises the bf16 AdaZero output once per linear inside
+ * FP8Linear.forward (ltx_serve/triton_ltx_ops.py:1692, :1676-1716); here x is read once. */
+int ogx_adazero_from_ada_e4m3_planes(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                                     int table_dtype, int64_t table_stride_row, const void* timestep,
+                                     int timestep_dtype, int64_t ts_stride_b, int64_t ts_stride_t,
+                                     int64_t ts_stride_p, int shift_index, int scale_index, float eps,
+                                     const float* input_scales, int planes, int quant_mode, void* y, void* q,
+                                     int64_t q_plane_stride, void* stream);
+
 /* Per-tensor E4M3 quantiser: q = e4m3(clamp(x * (1/s), -448, 448)).
  * x: bf16 or f16, n elements contiguous; input_scale: device f32 scalar.
  * Replaces fused_fp8_quantize_e4m3, ltx_serve/triton_ltx_ops.py:144-161. */
@@ -197,6 +208,15 @@ int ogx_fp8_scaled_mm(const void* a, int64_t M, int64_t K, int64_t lda, const vo
                       const float* scale_a, const float* scale_b, int64_t n_per_scale, const void* bias,
                       int bias_dtype, void* out, int64_t ldo, void* stream);
 
+/* ogx_fp8_scaled_mm over `planes` activation planes: a holds planes e4m3 [M, K] planes (row stride lda,
+ * plane stride M * lda); output columns [i*N/planes, (i+1)*N/planes) read plane i with scale_a[i] and
+ * scale_b[i] (N / planes a multiple of 256).  One launch for the packed Q/K/V projection of a checkpoint
+ * whose three linears quantise their input with different scales, where the reference runs three
+ * FP8Linear.forward calls (ltx_serve/triton_ltx_ops.py:1695-1707, once per linear). */
+int ogx_fp8_scaled_mm_planes(const void* a, int64_t planes, int64_t M, int64_t K, int64_t lda, const void* w,
+                             int64_t N, int64_t ldw, const float* scale_a, const float* scale_b, const void* bias,
+                             int bias_dtype, void* out, int64_t ldo, void* stream);
+
 /* The FFN's first projection with GELU and the next projection's input quantiser in the epilogue:
  * out_q = quant_{q_scale}(bf16(gelu(bf16(bf16(a @ w^T * scale_a * scale_b) + bf16(bias))))), e4m3
  * [M, N] with row stride ldq (a multiple of 16).  Equals ogx_fp8_scaled_mm followed by
@@ -293,19 +313,20 @@ int ogx_peer_barrier(unsigned int* local_signals, void* const* peer_signals, int
 
 /* No counterpart in the reference (an addition of this library).  ogx_peer_barrier for callers that
  * cannot allocate device memory, e.g. a runtime driving all of its GPUs from one process with their
- * memory reserved up front for its own pool.  The signal block is a 64-byte array inside the library,
+ * memory reserved up front for its own pool.  The barrier count is a 64-byte array inside the library,
  * one per GPU that loads it and held until the process exits; it is zero at load and never cleared
- * (barrier numbers only grow).  Ranks are GPUs of this process: devices[i] is rank i's device ordinal
- * (no ordinal twice), devices[rank] must be the current device, and every pair must be able to reach
- * each other (cudaDeviceCanAccessPeer); the call enables access from the current device to each peer
- * if the caller has not (a per-process mapping).  world is at most 8; larger values are rejected.
- * Set-up: the first call naming a device looks up that device's array address with the device made
- * current, which creates the device's primary context if it has none (the context, not this call,
- * takes device memory) and may load the library's module there.  So every device in devices[] should
- * already have its context, and one warm-up call per rank should run before serving starts and before
- * any stream capture.  count_out (device memory, may be NULL) receives the number of barriers this
- * rank has passed.  Every call on a device shares its array: one barrier group per process, and calls
- * that overlap on a GPU race.  Allocates no device memory. */
+ * (barrier numbers only grow).  The arrivals cross between GPUs through one 4 KB page of host memory
+ * inside the library, page-locked and mapped into every GPU at the first call (cudaHostRegister; it
+ * stays registered until the process exits), so no GPU touches another GPU's memory and no peer access
+ * is needed.  Ranks are GPUs of this process: devices[i] is rank i's device ordinal (below 64, no
+ * ordinal twice) and devices[rank] must be the current device.  world is at most 8; larger values are
+ * rejected.  Set-up: the first call naming a device looks up that device's array address with the
+ * device made current, which creates the device's primary context if it has none (the context, not
+ * this call, takes device memory) and may load the library's module there.  So every device in
+ * devices[] should already have its context, and one warm-up call per rank should run before serving
+ * starts and before any stream capture.  count_out (device memory, may be NULL) receives the number of
+ * barriers this rank has passed.  Every call on a device shares its count and its row of arrival slots:
+ * one barrier group per process, and calls that overlap on a GPU race.  Allocates no device memory. */
 int ogx_peer_barrier_static(int rank, int world, const int* devices, unsigned int* count_out, void* stream);
 
 /* ogx_video_qkv_rmsnorm_rope_scatter with one destination base per head group (groups = world size):

@@ -42,6 +42,10 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p, c_int,
         c_int64, c_int64, c_int64, c_int, c_int, c_float, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
     ],
+    "ogx_adazero_from_ada_e4m3_planes": [
+        c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p, c_int,
+        c_int64, c_int64, c_int64, c_int, c_int, c_float, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int64, c_void_p,
+    ],
     "ogx_fp8_quantize_e4m3": [c_void_p, c_int, c_int64, c_void_p, c_int, c_void_p, c_void_p],
     "ogx_bias_add_bf16": [c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p],
     "ogx_residual_gate_bias_from_ada": [
@@ -69,6 +73,10 @@ _SIGNATURES: dict[str, list] = {
     ],
     "ogx_fp8_scaled_mm": [
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
+        c_void_p, c_int, c_void_p, c_int64, c_void_p,
+    ],
+    "ogx_fp8_scaled_mm_planes": [
+        c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
         c_void_p, c_int, c_void_p, c_int64, c_void_p,
     ],
     "ogx_fp8_scaled_mm_residual_gate": [

@@ -178,9 +178,11 @@ struct AdaArgs {
   int64_t rows, tokens;
   int shift_index, scale_index;
   float eps;
-  const float* input_scale;  // device scalar (QUANT only)
+  const float* input_scale;  // device scalar (QUANT only); with nq > 1 an array of nq scales
   __nv_bfloat16* y;          // may be null when only q is wanted
   uint8_t* q;                // e4m3 output (QUANT only)
+  int nq;                    // e4m3 outputs (QUANT only; 0 means 1): output i, quantised with input_scale[i],
+  int64_t q_plane;           // at q + i * q_plane (bytes)
 };
 
 // ----------------------------------------------------------------- per-head gate

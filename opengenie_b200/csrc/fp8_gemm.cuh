@@ -69,7 +69,12 @@ struct Params {
   // block s holds the columns of source rank s), read through a 3-D map
   // {a_k_block, M, K / a_k_block}; a_k_block is a multiple of BK.
   int a_k_block;
-  const float* scale_a;  // device scalar
+  // 0: as above.  > 0: A is a_planes planes [M, K] (plane stride M * lda bytes) read through a 3-D map
+  // {K, M, a_planes}; output column n uses plane n / n_per_scale and its scale scale_a[n / n_per_scale]
+  // (one quantised copy of the activations per linear, each with its own input scale).  n_per_scale is a
+  // multiple of BN, so every tile reads one plane.
+  int a_planes;
+  const float* scale_a;  // device scalar; with a_planes > 0 one per plane
   const float* scale_b;  // device array, one entry per n_per_scale columns
   int n_per_scale;
   const void* bias;  // [N] or null
@@ -197,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = tile0; tile < num_tiles && ok; tile += tile_step) {
         const int m0 = (tile % num_m) * TM + static_cast<int>(crank) * BM;  // this CTA's A rows
         const int n0 = (tile / num_m) * BN + static_cast<int>(crank) * b_rows(PAIR);  // this CTA's B rows
+        const int plane = p.a_planes > 0 ? (tile / num_m) * BN / p.n_per_scale : 0;  // A plane of the tile
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&st.empty[stage], phase ^ 1u, abort)) {
             ok = false;
@@ -210,6 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (crank == 0) mbar_arrive_expect_tx(&st.full[stage], 2 * SBYTES);
             if (p.a_k_block > 0)
               tma_load_3d_pair(sa, &tmap_a, fb, (kb * BK) % p.a_k_block, m0, (kb * BK) / p.a_k_block);
+            else if (p.a_planes > 0)
+              tma_load_3d_pair(sa, &tmap_a, fb, kb * BK, m0, plane);
             else
               tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, m0);
             tma_load_2d_pair(sb, &tmap_b, fb, kb * BK, n0);
@@ -217,6 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(&st.full[stage], SBYTES);
             if (p.a_k_block > 0)
               tma_load_3d(sa, &tmap_a, &st.full[stage], (kb * BK) % p.a_k_block, m0, (kb * BK) / p.a_k_block);
+            else if (p.a_planes > 0)
+              tma_load_3d(sa, &tmap_a, &st.full[stage], kb * BK, m0, plane);
             else
               tma_load_2d(sa, &tmap_a, &st.full[stage], kb * BK, m0);
             tma_load_2d(sb, &tmap_b, &st.full[stage], kb * BK, n0);
@@ -333,7 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c + 1 < BN / 2 / 32) tmem_ld32(taddr + (c + 1) * 32, nxt);  // in flight while `cur` is processed
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < p.N) {
-          const float scale = sa * __ldg(p.scale_b + col0 / p.n_per_scale);
+          const float scale = (p.a_planes > 0 ? __ldg(p.scale_a + col0 / p.n_per_scale) : sa) *
+                              __ldg(p.scale_b + col0 / p.n_per_scale);
           __nv_bfloat16* orow = p.out + static_cast<int64_t>(row) * p.ldo + col0;
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {

@@ -425,6 +425,42 @@ int ogx_adazero_from_ada_e4m3(const void* x, int64_t batch, int64_t tokens, int6
   return ada_dispatch(a, cols, table_dtype, timestep_dtype, true, quant_mode, static_cast<cudaStream_t>(stream));
 }
 
+int ogx_adazero_from_ada_e4m3_planes(const void* x, int64_t batch, int64_t tokens, int64_t cols, const void* table,
+                                     int table_dtype, int64_t table_stride_row, const void* timestep,
+                                     int timestep_dtype, int64_t ts_stride_b, int64_t ts_stride_t,
+                                     int64_t ts_stride_p, int shift_index, int scale_index, float eps,
+                                     const float* input_scales, int planes, int quant_mode, void* y, void* q,
+                                     int64_t q_plane_stride, void* stream) {
+  int rc = ada_guard(x, batch, tokens, cols, table, table_dtype, timestep, timestep_dtype, ts_stride_b, ts_stride_t,
+                     ts_stride_p, shift_index, scale_index);
+  if (rc) return rc;
+  if (planes < 1 || planes > 3) return fail(OGX_EINVAL, "planes: 1 to 3 e4m3 outputs");
+  if (q == nullptr || (y != nullptr && !aligned16(y)) || !aligned16(q)) return fail(OGX_EINVAL, "output");
+  if (planes > 1 && (q_plane_stride % 16 || q_plane_stride < batch * tokens * cols))
+    return fail(OGX_EINVAL, "output: plane stride");
+  if (input_scales == nullptr) return fail(OGX_EINVAL, "input_scale");
+  if (quant_mode != OGX_QUANT_TORCH && quant_mode != OGX_QUANT_SINGLE) return fail(OGX_EINVAL, "quant_mode");
+  ogx::AdaArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.table = table;
+  a.ts = timestep;
+  a.ts_stride_b = ts_stride_b;
+  a.ts_stride_t = ts_stride_t;
+  a.ts_stride_p = ts_stride_p;
+  a.table_stride_row = table_stride_row;
+  a.rows = batch * tokens;
+  a.tokens = tokens > 0 ? tokens : 1;
+  a.shift_index = shift_index;
+  a.scale_index = scale_index;
+  a.eps = eps;
+  a.input_scale = input_scales;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.q = static_cast<uint8_t*>(q);
+  a.nq = planes;
+  a.q_plane = q_plane_stride;
+  return ada_dispatch(a, cols, table_dtype, timestep_dtype, true, quant_mode, static_cast<cudaStream_t>(stream));
+}
+
 int ogx_fp8_quantize_e4m3(const void* x, int x_dtype, int64_t n, const float* input_scale, int quant_mode, void* q,
                           void* stream) {
   if (x_dtype != OGX_DTYPE_BF16 && x_dtype != OGX_DTYPE_F16) return fail(OGX_EINVAL, "x_dtype");
@@ -736,7 +772,7 @@ bool gemm_use_pairs(int64_t M, int64_t N) {
 
 int gemm_common(const void* a, int64_t M, int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                 const float* scale_a, const float* scale_b, int64_t n_per_scale, CUtensorMap* ma, CUtensorMap* mb,
-                int64_t a_k_block = 0) {
+                int64_t a_k_block = 0, int64_t a_planes = 0) {
   if (a == nullptr || w == nullptr || scale_a == nullptr || scale_b == nullptr) return fail(OGX_EINVAL, "null_pointer");
   if (M < 0 || N <= 0 || K <= 0) return fail(OGX_EINVAL, "shape");
   if (K % 16 || N % 32) return fail(OGX_EINVAL, "shape: K % 16 and N % 32 must be 0");
@@ -746,7 +782,15 @@ int gemm_common(const void* a, int64_t M, int64_t K, int64_t lda, const void* w,
   if (!aligned16(a) || !aligned16(w)) return fail(OGX_EINVAL, "alignment");
   if (M == 0) return OGX_OK;
   int rc;
-  if (a_k_block > 0) {
+  if (a_planes > 0) {
+    // one [M, K] plane (row stride lda) per N segment of n_per_scale columns
+    if (a_k_block > 0 || N % a_planes || n_per_scale != N / a_planes || n_per_scale % ogx::gemm::BN)
+      return fail(OGX_EINVAL, "a_planes: N must split into planes of a multiple of %d columns", ogx::gemm::BN);
+    const uint64_t da[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M), static_cast<uint64_t>(a_planes)};
+    const uint64_t sa[2] = {static_cast<uint64_t>(lda), static_cast<uint64_t>(lda * M)};
+    const uint32_t ba[3] = {static_cast<uint32_t>(ogx::gemm::BK), static_cast<uint32_t>(ogx::gemm::BM), 1};
+    rc = make_map(ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a, da, sa, ba);
+  } else if (a_k_block > 0) {
     if (a_k_block % ogx::gemm::BK || K % a_k_block) return fail(OGX_EINVAL, "a_k_block");
     const uint64_t da[3] = {static_cast<uint64_t>(a_k_block), static_cast<uint64_t>(M),
                             static_cast<uint64_t>(K / a_k_block)};
@@ -906,6 +950,32 @@ int ogx_fp8_scaled_mm(const void* a, int64_t M, int64_t K, int64_t lda, const vo
   p.scale_a = scale_a;
   p.scale_b = scale_b;
   p.n_per_scale = static_cast<int>(n_per_scale);
+  p.bias = bias;
+  p.bias_fp32 = bias_dtype == OGX_DTYPE_F32;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  return gemm_launch<ogx::gemm::EPI_BIAS>(ma, mb, p, static_cast<cudaStream_t>(stream));
+}
+
+int ogx_fp8_scaled_mm_planes(const void* a, int64_t planes, int64_t M, int64_t K, int64_t lda, const void* w,
+                             int64_t N, int64_t ldw, const float* scale_a, const float* scale_b, const void* bias,
+                             int bias_dtype, void* out, int64_t ldo, void* stream) {
+  if (planes < 1 || planes > 8) return fail(OGX_EINVAL, "a_planes: 1 to 8 planes");
+  if (N % planes) return fail(OGX_EINVAL, "a_planes: N must split into planes of a multiple of %d columns",
+                              ogx::gemm::BN);
+  CUtensorMap ma, mb;
+  int rc = gemm_common(a, M, K, lda, w, N, ldw, scale_a, scale_b, N / planes, &ma, &mb, 0, planes);
+  if (rc || M == 0) return rc;
+  if (out == nullptr || !aligned16(out) || ldo % 8 || ldo < N) return fail(OGX_EINVAL, "output");
+  if (bias != nullptr && (!dtype_ok(bias_dtype) || !aligned16(bias))) return fail(OGX_EINVAL, "bias");
+  ogx::gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.a_planes = static_cast<int>(planes);
+  p.scale_a = scale_a;
+  p.scale_b = scale_b;
+  p.n_per_scale = static_cast<int>(N / planes);
   p.bias = bias;
   p.bias_fp32 = bias_dtype == OGX_DTYPE_F32;
   p.out = static_cast<__nv_bfloat16*>(out);
@@ -1243,17 +1313,23 @@ int ogx_attention_fwd_e4m3_to_peers(const void* q, const void* k, const void* v,
 // ogx_peer_barrier needs a 16-word signal block per rank, allocated by the caller.  Some callers
 // cannot allocate device memory: a runtime that drives all of its GPUs from one process and reserves
 // their memory up front for its own pool, so that no cudaMalloc may run once serving has started.
-// For them the signal block lives in this file-scope array instead, one per GPU that loads the
-// library (64 bytes, held until the process exits), and ogx_peer_barrier_static takes the ranks'
-// device ordinals instead of block pointers.  The ranks must be GPUs of this one process with peer
-// access enabled between them (UVA makes each device's copy of the array addressable by the others).
+// For them the barrier count lives in a file-scope device array (one per GPU that loads the library,
+// 64 bytes, held until the process exits) and the arrival slots in one page of host memory inside the
+// library, page-locked and mapped into every GPU of the process at the first call.  No GPU touches another
+// GPU's memory, so the ranks need no peer access between them; ogx_peer_barrier_static takes the ranks'
+// device ordinals instead of block pointers.
 namespace {
 
-// [0, 8) arrival slots, [8] barriers passed; zero when the library loads and never cleared after:
-// the barrier numbers only grow, so no call needs it zeroed again.
+// [8] barriers passed on this device; zero when the library loads and never cleared after: the barrier
+// numbers only grow, so no call needs it zeroed again.
 static __device__ __align__(256) unsigned int g_static_peer_block[ogx::kPeerSignalWords];
 
 constexpr int kMaxDevices = 64;
+
+// The arrival slots: row d (kPeerSignalWords words) of device d, word r the latest barrier number rank r
+// announced to it.  One 4 KB page.
+alignas(4096) unsigned int g_static_host_slots[kMaxDevices * ogx::kPeerSignalWords];
+static_assert(sizeof(g_static_host_slots) == 4096, "one page of arrival slots");
 
 // Device address of g_static_peer_block on `dev`, looked up once per device with that device current.
 int static_peer_block(int dev, unsigned int** out) {
@@ -1278,6 +1354,30 @@ int static_peer_block(int dev, unsigned int** out) {
   return OGX_OK;
 }
 
+// The device address of the arrival slots (the same in every GPU of the process: portable, mapped
+// page-locked memory under unified addressing), page-locked once per process.
+int static_host_slots(unsigned int** out) {
+  static std::mutex mu;
+  static unsigned int* dev_ptr = nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev_ptr == nullptr) {
+    cudaError_t e = cudaHostRegister(g_static_host_slots, sizeof(g_static_host_slots),
+                                     cudaHostRegisterPortable | cudaHostRegisterMapped);
+    if (e == cudaErrorHostMemoryAlreadyRegistered) {
+      cudaGetLastError();
+    } else if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(OGX_ECUDA, "cudaHostRegister of the barrier's arrival slots: %s", cudaGetErrorString(e));
+    }
+    void* p = nullptr;
+    const int rc = check_cuda(cudaHostGetDevicePointer(&p, g_static_host_slots, 0), "cudaHostGetDevicePointer");
+    if (rc) return rc;
+    dev_ptr = static_cast<unsigned int*>(p);
+  }
+  *out = dev_ptr;
+  return OGX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1285,15 +1385,21 @@ extern "C" {
 int ogx_peer_barrier_static(int rank, int world, const int* devices, unsigned int* count_out, void* stream) {
   if (devices == nullptr) return fail(OGX_EINVAL, "null_pointer");
   if (world < 1 || world > 8)
-    return fail(OGX_EINVAL, "world: the static signal block holds at most 8 ranks (got %d)", world);
+    return fail(OGX_EINVAL, "world: the static barrier holds at most 8 ranks (got %d)", world);
   if (rank < 0 || rank >= world) return fail(OGX_EINVAL, "world: rank %d outside [0, %d)", rank, world);
   int cur = 0;
   int rc = check_cuda(cudaGetDevice(&cur), "cudaGetDevice");
   if (rc) return rc;
   if (devices[rank] != cur)
     return fail(OGX_EINVAL, "devices[rank] is %d but the current device is %d", devices[rank], cur);
-  // Two ranks on one ordinal would share one slot/count block: their barrier numbers would drift apart and
-  // every later wait would run out.
+  ogx::DeviceList devs{};
+  for (int i = 0; i < world; ++i) {
+    if (devices[i] < 0 || devices[i] >= kMaxDevices)
+      return fail(OGX_EINVAL, "device ordinal %d out of range", devices[i]);
+    devs.d[i] = devices[i];
+  }
+  // Two ranks on one ordinal would share one arrival row and one count: their barrier numbers would drift
+  // apart and every later wait would run out.
   for (int i = 0; i < world; ++i)
     for (int j = i + 1; j < world; ++j)
       if (devices[i] == devices[j])
@@ -1301,31 +1407,12 @@ int ogx_peer_barrier_static(int rank, int world, const int* devices, unsigned in
   unsigned int* local = nullptr;
   rc = static_peer_block(cur, &local);
   if (rc) return rc;
-  ogx::PeerSignals ps{};
-  for (int i = 0; i < world; ++i) {
-    if (devices[i] != cur) {
-      int can = 0;
-      rc = check_cuda(cudaDeviceCanAccessPeer(&can, cur, devices[i]), "cudaDeviceCanAccessPeer");
-      if (rc) return rc;
-      if (!can) return fail(OGX_EINVAL, "device %d cannot access peer device %d", cur, devices[i]);
-      // The kernel stores into the peer's copy of the block: access must be enabled, not merely possible,
-      // or the store is an illegal address.  Enabling is a per-process mapping (no lasting GPU setting);
-      // an access the caller already enabled is reported as such and is fine.
-      const cudaError_t e = cudaDeviceEnablePeerAccess(devices[i], 0);
-      if (e == cudaErrorPeerAccessAlreadyEnabled) {
-        cudaGetLastError();  // clear the sticky-free status this call leaves
-      } else if (e != cudaSuccess) {
-        cudaGetLastError();
-        return fail(OGX_EINVAL, "peer access from device %d to device %d could not be enabled: %s", cur, devices[i],
-                    cudaGetErrorString(e));
-      }
-    }
-    rc = static_peer_block(devices[i], &ps.slot[i]);
-    if (rc) return rc;
-  }
+  unsigned int* slots = nullptr;
+  rc = static_host_slots(&slots);
+  if (rc) return rc;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ogx::peer_barrier_kernel<<<1, 32, 0, s>>>(local, ps, rank, world);
-  rc = check_launch("peer_barrier_kernel");
+  ogx::host_slot_barrier_kernel<<<1, 32, 0, s>>>(local, slots, devs, rank, world);
+  rc = check_launch("host_slot_barrier_kernel");
   if (rc || count_out == nullptr) return rc;
   return check_cuda(cudaMemcpyAsync(count_out, local + ogx::kPeerCountWord, sizeof(unsigned int),
                                     cudaMemcpyDeviceToDevice, s),

@@ -54,4 +54,45 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(unsigned int* local, P
   if (i == 0) local[kPeerCountWord] = epoch;
 }
 
+// The barrier of ogx_peer_barrier_static, for ranks that are GPUs of one process.  Its arrival slots are
+// page-locked host memory mapped into every GPU of the process: slots[d * kPeerSignalWords + r] holds the
+// latest barrier number rank r announced to device d.  No GPU reads or writes another GPU's memory; the
+// barrier count stays in this GPU's own block (`local`).  Stores go out with a system-scope release, loads
+// come in with a system-scope acquire; the wait is bounded as in peer_barrier_kernel.
+struct DeviceList {
+  int d[8];  // rank i's device ordinal
+};
+
+__device__ __forceinline__ int device_of(const DeviceList& devs, int i) {
+  int d = devs.d[0];  // constant-index selects (a runtime index into the parameter array would go to local memory)
+#pragma unroll
+  for (int j = 1; j < 8; ++j) d = (i == j) ? devs.d[j] : d;
+  return d;
+}
+
+__global__ void __launch_bounds__(32) host_slot_barrier_kernel(unsigned int* local, unsigned int* slots,
+                                                               DeviceList devs, int rank, int world) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = threadIdx.x;
+  const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(local + kPeerCountWord) + 1u;
+  if (i < world && i != rank) {
+    unsigned int* to_peer = slots + device_of(devs, i) * kPeerSignalWords + rank;
+    unsigned int* from_peer = slots + device_of(devs, rank) * kPeerSignalWords + i;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(to_peer), "r"(epoch) : "memory");
+    const unsigned long long t0 = global_ns();
+    for (uint32_t n = 0;; ++n) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(from_peer) : "memory");
+      if (static_cast<int>(v - epoch) >= 0) break;
+      if ((n & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
+        atomicOr(&g_ogx_status, OGX_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncwarp();  // every lane has read the count
+  if (i == 0) local[kPeerCountWord] = epoch;
+}
+
 }  // namespace ogx

@@ -6,10 +6,12 @@
 // Here one persistent CTA per SM streams its rows through a ring of shared-memory stages instead:
 //   warp 8 (one elected thread)  issues cp.async.bulk copies of whole rows (8 KB per 4096-column bf16
 //                                row) into the ring, a row as soon as its stage is free;
-//   warps 0..7                   each take every eighth row of the CTA: wait for its stage, reduce the
-//                                sum of squares from shared memory (warp shuffles, no block barrier),
-//                                write the outputs with 16-byte stores, free the stage.
-// With 11-24 stages (up to ~190 KB) a SM keeps enough row loads in flight for the HBM latency; no
+//   warps 0..W-1                 each take every W-th row of the CTA (W = 8, or the stage count where
+//                                fewer stages fit): wait for its stage, reduce the sum of squares from
+//                                shared memory (warp shuffles, no block barrier), write the outputs with
+//                                16-byte stores, free the stage.
+// The stage count is a multiple of W, so a stage is always consumed by the same warp (see ring_warps).
+// With 7-24 stages (up to ~190 KB) a SM keeps enough row loads in flight for the HBM latency; no
 // register holds a row.  Every wait is bounded (a wait that runs out records OGX_ERR_TIMEOUT, the
 // CTA stops and lets its copies in flight land before it exits).
 //
@@ -49,6 +51,14 @@ struct Ring {
   uint64_t empty[kMaxStages];
   int abort;
 };
+
+// Consumer warps and ring stages a kernel uses out of `stages` that fit: as many warps as stages (at most
+// kConsumerWarps) and the stages rounded down to a multiple of that, so row k goes to stage k % S and to warp
+// k % W with W dividing S: each stage is always consumed by the same warp.  A parity wait cannot tell the
+// phase it waits for from the one before it, so a warp reaching a stage one use ahead of the stage's other
+// consumer would take the previous fill for its own; with one consumer per stage that cannot happen.
+__host__ __device__ constexpr int ring_warps(int stages) { return stages < kConsumerWarps ? stages : kConsumerWarps; }
+__host__ __device__ constexpr int ring_stages(int stages) { return stages / ring_warps(stages) * ring_warps(stages); }
 
 __device__ __forceinline__ void ring_init(Ring& r, int stages) {
   if (threadIdx.x == 0) {
@@ -135,7 +145,8 @@ struct AdaLayout {
   static constexpr int kStagePerToken = COLS * 2 + 2 * COLS * static_cast<int>(sizeof(TsT));
   __host__ __device__ static constexpr int stage_bytes(bool uniform) { return uniform ? kStageUniform : kStagePerToken; }
   __host__ __device__ static constexpr int stages(bool uniform) {
-    return ((kDynLimit - kAda) / stage_bytes(uniform)) > kMaxStages ? kMaxStages : ((kDynLimit - kAda) / stage_bytes(uniform));
+    return ring_stages(((kDynLimit - kAda) / stage_bytes(uniform)) > kMaxStages ? kMaxStages
+                                                                                 : ((kDynLimit - kAda) / stage_bytes(uniform)));
   }
   __host__ __device__ static constexpr int smem_bytes(bool uniform) { return kAda + stages(uniform) * stage_bytes(uniform); }
 };
@@ -156,7 +167,8 @@ template <int COLS, typename TableT, typename TsT, bool QUANT, int QMODE, bool U
 __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
   pdl_trigger();
   using Lay = AdaLayout<COLS, TsT>;
-  constexpr int S = Lay::stages(UNIFORM);
+  constexpr int S = Lay::stages(UNIFORM);  // a multiple of W
+  constexpr int W = ring_warps(S);
   constexpr uint32_t SB = Lay::stage_bytes(UNIFORM);
   constexpr int VPL = COLS / 8 / 32;  // 16-byte vectors per lane
   extern __shared__ uint8_t smem_raw[];
@@ -220,14 +232,18 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
   } else {
     constexpr bool round_ada = std::is_same<TsT, __nv_bfloat16>::value;
     constexpr bool fast_quant = QUANT && QMODE == kQuantTorch;
-    float s = 0.f, r = 0.f;
+    // up to three e4m3 outputs of the same bf16 value, each with its own input scale (the per-linear scales
+    // of a checkpoint whose Q, K and V projections were calibrated apart)
+    const int nq = a.nq > 1 ? (a.nq < 3 ? a.nq : 3) : 1;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
     if (QUANT) {
-      s = __ldg(a.input_scale);
-      r = __frcp_rn(s);
+      s0 = __ldg(a.input_scale);
+      s1 = nq > 1 ? __ldg(a.input_scale + 1) : s0;
+      s2 = nq > 2 ? __ldg(a.input_scale + 2) : s0;
     }
-    const f2 r2{r, r};
+    const float rcp0 = __frcp_rn(s0), rcp1 = __frcp_rn(s1), rcp2 = __frcp_rn(s2);
     volatile int* abort = &ring.abort;
-    for (int k = static_cast<int>(warp); k < n; k += kConsumerWarps) {
+    for (int k = static_cast<int>(warp); warp < W && k < n; k += W) {
       const int st = k % S;
       if (!mbar_wait(&ring.full[st], (k / S) & 1, abort)) break;
       const uint8_t* stage = stages + static_cast<size_t>(st) * SB;
@@ -269,14 +285,23 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
           yw[i] = pack_bf16x2(y.x, y.y);
         }
         if (a.y != nullptr) reinterpret_cast<uint4*>(a.y + row * COLS)[vec] = make_uint4(yw[0], yw[1], yw[2], yw[3]);
-        if (fast_quant) {
-          const uint32_t lo = quant2_torch(bf16x2_to_f2(yw[0]), r2) | (quant2_torch(bf16x2_to_f2(yw[1]), r2) << 16);
-          const uint32_t hi = quant2_torch(bf16x2_to_f2(yw[2]), r2) | (quant2_torch(bf16x2_to_f2(yw[3]), r2) << 16);
-          reinterpret_cast<uint2*>(a.q + row * COLS)[vec] = make_uint2(nan_bytes_to_ff(lo), nan_bytes_to_ff(hi));
-        } else if (QUANT) {
-          float yb[8];
-          unpack8(make_uint4(yw[0], yw[1], yw[2], yw[3]), yb);
-          reinterpret_cast<uint2*>(a.q + row * COLS)[vec] = quant8<__nv_bfloat16, QMODE>(yb, s, r);
+        if (QUANT) {
+#pragma unroll 1
+          for (int qi = 0; qi < nq; ++qi) {
+            const float sq = qi == 0 ? s0 : (qi == 1 ? s1 : s2);
+            const float rq = qi == 0 ? rcp0 : (qi == 1 ? rcp1 : rcp2);
+            uint8_t* qrow = a.q + qi * a.q_plane + row * COLS;
+            if (fast_quant) {
+              const f2 r2{rq, rq};
+              const uint32_t lo = quant2_torch(bf16x2_to_f2(yw[0]), r2) | (quant2_torch(bf16x2_to_f2(yw[1]), r2) << 16);
+              const uint32_t hi = quant2_torch(bf16x2_to_f2(yw[2]), r2) | (quant2_torch(bf16x2_to_f2(yw[3]), r2) << 16);
+              reinterpret_cast<uint2*>(qrow)[vec] = make_uint2(nan_bytes_to_ff(lo), nan_bytes_to_ff(hi));
+            } else {
+              float yb[8];
+              unpack8(make_uint4(yw[0], yw[1], yw[2], yw[3]), yb);
+              reinterpret_cast<uint2*>(qrow)[vec] = quant8<__nv_bfloat16, QMODE>(yb, sq, rq);
+            }
+          }
         }
       }
       __syncwarp();
@@ -314,7 +339,9 @@ struct RopeLayout {
   static constexpr int kFixed = kWeights + kFreq;
   __host__ __device__ static constexpr int stage_bytes(bool copy_v) { return (copy_v ? 3 : 2) * 4096 * 2; }
   __host__ __device__ static constexpr int stages(bool copy_v) {
-    return ((kDynLimit - kFixed) / stage_bytes(copy_v)) > kMaxStages ? kMaxStages : ((kDynLimit - kFixed) / stage_bytes(copy_v));
+    return ring_stages(((kDynLimit - kFixed) / stage_bytes(copy_v)) > kMaxStages
+                           ? kMaxStages
+                           : ((kDynLimit - kFixed) / stage_bytes(copy_v)));
   }
   __host__ __device__ static constexpr int smem_bytes(bool copy_v) { return kFixed + stages(copy_v) * stage_bytes(copy_v); }
 };
@@ -434,7 +461,8 @@ __device__ __forceinline__ void rope_pair(const uint4* row, const float* w, int 
 template <typename WT, typename CsT, bool GEN, bool COPY_V>
 __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeArgs a, RopeSource src) {
   pdl_trigger();
-  constexpr int S = RopeLayout::stages(COPY_V);
+  constexpr int S = RopeLayout::stages(COPY_V);  // a multiple of W
+  constexpr int W = ring_warps(S);
   constexpr uint32_t SB = RopeLayout::stage_bytes(COPY_V);
   extern __shared__ uint8_t smem_raw[];
   __shared__ Ring ring;
@@ -474,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeA
     volatile int* abort = &ring.abort;
     const CsT* cosb = static_cast<const CsT*>(a.cos);
     const CsT* sinb = static_cast<const CsT*>(a.sin);
-    for (int k = static_cast<int>(warp); k < n; k += kConsumerWarps) {
+    for (int k = static_cast<int>(warp); warp < W && k < n; k += W) {
       const int st = k % S;
       if (!mbar_wait(&ring.full[st], (k / S) & 1, abort)) break;
       const uint8_t* stage = stages + static_cast<size_t>(st) * SB;
@@ -546,13 +574,15 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeA
 // ((x * inv_rms) * w, one bf16 rounding); the row is staged whole before its first store, so the output
 // may alias the input.
 constexpr int kRmsFixed = 2 * 4096 * 4;  // Q and K weights as fp32
-constexpr int kRmsStages = ((kDynLimit - kRmsFixed) / 8192) > kMaxStages ? kMaxStages : ((kDynLimit - kRmsFixed) / 8192);
+constexpr int kRmsStages =
+    ring_stages(((kDynLimit - kRmsFixed) / 8192) > kMaxStages ? kMaxStages : ((kDynLimit - kRmsFixed) / 8192));
 constexpr int kRmsSmem = kRmsFixed + kRmsStages * 8192;
 
 template <typename WT>
 __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_ring_kernel(RmsRowsArgs a) {
   pdl_trigger();
-  constexpr int S = kRmsStages;
+  constexpr int S = kRmsStages;  // a multiple of W
+  constexpr int W = ring_warps(S);
   extern __shared__ uint8_t smem_raw[];
   __shared__ Ring ring;
   uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 127u) & ~127u) - smem_u32(smem_raw));
@@ -586,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_ring_kernel(RmsRowsArg
     }
   } else {
     volatile int* abort = &ring.abort;
-    for (int k = static_cast<int>(warp); k < n; k += kConsumerWarps) {
+    for (int k = static_cast<int>(warp); warp < W && k < n; k += W) {
       const int st = k % S;
       if (!mbar_wait(&ring.full[st], (k / S) & 1, abort)) break;
       const uint4* row = reinterpret_cast<const uint4*>(stages + static_cast<size_t>(st) * 8192);

@@ -261,6 +261,50 @@ def fused_adazero_from_ada_fp8(
     return (q, y) if return_bf16 else q
 
 
+def fused_adazero_from_ada_fp8_planes(
+    x: torch.Tensor,
+    eps: float,
+    scale_shift_table: torch.Tensor,
+    timestep: torch.Tensor,
+    input_scales: torch.Tensor,
+    *,
+    shift_index: int,
+    scale_index: int,
+    out: torch.Tensor | None = None,
+    quant_mode: int = QUANT_TORCH,
+) -> torch.Tensor:
+    """AdaZero fused with up to three E4M3 quantisers of the same bf16 output: plane i of the result
+    [n, *x.shape] equals ``fused_adazero_from_ada_fp8(..., input_scales[i])`` bit for bit, with x read once.
+
+    For a checkpoint whose Q, K and V linears carry different input scales, where the reference quantises
+    the bf16 AdaZero output once per linear inside FP8Linear.forward (ltx_serve/triton_ltx_ops.py:1692,
+    :1676-1716).  ``input_scales``: float32 [n] on the device, n in 1..3; ``out``: e4m3 [n, *x.shape]."""
+    global _VIDEO_ADA_VALUES_CALLS
+    reason = ada_from_table_guard_reason(x, scale_shift_table, timestep)
+    if reason is not None:
+        raise ValueError(reason)
+    _check_index(scale_shift_table, shift_index, scale_index)
+    n = input_scales.numel()
+    if (n < 1 or n > 3 or not input_scales.is_cuda or input_scales.dtype != torch.float32
+            or not input_scales.is_contiguous()):
+        raise ValueError("input_scale")
+    if out is None:
+        out = torch.empty((n, *x.shape), device=x.device, dtype=torch.float8_e4m3fn)
+    if out.dtype != torch.float8_e4m3fn or tuple(out.shape) != (n, *x.shape) or not out.is_contiguous():
+        raise ValueError("out_shape")
+    _VIDEO_ADA_VALUES_CALLS += 1
+    ts_view = _ts_view(x, scale_shift_table, timestep)
+    _lib.call(
+        "ogx_adazero_from_ada_e4m3_planes",
+        x.data_ptr(), x.shape[0], x.shape[1], x.shape[2],
+        scale_shift_table.data_ptr(), _code(scale_shift_table), scale_shift_table.stride(0),
+        ts_view.data_ptr(), _code(ts_view), ts_view.stride(0), ts_view.stride(1), ts_view.stride(2),
+        shift_index, scale_index, float(eps), input_scales.data_ptr(), n, int(quant_mode), None, out.data_ptr(),
+        out.stride(0), _stream(x),
+    )
+    return out
+
+
 def fused_head_gate_mul_bf16(out: torch.Tensor, gates: torch.Tensor, heads: int, dim_head: int) -> torch.Tensor:
     """``out.view(B, L, H, d) * gates[..., None]`` (bf16): the optional per-head gate of the attention output.
 
@@ -737,6 +781,52 @@ def fp8_scaled_mm(
     return out if given else out.reshape(*qinput.shape[:-1], N)
 
 
+def fp8_scaled_mm_planes(
+    qplanes: torch.Tensor,
+    weight: torch.Tensor,
+    scales_a: torch.Tensor,
+    scales_b: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``fp8_scaled_mm`` over n activation planes: output columns [i*N/n, (i+1)*N/n) are
+    ``bf16(qplanes[i] @ weight[i*N/n:(i+1)*N/n].t() * scales_a[i] * scales_b[i]) (+ bf16(bias))``, one launch.
+
+    The packed Q/K/V projection of a checkpoint whose three linears quantise their input with different
+    scales (the reference runs FP8Linear.forward once per linear, ltx_serve/triton_ltx_ops.py:1695-1707).
+    ``qplanes``: e4m3 [n, ..., K] (each plane contiguous rows); ``scales_a``, ``scales_b``: float32 [n];
+    N / n a multiple of 256.  Returns bf16 [M, N] (or the caller's ``out``)."""
+    _require_cuda(qplanes, weight, scales_a, scales_b)
+    if qplanes.dtype != torch.float8_e4m3fn or weight.dtype != torch.float8_e4m3fn:
+        raise ValueError("fp8_dtype")
+    n = qplanes.shape[0]
+    K = qplanes.shape[-1]
+    a3 = qplanes.reshape(n, -1, K)
+    if not a3.is_contiguous() or weight.stride(-1) != 1 or weight.ndim != 2 or weight.shape[1] != K:
+        raise ValueError("fp8_shape")
+    M = a3.shape[1]
+    N = weight.shape[0]
+    if (scales_a.numel() != n or scales_b.numel() != n or scales_a.dtype != torch.float32
+            or scales_b.dtype != torch.float32 or N % n):
+        raise ValueError("scale")
+    given = out is not None
+    if out is None:
+        out = torch.empty((M, N), device=qplanes.device, dtype=torch.bfloat16)
+    if out.dtype != torch.bfloat16 or out.ndim != 2 or out.shape != (M, N) or out.stride(1) != 1:
+        raise ValueError("out_shape: out must be a [M, N] bf16 matrix with unit column stride")
+    if bias is not None and (bias.ndim != 1 or bias.shape[0] != N):
+        raise ValueError("bias_shape")
+    _lib.call(
+        "ogx_fp8_scaled_mm_planes",
+        a3.data_ptr(), n, M, K, a3.stride(1), weight.data_ptr(), N, weight.stride(0),
+        scales_a.contiguous().data_ptr(), scales_b.contiguous().data_ptr(),
+        _ptr(bias.contiguous()) if bias is not None else None, _code(bias) if bias is not None else DTYPE_BF16,
+        out.data_ptr(), out.stride(0), _stream(qplanes),
+    )
+    return out
+
+
 def fp8_scaled_mm_gelu_e4m3(
     qinput: torch.Tensor,
     weight: torch.Tensor,
@@ -970,11 +1060,13 @@ __all__ = [
     "fp8_qkv_from_shared_quantized_input",
     "fp8_scaled_mm",
     "fp8_scaled_mm_gelu_e4m3",
+    "fp8_scaled_mm_planes",
     "fp8_scaled_mm_residual_gate",
     "fused_adaln_affine_from_ada",
     "fused_adazero",
     "fused_adazero_from_ada",
     "fused_adazero_from_ada_fp8",
+    "fused_adazero_from_ada_fp8_planes",
     "fused_bias_add_bf16",
     "fused_fp8_quantize_e4m3",
     "fused_gelu_tanh_fp8_quantize_e4m3",

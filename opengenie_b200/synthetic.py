@@ -297,8 +297,9 @@ class BlockInputs:
         return BlockInputs(self.x.to(device), ts, self.cos.to(device), self.sin.to(device))
 
 
-def make_inputs(cfg: BlockConfig, seed: int = 1, *, dim: int = DIM) -> BlockInputs:
-    """Seeded block inputs (CPU) for one configuration."""
+def make_inputs(cfg: BlockConfig, seed: int = 1, *, dim: int = DIM, slots: int = ADA_SLOTS) -> BlockInputs:
+    """Seeded block inputs (CPU) for one configuration; ``slots`` Ada slots in the timestep embedding (6 for
+    the self-attention and FFN branches, 9 with the text cross-attention)."""
     g = torch.Generator().manual_seed(seed)
     L = cfg.tokens
     x = torch.randn((1, L, dim), generator=g)
@@ -307,15 +308,45 @@ def make_inputs(cfg: BlockConfig, seed: int = 1, *, dim: int = DIM) -> BlockInpu
         x[:, :clean_tokens] *= 0.5
     x = x.to(torch.bfloat16)
     if cfg.per_token_timestep:
-        ts_clean = torch.randn((ADA_SLOTS * dim,), generator=g)
-        ts_noisy = torch.randn((ADA_SLOTS * dim,), generator=g)
+        ts_clean = torch.randn((slots * dim,), generator=g)
+        ts_noisy = torch.randn((slots * dim,), generator=g)
         is_clean = (torch.arange(L) < clean_tokens)[:, None]
         ts = torch.where(is_clean, ts_clean[None], ts_noisy[None]).unsqueeze(0).to(torch.bfloat16).contiguous()
     else:
-        ts_vec = torch.randn((ADA_SLOTS * dim,), generator=g).to(torch.bfloat16)
-        ts = ts_vec.view(1, 1, -1).expand(1, L, ADA_SLOTS * dim)
+        ts_vec = torch.randn((slots * dim,), generator=g).to(torch.bfloat16)
+        ts = ts_vec.view(1, 1, -1).expand(1, L, slots * dim)
     cos, sin = rope_tables(cfg.frames, cfg.grid_h, cfg.grid_w)
     return BlockInputs(x, ts, cos, sin)
+
+
+@dataclass
+class LayerInputs:
+    """Inputs of one DiT layer's video branches with the text cross-attention: the video tokens, their 9-slot
+    timestep embedding (slots 0-2 self-attention, 3-5 FFN, 6-8 text cross-attention), the RoPE tables and the
+    prompt context with its 2-slot timestep embedding."""
+
+    x: torch.Tensor  # bf16 [1, L, D]
+    timestep: torch.Tensor  # bf16 [1, L, 9*D] (stride-0 over tokens when uniform)
+    cos: torch.Tensor
+    sin: torch.Tensor
+    context: torch.Tensor  # bf16 [1, L_ctx, D]
+    prompt_timestep: torch.Tensor  # bf16 [1, L_ctx, 2*D], stride-0 over tokens
+
+    def to(self, device) -> "LayerInputs":
+        b = BlockInputs(self.x, self.timestep, self.cos, self.sin).to(device)
+        pts = self.prompt_timestep[:, :1].to(device).expand(self.prompt_timestep.shape)
+        return LayerInputs(b.x, b.timestep, b.cos, b.sin, self.context.to(device), pts)
+
+
+def make_layer_inputs(cfg: BlockConfig, context_tokens: int = TEXT_CONTEXT_TOKENS, seed: int = 1, *,
+                      dim: int = DIM) -> LayerInputs:
+    """Seeded inputs (CPU) of a layer with the text cross-attention: ``make_inputs`` with 9 Ada slots, then the
+    prompt context ~ N(0, 1) and its uniform 2-slot timestep embedding from a second generator."""
+    b = make_inputs(cfg, seed, dim=dim, slots=TEXT_ADA_SLOTS)
+    g = torch.Generator().manual_seed(seed + 7919)
+    context = torch.randn((1, context_tokens, dim), generator=g).to(torch.bfloat16)
+    pts = torch.randn((PROMPT_ADA_SLOTS * dim,), generator=g).to(torch.bfloat16).view(1, 1, -1)
+    return LayerInputs(b.x, b.timestep, b.cos, b.sin, context, pts.expand(1, context_tokens, -1))
 
 
 def small_config(tokens_frames: int = 1, grid_h: int = 2, grid_w: int = 8, **kw) -> BlockConfig:

@@ -214,15 +214,23 @@ class UlyssesVideoSelfAttention:
         w = self.w
         p = self.plan
         Ll = x_loc.shape[1]
-        with self._phase("adazero_quant"):
-            xq = ltx_ops.fused_adazero_from_ada_fp8(x_loc, w.norm_eps, w.scale_shift_table, ts_loc,
-                                                    w.to_q.input_scale, shift_index=0, scale_index=1)
         qkv = ws["qkv"]
         if qkv.shape != (Ll, 3 * 4096) or not qkv.is_contiguous():
             raise ValueError("qkv workspace shape")
-        with self._phase("qkv_gemm"):
-            ltx_ops.fp8_scaled_mm(xq, self.blk.w_qkv, w.to_q.input_scale, self.blk.s_qkv, bias=self.blk.b_qkv,
-                                  out=qkv, n_per_scale=4096)
+        if self.blk.shared_quant:
+            with self._phase("adazero_quant"):
+                xq = ltx_ops.fused_adazero_from_ada_fp8(x_loc, w.norm_eps, w.scale_shift_table, ts_loc,
+                                                        w.to_q.input_scale, shift_index=0, scale_index=1)
+            with self._phase("qkv_gemm"):
+                ltx_ops.fp8_scaled_mm(xq, self.blk.w_qkv, w.to_q.input_scale, self.blk.s_qkv, bias=self.blk.b_qkv,
+                                      out=qkv, n_per_scale=4096)
+        else:  # Q, K and V linears with different input scales: one e4m3 copy of the activations per linear
+            with self._phase("adazero_quant"):
+                xq3 = ltx_ops.fused_adazero_from_ada_fp8_planes(x_loc, w.norm_eps, w.scale_shift_table, ts_loc,
+                                                               self.blk.s_in3, shift_index=0, scale_index=1)
+            with self._phase("qkv_gemm"):
+                ltx_ops.fp8_scaled_mm_planes(xq3, self.blk.w_qkv, self.blk.s_in3, self.blk.s_qkv,
+                                             bias=self.blk.b_qkv, out=qkv)
         send = ws["send1"]
         D = 4096
         positions = isinstance(rope[0], ltx_ops.RopePositions)
@@ -346,7 +354,7 @@ class UlyssesVideoSelfAttention:
         s_in = (amax.clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
         for lin in (w.to_q, w.to_k, w.to_v):
             lin.input_scale = s_in.clone()
-        self.blk.shared_quant = True
+        self.blk.input_scales_changed()
         ws = self.workspace(Ll)
         rope = (pe, t0) if isinstance(pe, ltx_ops.RopePositions) else (pe[0][:, :, t0:t0 + Ll], pe[1][:, :, t0:t0 + Ll])
         q, k, v = self._qkv_and_exchange(x_loc, ts_loc, rope, ws)

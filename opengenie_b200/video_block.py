@@ -31,6 +31,8 @@ from .synthetic import FP8_MAX, BlockWeights
 class VideoSelfAttentionBlock:
     """One DiT layer's video self-attention branch with weights resident in HBM."""
 
+    kernel_launches_per_step = 5  # without the optional per-head gate
+
     def __init__(self, weights: BlockWeights, device: torch.device | str = "cuda", *, to_gate_logits=None):
         """``to_gate_logits``: for checkpoints with gated attention, the module (or callable) mapping the
         AdaZero output [1, L, D] bf16 to per-head gate logits [1, L, H]; the attention output is then
@@ -45,10 +47,25 @@ class VideoSelfAttentionBlock:
         self.w_qkv = torch.cat([w.to_q.weight, w.to_k.weight, w.to_v.weight], dim=0).contiguous()
         self.s_qkv = torch.stack([w.to_q.weight_scale, w.to_k.weight_scale, w.to_v.weight_scale]).reshape(3).contiguous()
         self.b_qkv = torch.cat([w.to_q.bias, w.to_k.bias, w.to_v.bias]).contiguous()
+        # the per-linear weights, scales and biases become views of the packed copies: one copy in HBM
+        D = w.to_q.weight.shape[0]
+        for i, lin in enumerate((w.to_q, w.to_k, w.to_v)):
+            lin.weight = self.w_qkv[i * D:(i + 1) * D]
+            lin.weight_scale = self.s_qkv[i]
+            lin.bias = self.b_qkv[i * D:(i + 1) * D]
+        self.input_scales_changed()
+        self._ws: dict[int, dict[str, torch.Tensor]] = {}
+
+    def input_scales_changed(self) -> None:
+        """Re-reads the Q/K/V input scales: whether one quantiser serves all three linears, and the packed
+        [3] scales of the per-linear path.  Called at construction and by calibrate_input_scales; a caller
+        that replaces the input scales by hand calls it too (it compares device scalars, which synchronises,
+        so not inside a graph capture)."""
+        w = self.w
         self.shared_quant = bool(
             torch.equal(w.to_q.input_scale, w.to_k.input_scale) and torch.equal(w.to_q.input_scale, w.to_v.input_scale)
         )
-        self._ws: dict[int, dict[str, torch.Tensor]] = {}
+        self.s_in3 = torch.stack([w.to_q.input_scale, w.to_k.input_scale, w.to_v.input_scale]).reshape(3).contiguous()
 
     # ------------------------------------------------------------------ workspace
     def workspace(self, tokens: int) -> dict[str, torch.Tensor]:
@@ -81,13 +98,15 @@ class VideoSelfAttentionBlock:
                 ltx_ops_xq, self.w_qkv, w.to_q.input_scale, self.s_qkv, bias=self.b_qkv, out=ws["qkv"], n_per_scale=D
             )
         else:
-            norm = ltx_ops.fused_adazero_from_ada(vx, w.norm_eps, w.scale_shift_table, timestep, shift_index=0, scale_index=1)
-            ws["norm"] = norm
-            for i, lin in enumerate((w.to_q, w.to_k, w.to_v)):
-                xq = ltx_ops.fused_fp8_quantize_e4m3(norm, lin.input_scale)
-                ltx_ops.fp8_scaled_mm(
-                    xq, lin.weight, lin.input_scale, lin.weight_scale, bias=lin.bias, out=ws["qkv"][:, i * D:(i + 1) * D]
-                )
+            # a checkpoint whose Q, K and V linears quantise their input with different scales: one AdaZero
+            # launch writes the three e4m3 copies, one GEMM launch reads copy i for output columns of linear i
+            if self.to_gate_logits is not None:
+                ws["norm"] = ltx_ops.fused_adazero_from_ada(vx, w.norm_eps, w.scale_shift_table, timestep,
+                                                            shift_index=0, scale_index=1)
+            xq3 = ltx_ops.fused_adazero_from_ada_fp8_planes(vx, w.norm_eps, w.scale_shift_table, timestep, self.s_in3,
+                                                           shift_index=0, scale_index=1, out=ws.get("xq3"))
+            ws["xq3"] = xq3
+            ltx_ops.fp8_scaled_mm_planes(xq3, self.w_qkv, self.s_in3, self.s_qkv, bias=self.b_qkv, out=ws["qkv"])
         return ws["qkv"]
 
     def forward(
@@ -169,7 +188,7 @@ class VideoSelfAttentionBlock:
         s_in = (norm.float().abs().amax().clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
         for lin in (w.to_q, w.to_k, w.to_v):
             lin.input_scale = s_in.clone()
-        self.shared_quant = True
+        self.input_scales_changed()
         ws = self.workspace(vx.shape[1])
         qkv = self.qkv_projection(vx, timestep, ws)
         q = qkv[:, :D].unsqueeze(0)

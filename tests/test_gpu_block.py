@@ -324,3 +324,43 @@ def test_gated_attention_block(ogx_lib):
                                               bw.to_out.bias, inp.x, bw.scale_shift_table, inp.timestep, gate_index=2)
     assert torch.equal(out, ref)
     assert status_clean()
+
+
+@pytest.mark.parametrize("name", ["small", "c1_l9216"])
+def test_block_with_distinct_qkv_input_scales_equals_per_linear_composition(ogx_lib, name):
+    """A checkpoint whose Q, K and V linears quantise their input with different scales: the block's two
+    launches (three e4m3 copies from one AdaZero, one GEMM over the three planes) give the same Q/K/V and
+    the same block output as the reference's order of operations (bf16 AdaZero, then per linear its own
+    quantiser and FP8 GEMM), bit for bit."""
+    from opengenie_b200 import ltx_ops, synthetic
+    from opengenie_b200.video_block import VideoSelfAttentionBlock
+
+    cfg = synthetic.small_config(2, 6, 25) if name == "small" else synthetic.CONFIGS[name]
+    inp = synthetic.make_inputs(cfg, seed=71).to("cuda")
+    pe = (inp.cos, inp.sin)
+    blk = VideoSelfAttentionBlock(synthetic.make_weights(seed=72), "cuda")
+    blk.calibrate_input_scales(inp.x, inp.timestep, pe)
+    w = blk.w
+    w.to_k.input_scale = (w.to_q.input_scale * 1.25).contiguous()
+    w.to_v.input_scale = (w.to_q.input_scale * 0.8).contiguous()
+    blk.input_scales_changed()
+    assert not blk.shared_quant
+    out = blk(inp.x, inp.timestep, pe).clone()
+    qkv = blk.workspace(cfg.tokens)["qkv"].clone()  # Q and K after RoPE, V as projected
+
+    D = 4096
+    norm = ltx_ops.fused_adazero_from_ada(inp.x, w.norm_eps, w.scale_shift_table, inp.timestep, shift_index=0,
+                                         scale_index=1)
+    ref_qkv = torch.empty_like(qkv)
+    for i, lin in enumerate((w.to_q, w.to_k, w.to_v)):
+        xq = ltx_ops.fused_fp8_quantize_e4m3(norm, lin.input_scale)
+        ltx_ops.fp8_scaled_mm(xq, lin.weight, lin.input_scale, lin.weight_scale.reshape(1), bias=lin.bias,
+                              out=ref_qkv[:, i * D:(i + 1) * D])
+    q, k, v = (ref_qkv[:, i * D:(i + 1) * D].unsqueeze(0) for i in range(3))
+    blk.rope(q, k, pe)
+    assert torch.equal(qkv, ref_qkv)
+    oq = ltx_ops.attention(q, k, v, 32, out_e4m3_scale=w.to_out.input_scale)
+    ref = ltx_ops.fp8_scaled_mm_residual_gate(oq, w.to_out.weight, w.to_out.input_scale, w.to_out.weight_scale,
+                                             w.to_out.bias, inp.x, w.scale_shift_table, inp.timestep, gate_index=2)
+    assert torch.equal(out, ref)
+    assert status_clean()

@@ -76,6 +76,25 @@ def test_fp8_gemm_strided_output_columns(ops):
     assert (big[:, :256] == 0).all() and (big[:, 512:] == 0).all()
 
 
+@pytest.mark.parametrize("M,K", [(300, 4096), (1152, 1024), (9216, 4096)])
+def test_fp8_gemm_planes_equal_one_gemm_per_plane(ops, M, K):
+    """The packed Q/K/V GEMM over three activation planes (one e4m3 copy per linear, each with its own
+    input scale) equals three GEMMs, one per plane and weight segment, bit for bit."""
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    N = 3 * 4096
+    a3 = (torch.randn((3, M, K), device="cuda", generator=g) * 40).to(torch.float8_e4m3fn)
+    w = (torch.randn((N, K), device="cuda", generator=g) * 40).to(torch.float8_e4m3fn)
+    s_a = torch.tensor([0.011, 0.017, 0.0053], device="cuda")
+    s_b = torch.tensor([0.0021, 0.0013, 0.0034], device="cuda")
+    bias = (torch.randn(N, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    out = ops.fp8_scaled_mm_planes(a3, w, s_a, s_b, bias=bias)
+    for i in range(3):
+        seg = slice(i * 4096, (i + 1) * 4096)
+        ref = ops.fp8_scaled_mm(a3[i], w[seg], s_a[i].clone(), s_b[i].clone().reshape(1), bias=bias[seg])
+        assert torch.equal(out[:, seg], ref), i
+    assert status_clean()
+
+
 @pytest.mark.parametrize("N", [12288, 16384])
 def test_fp8_gemm_full_size_vs_cublas(ops, N):
     """C3: M=9216, K=4096, N in {12288, 16384} against torch._scaled_mm (cuBLASLt) on the same GPU."""

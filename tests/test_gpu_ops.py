@@ -131,6 +131,23 @@ def test_adazero_fused_quant_equals_separate_quant(ops):
     assert np.array_equal(codes(q_only), codes(q))
 
 
+@pytest.mark.parametrize("planes", [1, 2, 3])
+@pytest.mark.parametrize("uniform", [True, False])
+def test_adazero_fp8_planes_equal_one_call_per_scale(ops, planes, uniform):
+    """The multi-scale AdaZero (one e4m3 copy per input scale, x read once) equals one fused AdaZero+quant
+    call per scale, code for code, for token-uniform and per-token timesteps."""
+    x, table, ts = _ada_case(300, 4096, torch.float32, torch.bfloat16, uniform, seed=17 + planes)
+    x, table = x.cuda(), table.cuda()
+    ts = ts[:, :1].cuda().expand(ts.shape) if uniform else ts.cuda()
+    scales = torch.tensor([0.0123, 0.0071, 0.0302][:planes], device="cuda")
+    q3 = ops.fused_adazero_from_ada_fp8_planes(x, 1e-6, table, ts, scales, shift_index=0, scale_index=1)
+    assert q3.shape == (planes, *x.shape)
+    for i in range(planes):
+        qi = ops.fused_adazero_from_ada_fp8(x, 1e-6, table, ts, scales[i].clone(), shift_index=0, scale_index=1)
+        assert np.array_equal(codes(q3[i]), codes(qi)), i
+    assert status_clean()
+
+
 @pytest.mark.parametrize("rows", [1157, 2307, 4609])
 def test_adazero_rows_per_cta_widths_vs_oracle(ops, rows):
     """Row counts whose grids give each CTA 2, 4 and 8 rows (the host spreads short inputs over at least

@@ -64,9 +64,10 @@ def test_static_barrier_rejects_a_device_named_twice(ogx_lib):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in this process")
 def test_static_barrier_across_two_gpus_of_one_process(ogx_lib):
-    """The part the one-GPU case cannot reach: each device's copy of the array looked up on its own
-    device, and the stores into the other GPU's copy (plain peer stores, no multicast).  Two ranks on
-    GPUs 0 and 1 of this process, each on its own stream, pass two barriers together."""
+    """The part the one-GPU case cannot reach: each device's own count looked up on that device, and the
+    arrivals crossing between the GPUs through the library's page-locked host slots (no GPU touches the
+    other's memory).  Two ranks on GPUs 0 and 1 of this process, each on its own stream, pass two
+    barriers together."""
     from opengenie_b200 import _lib
 
     counts = [torch.zeros(1, dtype=torch.int32, device=f"cuda:{d}") for d in (0, 1)]
