@@ -881,12 +881,10 @@ def main() -> None:
     attn_ms = blk.time_attention(args.steps, args.warmup) if hasattr(blk, "time_attention") else None
     attn_ms = max_over_ranks(attn_ms, pg) if attn_ms is not None else None
     phases = None
-    if args.phases and hasattr(blk, "phase_summary"):
-        blk.profile = True
-        for _ in range(5):
-            step()
-        blk.profile = False
-        phases = blk.phase_summary()
+    if args.phases and hasattr(blk, "time_stages"):
+        # each stage replayed alone from a CUDA graph (device time, max over ranks); NVLink exchange only
+        stage_ms = blk.time_stages(x_loc, inp.timestep, pe, args.steps, args.warmup)
+        phases = {name: max_over_ranks(ms_, pg) for name, ms_ in stage_ms.items()} or None
     status = _lib.device_status(clear=True)
 
     if rank == 0:
@@ -927,6 +925,8 @@ def main() -> None:
         }
         if phases is not None:
             line["phases_ms"] = phases
+            line["phases_method"] = ("each stage of the step replayed alone from a CUDA graph on the buffers of a "
+                                     "full step, CUDA events, max over ranks; exchange stages include their barrier")
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_reference(args.config, 3, 1, budget_s=30.0)
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}

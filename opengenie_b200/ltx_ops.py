@@ -232,12 +232,13 @@ def fused_adazero_from_ada_fp8(
     scale_index: int,
     return_bf16: bool = False,
     quant_mode: int = QUANT_TORCH,
+    out: torch.Tensor | None = None,
 ) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
     """AdaZero fused with the E4M3 quantiser of the following FP8 linear.
 
     Equals ``fused_fp8_quantize_e4m3(fused_adazero_from_ada(...), input_scale)``
     bit for bit (reference :40-91 then :144-161), without writing the bf16
-    activation unless ``return_bf16``.
+    activation unless ``return_bf16``.  ``out``: a caller-provided e4m3 output of x's shape.
     """
     global _VIDEO_ADA_VALUES_CALLS
     reason = ada_from_table_guard_reason(x, scale_shift_table, timestep)
@@ -248,7 +249,9 @@ def fused_adazero_from_ada_fp8(
         raise ValueError("input_scale")
     _VIDEO_ADA_VALUES_CALLS += 1
     ts_view = _ts_view(x, scale_shift_table, timestep)
-    q = torch.empty(x.shape, device=x.device, dtype=torch.float8_e4m3fn)
+    if out is not None and (out.dtype != torch.float8_e4m3fn or out.shape != x.shape or not out.is_contiguous()):
+        raise ValueError("out_shape")
+    q = out if out is not None else torch.empty(x.shape, device=x.device, dtype=torch.float8_e4m3fn)
     y = torch.empty_like(x) if return_bf16 else None
     _lib.call(
         "ogx_adazero_from_ada_e4m3",

@@ -187,6 +187,8 @@ class UlyssesVideoSelfAttention:
             p = self.plan
             L = tokens_local * p.world
             ws = {
+                "xq": torch.empty((1, tokens_local, 4096), device=self.device, dtype=torch.float8_e4m3fn),
+                "xq3": torch.empty((3, 1, tokens_local, 4096), device=self.device, dtype=torch.float8_e4m3fn),
                 "qkv": torch.empty((tokens_local, 3 * 4096), device=self.device, dtype=torch.bfloat16),
                 "send1": torch.empty(p.qkv_send_shape(tokens_local), device=self.device, dtype=torch.bfloat16),
                 "recv1": torch.empty(p.qkv_send_shape(tokens_local), device=self.device, dtype=torch.bfloat16),
@@ -209,6 +211,84 @@ class UlyssesVideoSelfAttention:
         return t[:, t0:t1]
 
     # ------------------------------------------------------------------ stages
+    def _rope_source(self, rope, Ll: int) -> tuple:
+        """The rope arguments of the entry points: (cos, sin) tables of this rank's tokens, or
+        (RopePositions, first token of the slice) -> frequency tables, grid, first token."""
+        if isinstance(rope[0], ltx_ops.RopePositions):
+            pos, token0 = rope
+            reason = ltx_ops.rope_positions_guard_reason(pos, self.device)
+            if reason is None and (token0 < 0 or token0 + Ll > pos.tokens):
+                reason = "rope_shape"
+            if reason is not None:
+                raise ValueError(reason)
+            return True, (pos.inv_freq.data_ptr(), pos.slot_axis.data_ptr(), pos.grid_h, pos.grid_w, int(token0))
+        cos_loc, sin_loc = rope
+        if cos_loc.shape[2] != Ll or sin_loc.shape != cos_loc.shape:
+            raise ValueError("rope_shape")
+        return False, (cos_loc.data_ptr(), sin_loc.data_ptr(), ltx_ops._code(cos_loc), cos_loc.stride(1),
+                       cos_loc.stride(2))
+
+    def _stage_adazero(self, x_loc, ts_loc, ws) -> None:
+        w = self.w
+        if self.blk.shared_quant:
+            ltx_ops.fused_adazero_from_ada_fp8(x_loc, w.norm_eps, w.scale_shift_table, ts_loc, w.to_q.input_scale,
+                                               shift_index=0, scale_index=1, out=ws["xq"])
+        else:  # Q, K and V linears with different input scales: one e4m3 copy of the activations per linear
+            ltx_ops.fused_adazero_from_ada_fp8_planes(x_loc, w.norm_eps, w.scale_shift_table, ts_loc, self.blk.s_in3,
+                                                      shift_index=0, scale_index=1, out=ws["xq3"])
+
+    def _stage_qkv_gemm(self, ws) -> None:
+        w = self.w
+        if self.blk.shared_quant:
+            ltx_ops.fp8_scaled_mm(ws["xq"], self.blk.w_qkv, w.to_q.input_scale, self.blk.s_qkv, bias=self.blk.b_qkv,
+                                  out=ws["qkv"], n_per_scale=4096)
+        else:
+            ltx_ops.fp8_scaled_mm_planes(ws["xq3"], self.blk.w_qkv, self.blk.s_in3, self.blk.s_qkv,
+                                         bias=self.blk.b_qkv, out=ws["qkv"])
+
+    def _stage_rope_to_peers(self, Ll: int, rope, ws) -> None:
+        """Q/K RMSNorm + RoPE storing each head group into its rank's receive buffer, then the barrier."""
+        w, p = self.w, self.plan
+        qkv = ws["qkv"]
+        D = 4096
+        positions, src = self._rope_source(rope, Ll)
+        _lib.call(
+            "ogx_video_qkv_rmsnorm_rope_positions_to_peers" if positions else "ogx_video_qkv_rmsnorm_rope_to_peers",
+            qkv.data_ptr(), qkv[:, D:].data_ptr(), qkv[:, 2 * D:].data_ptr(), Ll, qkv.stride(0),
+            w.q_norm_weight.data_ptr(), w.k_norm_weight.data_ptr(), ltx_ops._code(w.q_norm_weight),
+            float(w.qk_eps), *src, ws["recv1_dst"], p.world, 3 * p.heads_local * p.head_dim,
+            ltx_ops._stream(qkv),
+        )
+
+    def _stage_attention_to_peers(self, L: int, Ll: int, ws) -> None:
+        """Attention on this rank's heads, each output row stored into the owning rank's receive buffer."""
+        w, p = self.w, self.plan
+        q, k, v = p.attention_views(ws["recv1"], L)
+        _lib.call(
+            "ogx_attention_fwd_e4m3_to_peers",
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), L, p.heads_local, q.stride(1), 128 ** -0.5,
+            w.to_out.input_scale.data_ptr(), ws["recv2_dst"], p.world, Ll, p.heads_local * p.head_dim,
+            ltx_ops._stream(q),
+        )
+
+    def _stage_out_proj(self, x_loc, ts_loc, ws, out) -> None:
+        w, p = self.w, self.plan
+        Ll = x_loc.shape[1]
+        ts_view = ltx_ops._ts_view(x_loc, w.scale_shift_table, ts_loc)
+        recv2 = ws["recv2"]
+        if (recv2.shape != p.out_send_shape(Ll) or ts_view.shape[1] != Ll or x_loc.shape != out.shape
+                or not out.is_contiguous()):
+            raise ValueError("out_projection_shape")
+        _lib.call(
+            "ogx_fp8_scaled_mm_residual_gate_kblocked",
+            recv2.data_ptr(), Ll, 4096, p.heads_local * p.head_dim, w.to_out.weight.data_ptr(), 4096,
+            w.to_out.weight.stride(0), w.to_out.input_scale.data_ptr(), w.to_out.weight_scale.data_ptr(), 4096,
+            w.to_out.bias.data_ptr(), ltx_ops._code(w.to_out.bias), x_loc.data_ptr(), x_loc.stride(1),
+            w.scale_shift_table.data_ptr(), ltx_ops._code(w.scale_shift_table), w.scale_shift_table.stride(0),
+            ts_view.data_ptr(), ltx_ops._code(ts_view), ts_view.stride(1), ts_view.stride(2), 2,
+            out.data_ptr(), out.stride(1), ltx_ops._stream(x_loc),
+        )
+
     def _qkv_and_exchange(self, x_loc, ts_loc, rope, ws):
         """``rope``: (cos, sin) tables of this rank's tokens, or (RopePositions, first token of the slice)."""
         w = self.w
@@ -217,52 +297,21 @@ class UlyssesVideoSelfAttention:
         qkv = ws["qkv"]
         if qkv.shape != (Ll, 3 * 4096) or not qkv.is_contiguous():
             raise ValueError("qkv workspace shape")
-        if self.blk.shared_quant:
-            with self._phase("adazero_quant"):
-                xq = ltx_ops.fused_adazero_from_ada_fp8(x_loc, w.norm_eps, w.scale_shift_table, ts_loc,
-                                                        w.to_q.input_scale, shift_index=0, scale_index=1)
-            with self._phase("qkv_gemm"):
-                ltx_ops.fp8_scaled_mm(xq, self.blk.w_qkv, w.to_q.input_scale, self.blk.s_qkv, bias=self.blk.b_qkv,
-                                      out=qkv, n_per_scale=4096)
-        else:  # Q, K and V linears with different input scales: one e4m3 copy of the activations per linear
-            with self._phase("adazero_quant"):
-                xq3 = ltx_ops.fused_adazero_from_ada_fp8_planes(x_loc, w.norm_eps, w.scale_shift_table, ts_loc,
-                                                               self.blk.s_in3, shift_index=0, scale_index=1)
-            with self._phase("qkv_gemm"):
-                ltx_ops.fp8_scaled_mm_planes(xq3, self.blk.w_qkv, self.blk.s_in3, self.blk.s_qkv,
-                                             bias=self.blk.b_qkv, out=qkv)
+        with self._phase("adazero_quant"):
+            self._stage_adazero(x_loc, ts_loc, ws)
+        with self._phase("qkv_gemm"):
+            self._stage_qkv_gemm(ws)
         send = ws["send1"]
         D = 4096
-        positions = isinstance(rope[0], ltx_ops.RopePositions)
-        if positions:
-            pos, token0 = rope
-            reason = ltx_ops.rope_positions_guard_reason(pos, qkv.device)
-            if reason is None and (token0 < 0 or token0 + Ll > pos.tokens):
-                reason = "rope_shape"
-            if reason is not None:
-                raise ValueError(reason)
-            # the rope arguments of the entry points: frequency tables, grid, first token
-            src = (pos.inv_freq.data_ptr(), pos.slot_axis.data_ptr(), pos.grid_h, pos.grid_w, int(token0))
-        else:
-            cos_loc, sin_loc = rope
-            if cos_loc.shape[2] != Ll or sin_loc.shape != cos_loc.shape:
-                raise ValueError("rope_shape")
-            src = (cos_loc.data_ptr(), sin_loc.data_ptr(), ltx_ops._code(cos_loc), cos_loc.stride(1), cos_loc.stride(2))
         if send.shape != p.qkv_send_shape(Ll):
             raise ValueError("rope_shape")
         if self.peer is not None:
             with self._phase("rope_to_peers"):
-                bases = ws["recv1_dst"]
-                _lib.call(
-                    "ogx_video_qkv_rmsnorm_rope_positions_to_peers" if positions else "ogx_video_qkv_rmsnorm_rope_to_peers",
-                    qkv.data_ptr(), qkv[:, D:].data_ptr(), qkv[:, 2 * D:].data_ptr(), Ll, qkv.stride(0),
-                    w.q_norm_weight.data_ptr(), w.k_norm_weight.data_ptr(), ltx_ops._code(w.q_norm_weight),
-                    float(w.qk_eps), *src, bases, p.world, 3 * p.heads_local * p.head_dim,
-                    ltx_ops._stream(qkv),
-                )
+                self._stage_rope_to_peers(Ll, rope, ws)
             with self._phase("barrier_seq_to_heads"):
                 self.peer.barrier()
             return p.attention_views(ws["recv1"], Ll * p.world)
+        positions, src = self._rope_source(rope, Ll)
         self._phase_ctx = self._phase("rope_scatter")
         self._phase_ctx.__enter__()
         _lib.call(
@@ -295,13 +344,7 @@ class UlyssesVideoSelfAttention:
         send2 = ws["send2"]
         if self.peer is not None:
             with self._phase("attention_to_peers"):
-                bases = ws["recv2_dst"]
-                _lib.call(
-                    "ogx_attention_fwd_e4m3_to_peers",
-                    q.data_ptr(), k.data_ptr(), v.data_ptr(), L, p.heads_local, q.stride(1), 128 ** -0.5,
-                    w.to_out.input_scale.data_ptr(), bases, p.world, Ll, p.heads_local * p.head_dim,
-                    ltx_ops._stream(q),
-                )
+                self._stage_attention_to_peers(L, Ll, ws)
             with self._phase("barrier_heads_to_seq"):
                 self.peer.barrier()
         else:
@@ -312,23 +355,8 @@ class UlyssesVideoSelfAttention:
                 p.exchange_out(send2, ws["recv2"])
         if out is None:
             out = torch.empty_like(x_loc)
-        ts_view = ltx_ops._ts_view(x_loc, w.scale_shift_table, ts_loc)
-        recv2 = ws["recv2"]
-        if (recv2.shape != p.out_send_shape(Ll) or ts_view.shape[1] != Ll or x_loc.shape != out.shape
-                or not out.is_contiguous()):
-            raise ValueError("out_projection_shape")
-        self._phase_ctx = self._phase("out_gemm_residual")
-        self._phase_ctx.__enter__()
-        _lib.call(
-            "ogx_fp8_scaled_mm_residual_gate_kblocked",
-            recv2.data_ptr(), Ll, 4096, p.heads_local * p.head_dim, w.to_out.weight.data_ptr(), 4096,
-            w.to_out.weight.stride(0), w.to_out.input_scale.data_ptr(), w.to_out.weight_scale.data_ptr(), 4096,
-            w.to_out.bias.data_ptr(), ltx_ops._code(w.to_out.bias), x_loc.data_ptr(), x_loc.stride(1),
-            w.scale_shift_table.data_ptr(), ltx_ops._code(w.scale_shift_table), w.scale_shift_table.stride(0),
-            ts_view.data_ptr(), ltx_ops._code(ts_view), ts_view.stride(1), ts_view.stride(2), 2,
-            out.data_ptr(), out.stride(1), ltx_ops._stream(x_loc),
-        )
-        self._phase_ctx.__exit__(None, None, None)
+        with self._phase("out_gemm_residual"):
+            self._stage_out_proj(x_loc, ts_loc, ws, out)
         return out
 
     def forward(self, x: torch.Tensor, timestep: torch.Tensor, pe: tuple[torch.Tensor, torch.Tensor]):
@@ -362,6 +390,45 @@ class UlyssesVideoSelfAttention:
         amax = attn.float().abs().amax().reshape(1)
         dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
         w.to_out.input_scale = (amax.clamp_min(1e-12) / FP8_MAX).reshape(()).to(torch.float32)
+
+    def time_stages(self, x_loc: torch.Tensor, timestep: torch.Tensor, pe, steps: int = 20,
+                    warmup: int = 3) -> dict[str, float]:
+        """Device time (ms) of each stage of a step on this rank, every stage replayed alone from a CUDA graph
+        on the buffers a full step left (``time_launches``), so host overhead adds nothing.  The exchange
+        stages include their barrier, and every rank replays the same stages in the same order, so a barrier
+        stage also holds the wait for the slowest rank.  NVLink exchange only (NCCL's collectives stay
+        eager); returns {} otherwise."""
+        from .graphs import time_launches
+
+        if self.peer is None:
+            return {}
+        p = self.plan
+        Ll = x_loc.shape[1]
+        L = Ll * p.world
+        t0 = p.rank * Ll
+        ts_loc = timestep[:, t0:t0 + Ll]
+        rope = (pe, t0) if isinstance(pe, ltx_ops.RopePositions) else (pe[0][:, :, t0:t0 + Ll], pe[1][:, :, t0:t0 + Ll])
+        out = torch.empty_like(x_loc)
+        self.forward_local(x_loc, timestep, pe, out=out)
+        ws = self.workspace(Ll)
+
+        def rope_exchange():
+            self._stage_rope_to_peers(Ll, rope, ws)
+            self.peer.barrier()
+
+        def attention_exchange():
+            self._stage_attention_to_peers(L, Ll, ws)
+            self.peer.barrier()
+
+        stages = {
+            "adazero_quant": lambda: self._stage_adazero(x_loc, ts_loc, ws),
+            "qkv_gemm": lambda: self._stage_qkv_gemm(ws),
+            "rope_to_peers+barrier": rope_exchange,
+            "attention_to_peers+barrier": attention_exchange,
+            "out_gemm_residual": lambda: self._stage_out_proj(x_loc, ts_loc, ws, out),
+            "barrier_alone": self.peer.barrier,
+        }
+        return {name: time_launches(fn, steps, warmup, self.device) for name, fn in stages.items()}
 
     def time_attention(self, steps: int, warmup: int = 3) -> float:
         """Average device time (ms) of this rank's attention kernel (H/P heads over all L tokens), launches
