@@ -840,6 +840,10 @@ def main() -> None:
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        if world > 1:
+            # the ranks leave the host barrier up to milliseconds apart; one untimed step, whose in-graph peer
+            # barriers hold every GPU until the last rank arrives, lines the devices up before the start event
+            run_step()
         ev0.record(stream)
         for _ in range(args.steps):
             run_step()
