@@ -525,6 +525,7 @@ struct PairShared {
   uint64_t k_empty[P_STAGES], v_empty[P_STAGES];
   uint64_t s_full[2];  // S(j) in group j % 2's buffer complete (both CTAs, committed by the first)
   uint64_t p_full[2];  // first CTA: P(j) written, one arrival per warp of group j % 2 in both CTAs (8)
+  uint64_t s_read[2];  // first CTA (split scores): S(j) loaded into registers by group j % 2 (8 arrivals)
   uint64_t o_done;     // the last PV complete (both CTAs)
   uint64_t drained;
   float red[2][2][128];  // [group][running max, row sum][row]: the partial results the epilogue merges
@@ -537,7 +538,15 @@ static_assert(PAIR_SMEM_BYTES + sizeof(PairShared) <= 232448, "pair attention sh
 // last, when most of the scores are spent and the polynomial has registers to work in.
 constexpr uint32_t kPairPolyChunkMask = 0x80u;
 
-template <bool OUT_E4M3>
+// Split scores (SPLIT_S): each S(j) is two N=64 MMAs.  With cta_group::2 each CTA supplies half of the
+// N keys, so the first MMA (S_lo, TMEM columns [0, 64)) covers keys [0, 32) and [64, 96) of the tile (the
+// first 32 of each CTA's 64) and the second (S_hi, columns [64, 128)) keys [32, 64) and [96, 128): column c
+// holds key c with bits 5 and 6 swapped.  P(j) goes to columns [64, 128) of the group's buffer, so S_lo(j+2)
+// is issued as soon as the group has loaded S(j) into registers, while its exponentials run; only
+// PV(j) and S_hi(j+2) then stand between P(j) and the group's next scores.
+__host__ __device__ constexpr int split_key_of_col(int c) { return (c & ~0x60) | ((c & 0x20) << 1) | ((c & 0x40) >> 1); }
+
+template <bool OUT_E4M3, bool SPLIT_S>
 __global__ void __launch_bounds__(kPairThreads, 1)
     attn_fwd_pair_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, Params p) {
@@ -571,6 +580,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     for (int g = 0; g < 2; ++g) {
       mbar_init(&st.s_full[g], 1);
       mbar_init(&st.p_full[g], 8);
+      mbar_init(&st.s_read[g], 8);
     }
     mbar_init(&st.o_done, 1);
     mbar_init(&st.drained, 1);
@@ -639,6 +649,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (crank == 0 && elect_one()) {
       // ---------------------------------------------------------- MMA issuer (first CTA, for the pair)
       constexpr uint32_t idesc_qk = make_idesc(1, 1, 0, 0, 2 * BQ, PBKV);  // bf16, K-major A and B
+      constexpr uint32_t idesc_qk_half = make_idesc(1, 1, 0, 0, 2 * BQ, PBKV / 2);
       constexpr uint32_t idesc_pv = make_idesc(1, 1, 0, 1, 2 * BQ, HD);    // bf16, A in TMEM, V MN-major
       // descriptors of the stage-0 operands; a stage's are these plus its byte offset / 16 (addresses stay
       // below 2^18, so the 14-bit address field never carries)
@@ -663,13 +674,32 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         both(&st.s_full[j & 1]);
         both(&st.k_empty[j % P_STAGES]);
       };
+      // split scores: half h of S(j) (keys [32h, 32h + 32) of each CTA's 64) into columns [64h, 64h + 64)
+      auto issue_s_half = [&](int j, int h) {
+        const uint64_t kd = k_desc0 + (((j % P_STAGES) * PK_BYTES + h * 4096) >> 4);
+        const uint32_t d = tmem + PTMEM_S + (j & 1) * 128 + h * 64;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t qoff = ((kk >> 2) * Q_HALF_BYTES + (kk & 3) * 32) >> 4;
+          const uint32_t koff = ((kk >> 2) * PK_HALF_BYTES + (kk & 3) * 32) >> 4;
+          mma_f16_ss_pair(d, q_desc + qoff, kd + koff, idesc_qk_half, kk > 0 ? 1u : 0u);
+        }
+        if (h == 1) {
+          both(&st.s_full[j & 1]);
+          both(&st.k_empty[j % P_STAGES]);
+        }
+      };
       auto issue_pv = [&](int j) {  // O_g += P(j) V(j), g = j % 2; each group's first PV overwrites
         const uint64_t vd = v_desc0 + (((j % P_STAGES) * PV_BYTES) >> 4);
-        const uint32_t pa = tmem + PTMEM_S + (j & 1) * 128;
+        const uint32_t pa = tmem + PTMEM_S + (j & 1) * 128 + (SPLIT_S ? 64 : 0);
         const uint32_t o = tmem + PTMEM_O + (j & 1) * 128;
 #pragma unroll
-        for (int kk = 0; kk < PBKV / 16; ++kk)
-          mma_f16_ts_pair(o, pa + kk * 8, vd + ((kk * 2048) >> 4), idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < PBKV / 16; ++kk) {
+          // P columns [8kk, 8kk + 8) hold the scores' columns [16kk, 16kk + 16): keys of V block kk, or with
+          // split scores of V block split_key_of_col(16kk) / 16
+          const int vb = SPLIT_S ? split_key_of_col(16 * kk) / 16 : kk;
+          mma_f16_ts_pair(o, pa + kk * 8, vd + ((vb * 2048) >> 4), idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+        }
         both(&st.v_empty[j % P_STAGES]);
         if (j + 1 == nkv) both(&st.o_done);
       };
@@ -677,9 +707,35 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       for (int j = 0; j < 2 && j < nkv && ok; ++j) {
         if (!mbar_wait(&st.k_full[j], 0, abort)) { ok = false; break; }
         tc_fence_after();
-        issue_s(j);
+        if constexpr (SPLIT_S) {
+          issue_s_half(j, 0);
+          issue_s_half(j, 1);
+        } else {
+          issue_s(j);
+        }
       }
-      for (int j = 0; j < nkv && ok; ++j) {
+      for (int j = 0; j < nkv && ok && SPLIT_S; ++j) {
+        // S_lo(j+2) as soon as group j % 2 holds S(j) in registers; then PV(j) and S_hi(j+2) behind it
+        const int s = j % P_STAGES;
+        const int j2 = j + 2;
+        if (j2 < nkv) {
+          if (!mbar_wait(&st.s_read[j & 1], (j >> 1) & 1, abort) ||
+              !mbar_wait(&st.k_full[j2 % P_STAGES], (j2 / P_STAGES) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s_half(j2, 0);
+        }
+        if (!mbar_wait(&st.v_full[s], (j / P_STAGES) & 1, abort) || !mbar_wait(&st.p_full[j & 1], (j >> 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(j);
+        if (j2 < nkv) issue_s_half(j2, 1);
+      }
+      for (int j = 0; j < nkv && ok && !SPLIT_S; ++j) {
         const int s = j % P_STAGES;
         if (!mbar_wait(&st.v_full[s], (j / P_STAGES) & 1, abort) || !mbar_wait(&st.p_full[j & 1], (j >> 1) & 1, abort)) {
           ok = false;
@@ -721,12 +777,22 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
       for (int h = 0; h < 4; ++h) tmem_ld32(s_tmem + h * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[h * 32]));
       tmem_ld_wait();
+      if constexpr (SPLIT_S) {  // the scores are in registers: S_lo(j+2) may overwrite columns [0, 64)
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (crank == 0)
+            mbar_arrive(&st.s_read[g]);
+          else
+            mbar_arrive_peer(cluster_addr(&st.s_read[g], 0));
+        }
+      }
       float* sf = reinterpret_cast<float*>(sr);
       const int kv_valid = p.L_kv - j * PBKV;
       if (kv_valid < PBKV) {
 #pragma unroll
         for (int i = 0; i < PBKV; ++i)
-          if (i >= kv_valid) sf[i] = -INFINITY;
+          if ((SPLIT_S ? split_key_of_col(i) : i) >= kv_valid) sf[i] = -INFINITY;
       }
       // row max: eight independent chains of 3-input max, then a tree
       float mq[8];
@@ -762,9 +828,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           rs[i & 3] = add2(rs[i & 3], pr);
           pk[i] = pack_bf16x2(pr.x, pr.y);
         }
-        // P chunk cc -> TMEM columns [8cc, 8cc+8): scores this thread has already read
+        // P chunk cc -> TMEM columns [8cc, 8cc+8) (+64 with split scores): scores this thread has already read
         asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(s_tmem + cc * 8),
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(s_tmem + (SPLIT_S ? 64 : 0) + cc * 8),
             "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]), "r"(pk[7])
             : "memory");
       }

@@ -165,7 +165,7 @@ int launch_ada_ring(const ogx::AdaArgs& a, cudaStream_t s) {
   if (rc) return rc;
   const int64_t sms = sm_count();
   const dim3 grid(static_cast<unsigned>(a.rows < sms ? a.rows : sms));
-  launch(kern, grid, ogx::rows::kThreads, static_cast<size_t>(smem), s, a);
+  launch(kern, grid, ogx::rows::kWideThreads, static_cast<size_t>(smem), s, a);
   return OGX_OK;
 }
 
@@ -233,7 +233,7 @@ int launch_rope_ring(const ogx::RopeArgs& a, const ogx::rows::RopeSource& src, c
   if (rc) return rc;
   const int64_t sms = sm_count();
   const dim3 grid(static_cast<unsigned>(a.tokens < sms ? a.tokens : sms));
-  launch(kern, grid, ogx::rows::kThreads, static_cast<size_t>(smem), s, a, src);
+  launch(kern, grid, ogx::rows::kRopeThreads, static_cast<size_t>(smem), s, a, src);
   return OGX_OK;
 }
 
@@ -737,11 +737,11 @@ int ogx_qk_rmsnorm(const void* q, int64_t q_rows, int64_t q_stride, const void* 
   if (weight_dtype == OGX_DTYPE_F32) {
     rc = ensure_smem(ogx::rows::qk_rmsnorm_ring_kernel<float>, static_cast<int>(smem));
     if (rc) return rc;
-    launch(ogx::rows::qk_rmsnorm_ring_kernel<float>, grid, ogx::rows::kThreads, smem, s, a);
+    launch(ogx::rows::qk_rmsnorm_ring_kernel<float>, grid, ogx::rows::kWideThreads, smem, s, a);
   } else {
     rc = ensure_smem(ogx::rows::qk_rmsnorm_ring_kernel<__nv_bfloat16>, static_cast<int>(smem));
     if (rc) return rc;
-    launch(ogx::rows::qk_rmsnorm_ring_kernel<__nv_bfloat16>, grid, ogx::rows::kThreads, smem, s, a);
+    launch(ogx::rows::qk_rmsnorm_ring_kernel<__nv_bfloat16>, grid, ogx::rows::kWideThreads, smem, s, a);
   }
   return check_launch("qk_rmsnorm_ring_kernel");
 }
@@ -863,16 +863,17 @@ int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, const ogx::gemm::P
   return check_launch("fp8_gemm_kernel");
 }
 
-// The attention kernel: the single-CTA kernel with 64-key tiles (the default, the faster of the two on
-// B200 at L=9216), or CTA pairs (attn_fwd_pair_kernel, 128-key tiles, M=256 MMAs over two SMs) when
-// OGX_ATTN_PAIRS=1 is set in the environment.
-bool attn_use_pairs() {
-  static const bool on = [] {
+// The attention kernel: the single-CTA kernel with 64-key tiles (the default), or CTA pairs
+// (attn_fwd_pair_kernel, 128-key tiles, M=256 MMAs over two SMs) when OGX_ATTN_PAIRS=1 is set in the
+// environment, with split score MMAs when it is 2.
+int attn_pairs_mode() {
+  static const int mode = [] {
     const char* e = std::getenv("OGX_ATTN_PAIRS");
-    return e != nullptr && e[0] == '1';
+    return (e != nullptr && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
   }();
-  return on;
+  return mode;
 }
+bool attn_use_pairs() { return attn_pairs_mode() != 0; }
 
 int attention_common(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens, int64_t kv_tokens,
                      int64_t heads, int64_t head_dim, int64_t stride_b, int64_t stride_t, int64_t kv_stride_b,
@@ -905,7 +906,8 @@ template <bool E4M3>
 int attention_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int64_t batch,
                      int64_t tokens, int64_t heads, const ogx::attn::Params& p, cudaStream_t s) {
   if (attn_use_pairs()) {
-    auto kern = ogx::attn::attn_fwd_pair_kernel<E4M3>;
+    auto kern = attn_pairs_mode() == 2 ? ogx::attn::attn_fwd_pair_kernel<E4M3, true>
+                                       : ogx::attn::attn_fwd_pair_kernel<E4M3, false>;
     int rc = ensure_smem(kern, ogx::attn::PAIR_SMEM_BYTES);
     if (rc) return rc;
     // one pair of CTAs (a cluster of two) per 256 queries and head

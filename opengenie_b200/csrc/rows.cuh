@@ -4,12 +4,12 @@
 // A row's RMS needs every column before any output can be written, so a kernel that holds the row in
 // registers keeps few rows in flight per SM and leaves HBM idle between a row's load and its reduction.
 // Here one persistent CTA per SM streams its rows through a ring of shared-memory stages instead:
-//   warp 8 (one elected thread)  issues cp.async.bulk copies of whole rows (8 KB per 4096-column bf16
+//   the last warp (one thread)   issues cp.async.bulk copies of whole rows (8 KB per 4096-column bf16
 //                                row) into the ring, a row as soon as its stage is free;
-//   warps 0..W-1                 each take every W-th row of the CTA (W = 8, or the stage count where
-//                                fewer stages fit): wait for its stage, reduce the sum of squares from
-//                                shared memory (warp shuffles, no block barrier), write the outputs with
-//                                16-byte stores, free the stage.
+//   warps 0..W-1                 each take every W-th row of the CTA (W = the kernel's consumer warps,
+//                                or the stage count where fewer stages fit): wait for its stage, reduce
+//                                the sum of squares from shared memory (warp shuffles, no block
+//                                barrier), write the outputs with 16-byte stores, free the stage.
 // The stage count is a multiple of W, so a stage is always consumed by the same warp (see ring_warps).
 // With 7-24 stages (up to ~190 KB) a SM keeps enough row loads in flight for the HBM latency; no
 // register holds a row.  Every wait is bounded (a wait that runs out records OGX_ERR_TIMEOUT, the
@@ -30,8 +30,16 @@
 namespace ogx {
 namespace rows {
 
+// Consumer warps per CTA (at most; never more than the ring has stages): 10 for the RoPE kernel, whose
+// ring holds 10 Q+K stages, and 16 for AdaZero and the RMSNorm-only kernel.  A row's work is a long chain
+// of dependent shared-memory loads and packed arithmetic, so the more warps per SM sub-partition, the more
+// of the issue slots are used.
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kRopeWarps = 10;
+constexpr int kWideWarps = 16;
+__host__ __device__ constexpr int ring_threads(int consumer_warps) { return (consumer_warps + 1) * 32; }
+constexpr int kRopeThreads = ring_threads(kRopeWarps);
+constexpr int kWideThreads = ring_threads(kWideWarps);
 // Shared memory per CTA on sm_100 is at most 232448 bytes; 1 KB stays for the static ring state and the
 // 128-byte alignment of the dynamic part.
 constexpr int kDynLimit = 232448 - 1024;
@@ -53,12 +61,15 @@ struct Ring {
 };
 
 // Consumer warps and ring stages a kernel uses out of `stages` that fit: as many warps as stages (at most
-// kConsumerWarps) and the stages rounded down to a multiple of that, so row k goes to stage k % S and to warp
-// k % W with W dividing S: each stage is always consumed by the same warp.  A parity wait cannot tell the
-// phase it waits for from the one before it, so a warp reaching a stage one use ahead of the stage's other
-// consumer would take the previous fill for its own; with one consumer per stage that cannot happen.
-__host__ __device__ constexpr int ring_warps(int stages) { return stages < kConsumerWarps ? stages : kConsumerWarps; }
-__host__ __device__ constexpr int ring_stages(int stages) { return stages / ring_warps(stages) * ring_warps(stages); }
+// the kernel's consumer warps, cw) and the stages rounded down to a multiple of that, so row k goes to
+// stage k % S and to warp k % W with W dividing S: each stage is always consumed by the same warp.  A
+// parity wait cannot tell the phase it waits for from the one before it, so a warp reaching a stage one
+// use ahead of the stage's other consumer would take the previous fill for its own; with one consumer per
+// stage that cannot happen.
+__host__ __device__ constexpr int ring_warps(int stages, int cw = kConsumerWarps) { return stages < cw ? stages : cw; }
+__host__ __device__ constexpr int ring_stages(int stages, int cw = kConsumerWarps) {
+  return stages / ring_warps(stages, cw) * ring_warps(stages, cw);
+}
 
 __device__ __forceinline__ void ring_init(Ring& r, int stages) {
   if (threadIdx.x == 0) {
@@ -146,7 +157,8 @@ struct AdaLayout {
   __host__ __device__ static constexpr int stage_bytes(bool uniform) { return uniform ? kStageUniform : kStagePerToken; }
   __host__ __device__ static constexpr int stages(bool uniform) {
     return ring_stages(((kDynLimit - kAda) / stage_bytes(uniform)) > kMaxStages ? kMaxStages
-                                                                                 : ((kDynLimit - kAda) / stage_bytes(uniform)));
+                                                                                 : ((kDynLimit - kAda) / stage_bytes(uniform)),
+                       kWideWarps);
   }
   __host__ __device__ static constexpr int smem_bytes(bool uniform) { return kAda + stages(uniform) * stage_bytes(uniform); }
 };
@@ -164,11 +176,11 @@ __device__ __forceinline__ void store8<float>(float* p, const float (&f)[8]) {
 }
 
 template <int COLS, typename TableT, typename TsT, bool QUANT, int QMODE, bool UNIFORM>
-__global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
+__global__ void __launch_bounds__(kWideThreads, 1) adazero_ring_kernel(AdaArgs a) {
   pdl_trigger();
   using Lay = AdaLayout<COLS, TsT>;
   constexpr int S = Lay::stages(UNIFORM);  // a multiple of W
-  constexpr int W = ring_warps(S);
+  constexpr int W = ring_warps(S, kWideWarps);
   constexpr uint32_t SB = Lay::stage_bytes(UNIFORM);
   constexpr int VPL = COLS / 8 / 32;  // 16-byte vectors per lane
   extern __shared__ uint8_t smem_raw[];
@@ -214,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) adazero_ring_kernel(AdaArgs a) {
   const uint32_t warp = warp_idx();
   const uint32_t lane = threadIdx.x & 31;
 
-  if (warp == kConsumerWarps) {
+  if (warp == kWideWarps) {
     if (elect_one()) {
       const TsT* ts = static_cast<const TsT*>(a.ts);
       ring_produce(ring, stages, S, SB, n, SB, [&](int k, uint8_t* st, uint64_t* bar) {
@@ -341,7 +353,8 @@ struct RopeLayout {
   __host__ __device__ static constexpr int stages(bool copy_v) {
     return ring_stages(((kDynLimit - kFixed) / stage_bytes(copy_v)) > kMaxStages
                            ? kMaxStages
-                           : ((kDynLimit - kFixed) / stage_bytes(copy_v)));
+                           : ((kDynLimit - kFixed) / stage_bytes(copy_v)),
+                       kRopeWarps);
   }
   __host__ __device__ static constexpr int smem_bytes(bool copy_v) { return kFixed + stages(copy_v) * stage_bytes(copy_v); }
 };
@@ -459,10 +472,10 @@ __device__ __forceinline__ void rope_pair(const uint4* row, const float* w, int 
 }
 
 template <typename WT, typename CsT, bool GEN, bool COPY_V>
-__global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeArgs a, RopeSource src) {
+__global__ void __launch_bounds__(kRopeThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeArgs a, RopeSource src) {
   pdl_trigger();
   constexpr int S = RopeLayout::stages(COPY_V);  // a multiple of W
-  constexpr int W = ring_warps(S);
+  constexpr int W = ring_warps(S, kRopeWarps);
   constexpr uint32_t SB = RopeLayout::stage_bytes(COPY_V);
   extern __shared__ uint8_t smem_raw[];
   __shared__ Ring ring;
@@ -489,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeA
   const uint32_t warp = warp_idx();
   const uint32_t lane = threadIdx.x & 31;
 
-  if (warp == kConsumerWarps) {
+  if (warp == kRopeWarps) {
     if (elect_one()) {
       ring_produce(ring, stages, S, SB, n, SB, [&](int k, uint8_t* st, uint64_t* bar) {
         const int64_t t = r0 + k;
@@ -574,15 +587,15 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_rope_ring_kernel(RopeA
 // ((x * inv_rms) * w, one bf16 rounding); the row is staged whole before its first store, so the output
 // may alias the input.
 constexpr int kRmsFixed = 2 * 4096 * 4;  // Q and K weights as fp32
-constexpr int kRmsStages =
-    ring_stages(((kDynLimit - kRmsFixed) / 8192) > kMaxStages ? kMaxStages : ((kDynLimit - kRmsFixed) / 8192));
+constexpr int kRmsStages = ring_stages(
+    ((kDynLimit - kRmsFixed) / 8192) > kMaxStages ? kMaxStages : ((kDynLimit - kRmsFixed) / 8192), kWideWarps);
 constexpr int kRmsSmem = kRmsFixed + kRmsStages * 8192;
 
 template <typename WT>
-__global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_ring_kernel(RmsRowsArgs a) {
+__global__ void __launch_bounds__(kWideThreads, 1) qk_rmsnorm_ring_kernel(RmsRowsArgs a) {
   pdl_trigger();
   constexpr int S = kRmsStages;  // a multiple of W
-  constexpr int W = ring_warps(S);
+  constexpr int W = ring_warps(S, kWideWarps);
   extern __shared__ uint8_t smem_raw[];
   __shared__ Ring ring;
   uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 127u) & ~127u) - smem_u32(smem_raw));
@@ -604,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1) qk_rmsnorm_ring_kernel(RmsRowsArg
   __syncthreads();
   const uint32_t warp = warp_idx();
   const uint32_t lane = threadIdx.x & 31;
-  if (warp == kConsumerWarps) {
+  if (warp == kWideWarps) {
     if (elect_one()) {
       ring_produce(ring, stages, S, 8192u, n, 8192u, [&](int k, uint8_t* st, uint64_t* bar) {
         const int64_t r = r0 + k;

@@ -237,16 +237,17 @@ def test_attention_full_size_vs_torch_sdpa(ops, L):
     assert status_clean()
 
 
-def test_attention_cta_pair_kernel_same_cases():
-    """The CTA-pair attention kernel (selected with OGX_ATTN_PAIRS=1, read once per process) passes the same
-    attention cases as the default kernel: oracle shapes, the rescale path, the e4m3 epilogue and the full
-    sizes.  Runs them in a child pytest with the variable set."""
+@pytest.mark.parametrize("mode", ["1", "2"])
+def test_attention_cta_pair_kernel_same_cases(mode):
+    """The CTA-pair attention kernel (selected with OGX_ATTN_PAIRS=1, or 2 for its split score MMAs; read
+    once per process) passes the same attention cases as the default kernel: oracle shapes, the rescale
+    path, the e4m3 epilogue and the full sizes.  Runs them in a child pytest with the variable set."""
     import os
     import subprocess
     import sys
 
     here = os.path.dirname(os.path.abspath(__file__))
-    env = dict(os.environ, OGX_ATTN_PAIRS="1")
+    env = dict(os.environ, OGX_ATTN_PAIRS=mode)
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
                         os.path.join(here, "test_gpu_gemm_attention.py"), "-k", "attention and not cta_pair"],
                        env=env, capture_output=True, text=True, timeout=600)
