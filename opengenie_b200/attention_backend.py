@@ -16,6 +16,7 @@ fail-closed call that either returns the new residual stream or declines with a 
 from __future__ import annotations
 
 import importlib
+import weakref
 from collections import Counter
 
 import torch
@@ -120,9 +121,54 @@ def install_attention_class(cls, attention: str = "b200-native"):
 
 
 # ---------------------------------------------------------------- the whole branch
+class _BranchCache:
+    """Fused branches per reference block.  Entries are keyed weakly by the block object, so a freed block's
+    entry goes with it and a new block at the same address never meets it; a block that cannot be weakly
+    referenced is kept alive by its entry instead.  Each entry remembers the address and in-place version
+    counter of every source tensor it was built from, and is rebuilt when one of them changed (weights
+    reloaded in place, or a parameter replaced)."""
+
+    def __init__(self):
+        self._weak: weakref.WeakKeyDictionary = weakref.WeakKeyDictionary()
+        self._strong: dict[int, tuple[object, tuple]] = {}
+
+    @staticmethod
+    def _source_key(tensors) -> tuple:
+        return tuple((t.data_ptr(), t._version) for t in tensors if isinstance(t, torch.Tensor))
+
+    def _lookup(self, block):
+        try:
+            return self._weak.get(block)
+        except TypeError:  # not weakly referenceable
+            entry = self._strong.get(id(block))
+            return entry[1] if entry is not None and entry[0] is block else None
+
+    def _store(self, block, value) -> None:
+        try:
+            self._weak[block] = value
+        except TypeError:
+            self._strong[id(block)] = (block, value)
+
+    def get(self, block, tensors, build):
+        """The cached branch of ``block`` if its source ``tensors`` are unchanged, else ``build()`` cached."""
+        key = self._source_key(tensors)
+        hit = self._lookup(block)
+        if hit is None or hit[0] != key:
+            hit = (key, build())
+            self._store(block, hit)
+        return hit[1]
+
+    def __len__(self) -> int:
+        return len(self._weak) + len(self._strong)
+
+
+def _linear_tensors(m) -> list:
+    return [getattr(m, name, None) for name in ("weight", "weight_scale", "input_scale", "bias")]
+
+
 _MSA_BRANCH_CALLS = 0
 _MSA_BRANCH_FALLBACK_REASONS: Counter = Counter()
-_MSA_BLOCKS: dict[int, object] = {}
+_MSA_BLOCKS = _BranchCache()
 
 
 def _decline(reason: str):
@@ -159,8 +205,8 @@ def video_msa_branch(block, video, vx: torch.Tensor, *, token_counts: set[int] |
     if pe is None:
         return _decline("missing_rope")
     attn = block.attn1
-    fused = _MSA_BLOCKS.get(id(block))
-    if fused is None:
+
+    def build():
         def lin(m):
             return Fp8Linear(m.weight, m.weight_scale, m.input_scale, m.bias)
 
@@ -168,8 +214,11 @@ def video_msa_branch(block, video, vx: torch.Tensor, *, token_counts: set[int] |
                          attn.k_norm.weight, block.scale_shift_table, float(block.norm_eps),
                          float(getattr(attn.q_norm, "eps", 1e-6)))
         # gated checkpoints: the per-head gate 2*sigmoid(to_gate_logits(norm)) scales the attention output
-        fused = VideoSelfAttentionBlock(w, vx.device, to_gate_logits=getattr(attn, "to_gate_logits", None))
-        _MSA_BLOCKS[id(block)] = fused
+        return VideoSelfAttentionBlock(w, vx.device, to_gate_logits=getattr(attn, "to_gate_logits", None))
+
+    sources = [t for m in (attn.to_q, attn.to_k, attn.to_v, attn.to_out[0]) for t in _linear_tensors(m)]
+    sources += [attn.q_norm.weight, attn.k_norm.weight, block.scale_shift_table]
+    fused = _MSA_BLOCKS.get(block, sources, build)
     _MSA_BRANCH_CALLS += 1
     return fused(vx, video.timesteps, (pe[0], pe[1]))
 
@@ -182,7 +231,7 @@ def collect_video_msa_branch_stats() -> dict:
 
 _TEXT_BRANCH_CALLS = 0
 _TEXT_BRANCH_FALLBACK_REASONS: Counter = Counter()
-_TEXT_BRANCHES: dict[int, object] = {}
+_TEXT_BRANCHES = _BranchCache()
 
 
 def _decline_text(reason: str):
@@ -217,7 +266,7 @@ def video_text_cross_attention_branch(block, x: torch.Tensor, context: torch.Ten
     :2821-2835), on shapes other than batch 1 x 4096 (`shape`, `context_shape`), a table of fewer than 9
     slots (`table_shape`), a context mask (`mask`: pass the prompt's valid tokens as the context instead) and
     gated attention (`gated_attention`).  Otherwise the eight launches of ``VideoTextCrossAttention``, built
-    once per block from its modules.
+    once per block from its modules (and again when one of their tensors is replaced or changed in place).
     """
     global _TEXT_BRANCH_CALLS
     from .video_text_attention import VideoTextCrossAttention
@@ -236,10 +285,11 @@ def video_text_cross_attention_branch(block, x: torch.Tensor, context: torch.Ten
         return _decline_text("mask")
     if getattr(attn, "to_gate_logits", None) is not None:
         return _decline_text("gated_attention")
-    branch = _TEXT_BRANCHES.get(id(block))
-    if branch is None:
-        branch = _TEXT_BRANCHES[id(block)] = VideoTextCrossAttention(text_attention_weights_from_modules(block, attn),
-                                                                     x.device)
+    sources = [t for m in (attn.to_q, attn.to_k, attn.to_v, attn.to_out[0]) for t in _linear_tensors(m)]
+    sources += [attn.q_norm.weight, attn.k_norm.weight, block.scale_shift_table,
+                getattr(block, "prompt_scale_shift_table", None)]
+    branch = _TEXT_BRANCHES.get(
+        block, sources, lambda: VideoTextCrossAttention(text_attention_weights_from_modules(block, attn), x.device))
     _TEXT_BRANCH_CALLS += 1
     return branch(x, timestep, context, prompt_timestep)
 

@@ -128,3 +128,41 @@ def test_text_attention_weights_read_from_the_reference_modules():
     assert w.scale_shift_table is block.scale_shift_table
     assert w.prompt_scale_shift_table is block.prompt_scale_shift_table
     assert w.norm_eps == 1e-6 and w.qk_eps == 1e-5
+
+
+def test_branch_cache_rebuilds_on_changed_weights_and_forgets_freed_blocks():
+    """The fused-branch caches key blocks weakly and check their source tensors: the same block with unchanged
+    tensors gets the cached branch; an in-place change or a replaced tensor rebuilds it; a freed block's entry
+    goes away (so a new block at a reused address is built afresh); blocks that cannot be weakly referenced
+    are held by their entry."""
+    import gc
+
+    cache = ab._BranchCache()
+    built = []
+
+    def build():
+        built.append(object())
+        return built[-1]
+
+    mod = torch.nn.Linear(4, 4)
+    srcs = lambda: [mod.weight, mod.bias]  # noqa: E731
+    first = cache.get(mod, srcs(), build)
+    assert cache.get(mod, srcs(), build) is first and len(built) == 1
+    with torch.no_grad():
+        mod.weight.add_(1.0)  # in place: same address, new version
+    second = cache.get(mod, srcs(), build)
+    assert second is not first and len(built) == 2
+    mod.bias = torch.nn.Parameter(torch.zeros(4))  # replaced tensor
+    third = cache.get(mod, srcs(), build)
+    assert third is not second and len(built) == 3
+    assert len(cache) == 1
+    del mod
+    gc.collect()
+    assert len(cache) == 0
+
+    ns = types.SimpleNamespace(w=torch.ones(2))
+    a = cache.get(ns, [ns.w], build)
+    assert cache.get(ns, [ns.w], build) is a
+    other = types.SimpleNamespace(w=torch.ones(2))
+    assert cache.get(other, [other.w], build) is not a
+    assert len(cache) == 2
