@@ -869,6 +869,11 @@ def main() -> None:
     pipe.run([x_host] * 2, out_hosts)  # warm-up
     torch.cuda.synchronize(dev)
     barrier(pg)
+    if world > 1:
+        # as before the device-timed region: one untimed step, held by its in-graph peer barriers until the
+        # last rank arrives, lines the GPUs up before the start event
+        pipe.run([x_host], [out_hosts[0]])
+        pipe.wait_streams(stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     pipe.start_after(e0)
